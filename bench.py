@@ -1,0 +1,366 @@
+"""Exact top-k single-query search benchmark on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload mixed-100m] [--rows R]
+
+Workload (default): the 100M x 384 float32 unit-norm corpus -- half from a
+16,384-centre Zipf(1.1) mixture (sigma 0.1), half anisotropic spread vectors --
+with a 1,024-root / 32-children / rank-32 index, k = 10, queries drawn from the
+same law, issued one at a time.  Synthetic, seeded; generated on the device.
+Scaling is strong: the R rows are split into N contiguous shards, one per GPU;
+each GPU builds and searches its own shard index; the N local top-k lists are
+merged after an NCCL all-gather (k scores + k ids per GPU per query).
+
+A step is one query: root scan -> seed scan -> bounds -> main leaf scan (fused
+top-k) on every GPU, then the all-gather merge.  `value` is queries/s of the
+whole job (device time, CUDA events, max over ranks); `e2e` is the same metric
+through the public C ABI (circuit_search with host buffers: H2D query, search,
+D2H results per query) at N = 1, or the torch-level equivalent with an NCCL
+merge at N > 1.  Inputs (19-154 GB per GPU) exceed the 126 MB L2, so no flush
+is needed between steps.
+
+`--impl reference` times the reference's own CPU search path (brute force
+``topk(X @ q)``, circuit_rag/search.py:58-61) -- the oracle port -- on the host
+cores, on a bounded row sample of the same workload, rank 0 only.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "circuit-rag_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "queries/sec @k=10 on 100M x 384 fp32 (single-query exact search)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="mixed-100m")
+    ap.add_argument("--rows", type=int, default=0, help="total rows (default: the workload's N)")
+    ap.add_argument("--e2e-steps", type=int, default=0)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    return ap.parse_args()
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def clock_sampler(device_index):
+    try:
+        return subprocess.Popen(
+            ["nvidia-smi", "-i", str(device_index),
+             "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap",
+             "--format=csv,noheader,nounits", "-lms", "200"],
+            stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+    except OSError:
+        return None
+
+
+def clock_summary(proc):
+    if proc is None:
+        return None
+    proc.terminate()
+    try:
+        out, _ = proc.communicate(timeout=5)
+    except subprocess.TimeoutExpired:
+        proc.kill()
+        out, _ = proc.communicate()
+    sm, mx, reasons = [], 0.0, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for line in out.strip().splitlines():
+        f = [x.strip() for x in line.split(",")]
+        if len(f) < 7:
+            continue
+        try:
+            sm.append(float(f[0]))
+            mx = max(mx, float(f[1]))
+        except ValueError:
+            continue
+        for n, v in zip(names, f[3:7]):
+            if v.lower() == "active":
+                reasons.add(n)
+    if not sm:
+        return None
+    return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def cpu_baseline(w, n_total, seconds, k):
+    """The reference CPU path (oracle port of search.py:58-61) on a row sample."""
+    from oracle import oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample = min(n_total, 1 << 20)
+    X = w.corpus(0, sample, device="cpu")
+    Q = w.query_batch(64, device="cpu")
+    oracle.torch_flat_search(X, Q[0], k)
+    lat = []
+    t_end = time.perf_counter() + seconds
+    i = 0
+    while time.perf_counter() < t_end and i < 10_000:
+        t0 = time.perf_counter()
+        oracle.torch_flat_search(X, Q[i % len(Q)], k)
+        lat.append(time.perf_counter() - t0)
+        i += 1
+    per_q = statistics.median(lat)
+    scale = n_total / sample
+    return {
+        "value": 1.0 / (per_q * scale),
+        "unit": "queries/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{sample} rows of the same workload, {len(lat)} single queries, torch.topk(X @ q) on CPU; "
+                  f"per-query time scaled x{scale:.1f} to {n_total} rows (brute force is linear in rows)",
+        "p50_us_on_sample": per_q * 1e6,
+    }
+
+
+def run_reference(args, world, rank):
+    from circuit_rag.synthetic import WORKLOADS
+
+    if rank != 0:
+        return
+    w = WORKLOADS[args.workload]
+    n_total = args.rows or w.n
+    cb = cpu_baseline(w, n_total, max(5.0, args.cpu_seconds), w.k)
+    line = {
+        "metric": METRIC, "value": cb["value"], "unit": "queries/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": args.workload, "N": n_total, "D": w.dim, "k": w.k},
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": cb["value"], "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    import torch.distributed as dist
+
+    from circuit_rag import _native
+    from circuit_rag.hierarchy.build import build_circuit_index_streaming
+    from circuit_rag.search import _launch
+    from circuit_rag.synthetic import WORKLOADS
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    w = WORKLOADS[args.workload]
+    n_total = args.rows or w.n
+    start, stop = rank * n_total // world, (rank + 1) * n_total // world
+    k, D = w.k, w.dim
+
+    t0 = time.time()
+    idx = build_circuit_index_streaming(lambda s, e: w.corpus(start + s, start + e, device=dev), stop - start, D,
+                                        w.num_roots, w.children_per_root, w.rank, device=dev)
+    idx.original_ids += start  # global row ids
+    torch.cuda.synchronize()
+    build_s = time.time() - t0
+    handle = idx.native_handle()
+    L = _native.lib()
+
+    steps, warm = args.steps, args.warmup
+    Q = w.query_batch(steps + warm, device=dev)
+    stream = torch.cuda.current_stream()
+    scores = torch.empty(k, device=dev)
+    ids = torch.empty(k, dtype=torch.int32, device=dev)
+    g_scores = torch.empty(world * k, device=dev) if world > 1 else None
+    g_ids = torch.empty(world * k, dtype=torch.int32, device=dev) if world > 1 else None
+    out_s = torch.empty((steps, k), device=dev)
+    out_i = torch.empty((steps, k), dtype=torch.int32, device=dev)
+    q_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    s_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+
+    def one(i, timed):
+        q = Q[i]
+        if timed:
+            q_ev[i - warm][0].record(stream)
+            e0, e1 = s_ev[i - warm]
+        else:
+            e0 = e1 = None
+        _launch(handle, q, k, 0, scores, ids, None, stream, e0, e1)
+        if world > 1:
+            dist.all_gather_into_tensor(g_scores, scores)
+            dist.all_gather_into_tensor(g_ids, ids)
+            top = torch.topk(g_scores, k)
+            res_s, res_i = top.values, g_ids[top.indices]
+        else:
+            res_s, res_i = scores, ids
+        if timed:
+            out_s[i - warm].copy_(res_s)
+            out_i[i - warm].copy_(res_i)
+            q_ev[i - warm][1].record(stream)
+
+    for i in range(warm):
+        one(i, False)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks_proc = clock_sampler(local) if rank == 0 else None
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t_start.record(stream)
+    for i in range(warm, warm + steps):
+        one(i, True)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = clock_summary(clocks_proc)
+    elapsed_ms = t_start.elapsed_time(t_end)
+    lat_us = sorted(a.elapsed_time(b) * 1000.0 for a, b in q_ev)
+    scan_ms = [a.elapsed_time(b) for a, b in s_ev]
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+
+    # rows scanned per query (deterministic; untimed replay with traces)
+    snap = torch.empty(_native.TRACE_SNAPSHOT_BYTES, dtype=torch.uint8, device=dev)
+    main_rows, all_rows = [], []
+    for i in range(warm, warm + steps):
+        _launch(handle, Q[i], k, 0, scores, ids, None, stream)
+        L.circuit_trace_snapshot_async(handle, snap.data_ptr(), stream.cuda_stream)
+        host = snap.cpu()
+        raw = host.numpy().view(np.uint64)
+        seed_rows, main_r = int(raw[1] & 0xFFFFFFFF), int(raw[2] & 0xFFFFFFFF)
+        main_rows.append(main_r)
+        all_rows.append(seed_rows + main_r)
+
+    # correctness spot check of the timed results against float64 brute force on this shard (rank-local)
+    n_local = stop - start
+    check = {}
+    if world == 1:
+        from oracle import oracle
+
+        leaf = idx.leaf_vectors
+        bad = 0
+        for j in range(min(3, steps)):
+            q = Q[warm + j].double()
+            ex = torch.empty(n_local, dtype=torch.float64, device=dev)
+            for a in range(0, n_local, 1 << 22):
+                ex[a:a + (1 << 22)] = leaf[a:a + (1 << 22)].double() @ q
+            exact = torch.empty_like(ex)
+            exact[idx.original_ids.long() - start] = ex
+            try:
+                oracle.check_topk(exact.cpu().numpy(), k, out_s[j].cpu().numpy(), out_i[j].cpu().numpy() - start)
+            except AssertionError:
+                bad += 1
+        check = {"checked_queries": min(3, steps), "mismatches": bad}
+
+    # e2e through the public API
+    e2e = None
+    e2e_steps = args.e2e_steps or min(steps, 50)
+    if world == 1:
+        hq = np.ascontiguousarray(Q[warm:warm + e2e_steps].cpu().numpy())
+        hs = np.zeros(k, np.float32)
+        hi = np.zeros(k, np.int32)
+        tr = _native.Trace()
+        L.circuit_search(handle, hq[0].ctypes.data, k, hs.ctypes.data, hi.ctypes.data, ctypes.byref(tr))
+        t0 = time.perf_counter()
+        for j in range(e2e_steps):
+            rc = L.circuit_search(handle, hq[j].ctypes.data, k, hs.ctypes.data, hi.ctypes.data, ctypes.byref(tr))
+            assert rc == 0, _native.last_error()
+        e2e_s = time.perf_counter() - t0
+        e2e = {"value": e2e_steps / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": D * 4,
+               "d2h_bytes_per_step": k * 8, "api": "circuit_search (C ABI, host buffers)"}
+    else:
+        hq = Q[warm:warm + e2e_steps].cpu().pin_memory()
+        hres = torch.empty((2, k), pin_memory=True)
+        dq = torch.empty(D, device=dev)
+        torch.cuda.synchronize()
+        dist.barrier()
+        t0 = time.perf_counter()
+        for j in range(e2e_steps):
+            dq.copy_(hq[j], non_blocking=True)
+            _launch(handle, dq, k, 0, scores, ids, None, stream)
+            dist.all_gather_into_tensor(g_scores, scores)
+            dist.all_gather_into_tensor(g_ids, ids)
+            top = torch.topk(g_scores, k)
+            if rank == 0:
+                hres[0].copy_(top.values, non_blocking=True)
+                hres[1].copy_(g_ids[top.indices].float(), non_blocking=True)
+            torch.cuda.synchronize()
+        e2e_s = torch.tensor([time.perf_counter() - t0], device=dev)
+        dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+        e2e = {"value": e2e_steps / float(e2e_s.item()), "unit": "queries/s", "h2d_bytes_per_step": D * 4,
+               "d2h_bytes_per_step": k * 8, "api": "circuit_search_async + NCCL all-gather merge (torch)"}
+
+    peak, peak_kind = measured_peaks()
+    mean_scan_ms = statistics.mean(scan_ms)
+    alg_bytes = statistics.mean(main_rows) * D * 4
+    achieved = alg_bytes / (mean_scan_ms * 1e-3) / 1e9
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+            "kernel": "k_scan (final leaf scan, fused top-k)",
+            "algorithmic_bytes_per_launch": alg_bytes, "mean_launch_ms": mean_scan_ms}
+
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu = cpu_baseline(w, n_total, args.cpu_seconds, k)
+        cpu = {kk: cpu[kk] for kk in ("value", "unit", "cores", "kind", "sample")}
+
+    if rank == 0:
+        value = steps / (elapsed_ms / 1000.0)
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "queries/s", "n_gpus": world, "steps": steps,
+            "warmup": warm, "ms_per_step": round(elapsed_ms / steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "N": n_total, "D": D, "k": k, "num_roots": w.num_roots,
+                       "children_per_root": w.children_per_root, "rank": w.rank, "rows_per_gpu": n_local,
+                       "parallelism": f"shard{world}", "l2": "inputs larger than L2, no flush needed"},
+            "p50_us": round(lat_us[len(lat_us) // 2], 2), "p99_us": round(lat_us[min(len(lat_us) - 1,
+                                                                                      len(lat_us) * 99 // 100)], 2),
+            "pruned_leaf_fraction": round(1.0 - statistics.mean(all_rows) / n_local, 5),
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 4 * steps, "clocks": clocks,
+            "build_s": round(build_s, 1), "check": check,
+        }
+        print(json.dumps(line), flush=True)
+    idx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,446 @@
+"""CircuitIndex (index container + device workspace + CUDA-graph replay) and the
+index builder.
+
+Container: reference circuit_rag/hierarchy/build.py:7-131.  The index tensors
+keep the reference names, shapes and dtypes (float32 / int32), so a
+``.circuit`` file written by either side loads in the other.  When the index
+lives on a CUDA device it owns a native handle (libcircuit.so) that borrows the
+tensors' device memory and holds the search workspace; searches never copy the
+index.
+
+Builder: reference build.py:133-387.  Same hierarchy (k-means roots; per-root
+rank-r PCA basis, orthonormalised by QR; per-root k-means children; per-child
+coordinate boxes in the root basis and residual radii; root-major,
+child-contiguous leaf layout), built with torch on CPU or GPU.  Unlike the
+reference, every certificate (root radius, box, residual radius) is computed
+in float64 from the float32 data and basis and rounded outward to float32, then
+widened by the reference's 1e-5 slack, so the stored bounds hold for the exact
+projections of the stored float32 vectors.  Builder outputs are not bitwise
+the reference's (different k-means), only structurally identical.
+"""
+from typing import Optional
+
+import numpy as np
+import torch
+
+from circuit_rag import _native
+
+MAX_RANK = _native.CIRCUIT_MAX_RANK
+
+
+def _default_device() -> str:
+    return "cuda" if torch.cuda.is_available() else "cpu"
+
+
+class CircuitIndex:
+    _FLOAT = ("root_centers", "root_radii", "bases", "child_intervals_l", "child_intervals_u", "child_radii",
+              "leaf_vectors")
+    _INT = ("child_parent_ids", "leaf_offsets", "leaf_sizes", "original_ids")
+
+    def __init__(self, root_centers, root_radii, bases, child_intervals_l, child_intervals_u, child_radii,
+                 child_parent_ids, leaf_offsets, leaf_sizes, leaf_vectors, original_ids, dim, rank,
+                 device: Optional[str] = None):
+        if device is None:
+            device = _default_device()
+        if str(device).startswith("cuda") and not torch.cuda.is_available():
+            device = "cpu"  # storage only; searches require a CUDA device
+        self.device = device
+        given = dict(root_centers=root_centers, root_radii=root_radii, bases=bases,
+                     child_intervals_l=child_intervals_l, child_intervals_u=child_intervals_u,
+                     child_radii=child_radii, child_parent_ids=child_parent_ids, leaf_offsets=leaf_offsets,
+                     leaf_sizes=leaf_sizes, leaf_vectors=leaf_vectors, original_ids=original_ids)
+        for name, t in given.items():
+            t = torch.as_tensor(t)
+            dt = torch.float32 if name in self._FLOAT else torch.int32
+            setattr(self, name, t.to(device=device, dtype=dt).contiguous())
+        self.dim = int(dim)
+        self.rank = int(rank)
+        self.num_roots = self.root_centers.shape[0]
+        self.num_total_children = self.child_radii.shape[0]
+        self.N = self.leaf_vectors.shape[0]
+        self._cuda_graphs = {}
+        self._handle = None
+        self._ws = {}
+
+    # ------------------------------------------------------------------ native handle
+    @property
+    def is_cuda(self) -> bool:
+        return self.leaf_vectors.is_cuda
+
+    def native_handle(self):
+        """The libcircuit handle over this index's device tensors (created on first use)."""
+        if self._handle is None:
+            if not self.is_cuda:
+                raise RuntimeError("circuit-b200 searches run on a CUDA device; build or load the index with "
+                                   "device='cuda'")
+            lib = _native.lib()
+            dev = self.leaf_vectors.device.index or 0
+            with torch.cuda.device(dev):
+                torch.cuda.current_stream().synchronize()
+                h = lib.circuit_index_from_device(
+                    dev, self.dim, self.rank, self.num_roots, self.num_total_children, self.N,
+                    self.root_centers.data_ptr(), self.root_radii.data_ptr(), self.bases.data_ptr(),
+                    self.child_intervals_l.data_ptr(), self.child_intervals_u.data_ptr(),
+                    self.child_radii.data_ptr(), self.child_parent_ids.data_ptr(), self.leaf_offsets.data_ptr(),
+                    self.leaf_sizes.data_ptr(), self.leaf_vectors.data_ptr(), self.original_ids.data_ptr())
+            if not h:
+                raise _native.NativeLibraryError(f"circuit_index_from_device failed: {_native.last_error()}")
+            self._handle = h
+        return self._handle
+
+    def close(self) -> None:
+        """Release the native handle (the tensors stay valid)."""
+        self._cuda_graphs = {}
+        if self._handle is not None:
+            _native.lib().circuit_destroy_index(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ------------------------------------------------------------------ workspaces
+    def _init_workspace(self):
+        """Reference build.py:35-49: the ws_* tensors used by the op-level
+        ``circuit_cuda.hierarchical_search``.  The fused search does not need
+        them; they are allocated on first access."""
+        for name in ("ws_survivor_mask", "ws_vector_scores"):
+            getattr(self, name)
+
+    _WS_SPECS = {
+        "ws_survivor_mask": ("R", torch.int32),
+        "ws_survivor_indices": ("R", torch.int32),
+        "ws_num_survivors": ("1", torch.int32),
+        "ws_root_dot_products": ("R", torch.float32),
+        "ws_projected_queries": ("Rr", torch.float32),
+        "ws_perp_norms": ("R", torch.float32),
+        "ws_child_survivor_mask": ("C", torch.int32),
+        "ws_child_survivor_indices": ("C", torch.int32),
+        "ws_num_child_survivors": ("1", torch.int32),
+        "ws_vector_scores": ("N", torch.float32),
+    }
+
+    def __getattr__(self, name):
+        spec = CircuitIndex._WS_SPECS.get(name)
+        if spec is None:
+            raise AttributeError(name)
+        ws = self.__dict__.setdefault("_ws", {})
+        if name not in ws:
+            shape = {"R": (self.num_roots,), "1": (1,), "Rr": (self.num_roots, self.rank),
+                     "C": (self.num_total_children,), "N": (self.N,)}[spec[0]]
+            fill = -1e9 if name == "ws_vector_scores" else 0
+            ws[name] = torch.full(shape, fill, dtype=spec[1], device=self.leaf_vectors.device)
+        return ws[name]
+
+    # ------------------------------------------------------------------ CUDA graphs
+    def warmup_cuda_graph(self, k: int = 10):
+        """Capture one search (pruning on) into a CUDA graph on static buffers
+        (reference build.py:51-106 captured it with pruning off)."""
+        from circuit_rag.search import _launch
+
+        if not self.is_cuda:
+            return
+        k_actual = min(k, self.N)
+        h = self.native_handle()
+        static_query = torch.zeros(self.dim, dtype=torch.float32, device=self.leaf_vectors.device)
+        static_vals = torch.empty(k_actual, dtype=torch.float32, device=static_query.device)
+        static_ids = torch.empty(k_actual, dtype=torch.int32, device=static_query.device)
+        s = torch.cuda.Stream(device=static_query.device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                _launch(h, static_query, k_actual, 10001, static_vals, static_ids, None, s)
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            _launch(h, static_query, k_actual, 10001, static_vals, static_ids, None, s)
+        self._cuda_graphs[k] = {"graph": graph, "stream": s, "static_query": static_query,
+                                "static_top_vals": static_vals, "static_top_ids": static_ids}
+
+    def has_cuda_graph(self, k: int = 10) -> bool:
+        return k in self._cuda_graphs
+
+    def search_graph(self, query: torch.Tensor, k: int = 10):
+        """Replay the captured search (reference build.py:111-118)."""
+        if not self.has_cuda_graph(k):
+            self.warmup_cuda_graph(k)
+        g = self._cuda_graphs[k]
+        g["static_query"].copy_(query)
+        g["graph"].replay()
+        return g["static_top_vals"], g["static_top_ids"].clone()
+
+    # ------------------------------------------------------------------ persistence
+    def save(self, filepath: str) -> int:
+        """Write this index to a .circuit file (reference build.py:120-123)."""
+        from circuit_rag.storage.format import save_circuit_index
+
+        return save_circuit_index(self, filepath)
+
+    @classmethod
+    def load(cls, filepath: str, device: Optional[str] = None, use_mmap: bool = True) -> "CircuitIndex":
+        """Load a .circuit file (reference build.py:125-131)."""
+        from circuit_rag.storage.format import load_circuit_index
+
+        if device is None:
+            device = _default_device()
+        return load_circuit_index(filepath, device=device, use_mmap=use_mmap)
+
+
+# ====================================================================== builder
+_EPS = 1e-5  # the reference's certificate slack (build.py:188, :223-227)
+
+
+def _round_up_f32(x: torch.Tensor) -> torch.Tensor:
+    """float64 -> float32 rounded towards +inf."""
+    f = x.to(torch.float32)
+    low = f.to(torch.float64) < x
+    return torch.where(low, torch.nextafter(f, torch.full_like(f, float("inf"))), f)
+
+
+def _round_down_f32(x: torch.Tensor) -> torch.Tensor:
+    f = x.to(torch.float32)
+    high = f.to(torch.float64) > x
+    return torch.where(high, torch.nextafter(f, torch.full_like(f, float("-inf"))), f)
+
+
+def _assign(X: torch.Tensor, centers: torch.Tensor, chunk: int = 1 << 16) -> torch.Tensor:
+    """argmax_j <x, c_j> per row (reference build.py:153-154), in row chunks."""
+    out = torch.empty(X.shape[0], dtype=torch.long, device=X.device)
+    ct = centers.T.contiguous()
+    for s in range(0, X.shape[0], chunk):
+        out[s:s + chunk] = torch.argmax(X[s:s + chunk] @ ct, dim=1)
+    return out
+
+
+def _kmeans(X: torch.Tensor, k: int, iters: int, gen: torch.Generator) -> torch.Tensor:
+    """Lloyd iterations with max-inner-product assignment (reference build.py:150-161)."""
+    n = X.shape[0]
+    init = torch.randperm(n, generator=gen, device="cpu")[:k].to(X.device)
+    centers = X[init].clone()
+    for _ in range(iters):
+        labels = _assign(X, centers)
+        sums = torch.zeros_like(centers).index_add_(0, labels, X)
+        counts = torch.bincount(labels, minlength=k).to(X.dtype)
+        nz = counts > 0
+        centers[nz] = sums[nz] / counts[nz, None]
+    return centers
+
+
+def build_circuit_index(X, num_roots: int = 128, children_per_root: int = 16, rank: int = 8,
+                        random_state: int = 42, device: Optional[str] = None) -> CircuitIndex:
+    """Build the two-level hierarchy (reference build.py:256-275 signature).
+    ``rank`` may be up to 64 (the reference rejects rank > 32, build.py:266-267)."""
+    if rank > MAX_RANK:
+        raise ValueError(f"rank must be <= {MAX_RANK}")
+    if rank < 1:
+        raise ValueError("rank must be >= 1")
+    if device is None:
+        device = _default_device()
+    if str(device).startswith("cuda") and not torch.cuda.is_available():
+        device = "cpu"
+    Xt = torch.as_tensor(np.ascontiguousarray(X, dtype=np.float32) if isinstance(X, np.ndarray) else X)
+    Xt = Xt.to(device=device, dtype=torch.float32).contiguous()
+    N, D = Xt.shape
+    if N < num_roots:
+        raise ValueError("corpus smaller than num_roots")
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(random_state)
+
+    root_centers = _kmeans(Xt, num_roots, 8, gen)
+    root_labels = _assign(Xt, root_centers)
+    order = torch.argsort(root_labels, stable=True)
+    counts = torch.bincount(root_labels, minlength=num_roots).cpu().tolist()
+
+    C = num_roots * children_per_root
+    f32 = dict(dtype=torch.float32, device=device)
+    root_radii = torch.zeros(num_roots, **f32)
+    bases = torch.zeros((num_roots, D, rank), **f32)
+    child_l = torch.zeros((C, rank), **f32)
+    child_u = torch.zeros((C, rank), **f32)
+    child_radii = torch.zeros(C, **f32)
+    child_parent = torch.zeros(C, dtype=torch.int32, device=device)
+    leaf_offsets = torch.zeros(C, dtype=torch.int32, device=device)
+    leaf_sizes = torch.zeros(C, dtype=torch.int32, device=device)
+    ordered_rows = []
+    cursor = 0
+    start = 0
+    for p in range(num_roots):
+        n_p = counts[p]
+        if n_p == 0:
+            continue
+        idx = order[start:start + n_p]
+        start += n_p
+        vecs = Xt[idx]
+        c = root_centers[p]
+        diffs64 = vecs.double() - c.double()
+        root_radii[p] = _round_up_f32(diffs64.norm(dim=1).max() + _EPS)
+        actual = min(rank, n_p, D)
+        Vfull = torch.zeros((D, rank), dtype=torch.float64, device=device)
+        if n_p > 1:
+            _, _, Vh = torch.linalg.svd(diffs64, full_matrices=False)
+            Vfull[:, :actual] = Vh[:actual].T
+        else:
+            Vfull[:, :actual] = torch.eye(D, dtype=torch.float64, device=device)[:, :actual]
+        Q, _ = torch.linalg.qr(Vfull)
+        Q32 = Q.to(torch.float32)
+        bases[p] = Q32
+        Q64 = Q32.double()  # certificates are computed for the stored float32 basis
+        k_c = min(children_per_root, n_p)
+        if k_c > 1:
+            cc = _kmeans(vecs, k_c, 5, gen)
+            clabels = _assign(vecs, cc)
+        else:
+            clabels = torch.zeros(n_p, dtype=torch.long, device=device)
+        corder = torch.argsort(clabels, stable=True)
+        ccounts = torch.bincount(clabels, minlength=k_c).cpu().tolist()
+        cs = 0
+        for ci in range(k_c):
+            g = p * children_per_root + ci
+            child_parent[g] = p
+            m = ccounts[ci]
+            if m == 0:
+                continue
+            sub = corder[cs:cs + m]
+            cs += m
+            cd = diffs64[sub]
+            z = cd @ Q64
+            child_l[g] = _round_down_f32(z.min(dim=0).values - _EPS)
+            child_u[g] = _round_up_f32(z.max(dim=0).values + _EPS)
+            res = cd - z @ Q64.T
+            child_radii[g] = _round_up_f32(res.norm(dim=1).max() + _EPS)
+            leaf_offsets[g] = cursor
+            leaf_sizes[g] = m
+            ordered_rows.append(idx[sub])
+            cursor += m
+    ordered = torch.cat(ordered_rows)
+    return CircuitIndex(
+        root_centers=root_centers, root_radii=root_radii, bases=bases, child_intervals_l=child_l,
+        child_intervals_u=child_u, child_radii=child_radii, child_parent_ids=child_parent,
+        leaf_offsets=leaf_offsets, leaf_sizes=leaf_sizes, leaf_vectors=Xt[ordered],
+        original_ids=ordered.to(torch.int32), dim=D, rank=rank, device=device)
+
+
+def _eig_basis(gram: torch.Tensor, rank: int) -> torch.Tensor:
+    """Top-`rank` eigenvectors of a float64 Gram matrix, orthonormalised by QR
+    and rounded to float32 (the PCA basis of reference build.py:190-195)."""
+    D = gram.shape[0]
+    evals, evecs = torch.linalg.eigh(gram)
+    V = torch.zeros((D, rank), dtype=torch.float64, device=gram.device)
+    take = min(rank, D)
+    V[:, :take] = evecs[:, -take:].flip(1)
+    Q, _ = torch.linalg.qr(V)
+    return Q.to(torch.float32)
+
+
+def build_circuit_index_streaming(rows_fn, n: int, dim: int, num_roots: int, children_per_root: int, rank: int,
+                                  random_state: int = 42, device: str = "cuda", chunk: int = 1 << 18,
+                                  sample: int = 1 << 19) -> CircuitIndex:
+    """Build an index over a corpus too large to hold twice: ``rows_fn(start,
+    stop)`` must return rows [start, stop) deterministically (as the seeded
+    generators of circuit_rag.synthetic do).  Two generation passes: the first
+    assigns roots (k-means centres fitted on the first ``sample`` rows), the
+    second scatters rows straight into their root-major slot.  Per root, the
+    Gram matrix, child k-means, child ordering and certificates are computed in
+    row sub-chunks, so extra memory is one root's rows plus a float64 chunk.
+    Certificates are exact for the stored float32 data, as in build_circuit_index."""
+    if not 1 <= rank <= MAX_RANK:
+        raise ValueError(f"rank must be in [1, {MAX_RANK}]")
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(random_state)
+    allow = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True  # assignments only pick clusters; certificates are fp64
+    try:
+        S = rows_fn(0, min(sample, n)).to(device)
+        root_centers = _kmeans(S, num_roots, 8, gen)
+        del S
+        labels = torch.empty(n, dtype=torch.int32, device=device)
+        for s in range(0, n, chunk):
+            e = min(n, s + chunk)
+            labels[s:e] = _assign(rows_fn(s, e).to(device), root_centers).to(torch.int32)
+        counts = torch.bincount(labels, minlength=num_roots)
+        root_off = torch.cumsum(counts, 0) - counts
+        leaf = torch.empty((n, dim), dtype=torch.float32, device=device)
+        orig = torch.empty(n, dtype=torch.int32, device=device)
+        cursor = root_off.clone()
+        for s in range(0, n, chunk):
+            e = min(n, s + chunk)
+            X = rows_fn(s, e).to(device)
+            lab = labels[s:e].long()
+            order = torch.argsort(lab, stable=True)
+            ls = lab[order]
+            cnt = torch.bincount(ls, minlength=num_roots)
+            first = torch.cumsum(cnt, 0) - cnt
+            pos = cursor[ls] + (torch.arange(e - s, device=device) - first[ls])
+            leaf[pos] = X[order]
+            orig[pos] = (order + s).to(torch.int32)
+            cursor += cnt
+        del labels
+        C = num_roots * children_per_root
+        f32 = dict(dtype=torch.float32, device=device)
+        root_radii = torch.zeros(num_roots, **f32)
+        bases = torch.zeros((num_roots, dim, rank), **f32)
+        child_l = torch.zeros((C, rank), **f32)
+        child_u = torch.zeros((C, rank), **f32)
+        child_radii = torch.zeros(C, **f32)
+        child_parent = torch.zeros(C, dtype=torch.int32, device=device)
+        leaf_offsets = torch.zeros(C, dtype=torch.int32, device=device)
+        leaf_sizes = torch.zeros(C, dtype=torch.int32, device=device)
+        counts_l = counts.tolist()
+        offs_l = root_off.tolist()
+        sub = 1 << 17
+        for p in range(num_roots):
+            n_p, o_p = counts_l[p], offs_l[p]
+            if n_p == 0:
+                continue
+            c64 = root_centers[p].double()
+            gram = torch.zeros((dim, dim), dtype=torch.float64, device=device)
+            rad = torch.zeros((), dtype=torch.float64, device=device)
+            for a in range(o_p, o_p + n_p, sub):
+                d = leaf[a:min(o_p + n_p, a + sub)].double() - c64
+                gram += d.T @ d
+                rad = torch.maximum(rad, d.norm(dim=1).max())
+            root_radii[p] = _round_up_f32(rad + _EPS)
+            Q32 = _eig_basis(gram, rank)
+            bases[p] = Q32
+            Q64 = Q32.double()
+            k_c = min(children_per_root, n_p)
+            if k_c > 1:
+                cc = _kmeans(leaf[o_p:o_p + min(n_p, 1 << 16)], k_c, 5, gen)
+                clab = torch.cat([_assign(leaf[a:min(o_p + n_p, a + sub)], cc) for a in range(o_p, o_p + n_p, sub)])
+            else:
+                clab = torch.zeros(n_p, dtype=torch.long, device=device)
+            perm = torch.argsort(clab, stable=True)
+            leaf[o_p:o_p + n_p] = leaf[o_p:o_p + n_p][perm]
+            orig[o_p:o_p + n_p] = orig[o_p:o_p + n_p][perm]
+            ccounts = torch.bincount(clab, minlength=k_c).tolist()
+            cs = o_p
+            for ci in range(k_c):
+                g = p * children_per_root + ci
+                child_parent[g] = p
+                m = ccounts[ci]
+                if m == 0:
+                    continue
+                lo = torch.full((rank,), float("inf"), dtype=torch.float64, device=device)
+                hi = torch.full((rank,), float("-inf"), dtype=torch.float64, device=device)
+                rr = torch.zeros((), dtype=torch.float64, device=device)
+                for a in range(cs, cs + m, sub):
+                    d = leaf[a:min(cs + m, a + sub)].double() - c64
+                    z = d @ Q64
+                    lo = torch.minimum(lo, z.min(dim=0).values)
+                    hi = torch.maximum(hi, z.max(dim=0).values)
+                    rr = torch.maximum(rr, (d - z @ Q64.T).norm(dim=1).max())
+                child_l[g] = _round_down_f32(lo - _EPS)
+                child_u[g] = _round_up_f32(hi + _EPS)
+                child_radii[g] = _round_up_f32(rr + _EPS)
+                leaf_offsets[g] = cs
+                leaf_sizes[g] = m
+                cs += m
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = allow
+    return CircuitIndex(
+        root_centers=root_centers, root_radii=root_radii, bases=bases, child_intervals_l=child_l,
+        child_intervals_u=child_u, child_radii=child_radii, child_parent_ids=child_parent,
+        leaf_offsets=leaf_offsets, leaf_sizes=leaf_sizes, leaf_vectors=leaf, original_ids=orig, dim=dim,
+        rank=rank, device=device)

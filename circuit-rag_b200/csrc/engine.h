@@ -1,0 +1,91 @@
+// Internal (non-ABI) declarations shared by the kernels (.cu) and the host
+// library (index.cpp / ops).  Nothing here crosses the C ABI: include/circuit.h
+// is the only public header.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace cb {
+
+constexpr int KMAX = 256;          // largest k a search accepts
+constexpr int MAX_RANK = 64;       // largest rank r of a parent basis
+constexpr int MAX_DIM = 2048;      // largest vector dimension D (D % 4 == 0)
+constexpr int SCAN_CONSUMER_WARPS = 8;
+constexpr int SCAN_THREADS = (SCAN_CONSUMER_WARPS + 1) * 32;  // + one TMA producer warp
+constexpr int BOUNDS_WARPS = 4;
+constexpr int ROOT_SCAN_WARPS = 8;
+
+// Per-query control block.  The first CTRL_RESET_BYTES are zeroed by one
+// cudaMemsetAsync at the start of every search; seed_list is always fully
+// rewritten by the seed merge before it is read.
+struct SearchCtrl {
+  unsigned long long best_packed;  // argmax root: prio<<62 | key<<30 | (2^30-1-root)
+  unsigned long long seed_packed;  // seed range list: n_ranges<<32 | n_rows
+  unsigned long long main_packed;  // main range list: n_ranges<<32 | n_rows (atomicAdd)
+  uint32_t k1_done;                // last-CTA tickets
+  uint32_t seed_done;
+  uint32_t main_done;
+  uint32_t theta_key;              // running global threshold key (atomicMax)
+  uint32_t seed_T_key;             // k-th best key of the seed rows (0 = none)
+  uint32_t n_surv_roots;           // roots whose bound survived (seed root included)
+  uint32_t n_surv_children;        // non-empty children scanned (seed root's included)
+  float qn2;                       // fl(sum q_i^2)
+  int best_root;
+  int error;                       // cb::ERR_* bits
+  uint32_t pad[8];
+  unsigned long long seed_list[KMAX];
+};
+constexpr size_t CTRL_RESET_BYTES = 96;
+static_assert(offsetof(SearchCtrl, seed_list) == CTRL_RESET_BYTES, "ctrl layout");
+
+// Read-only device view of one index (all pointers are device pointers).
+struct IndexView {
+  const float* root_centers;    // [R, D]
+  const float* root_radii;      // [R]
+  const float* bases;           // [R, D, r]  (r innermost)
+  const float* child_l;         // [C, r]
+  const float* child_u;         // [C, r]
+  const float* child_radii;     // [C]
+  const int* child_parent;      // [C]
+  const int* leaf_offsets;      // [C]
+  const int* leaf_sizes;        // [C]
+  const float* leaf;            // [N, D]
+  const int* original_ids;      // [N]
+  // derived once per index by prepare()
+  const int* root_child_ptr;    // [R+1]  CSR over non-empty children, grouped by parent
+  const int* root_child_list;   // [nnz children]
+  const int* root_rows;         // [R]  leaf rows under each root
+  const double* root_cn;        // [R]  upper bound of ||c_r||
+  const double* root_defect;    // [R]  upper bound of ||V_r^T V_r - I||_2
+  int D, D4, rank, R, C, N;
+};
+
+// Device workspace owned by one index handle (one in-flight search at a time).
+struct Workspace {
+  SearchCtrl* ctrl;
+  int4* seed_ranges;                 // [max children of a root]
+  int4* main_ranges;                 // [C]
+  int4* flat_range;                  // [1] = {0, 0, N, -1}
+  unsigned long long* flat_packed;   // [1] = 1<<32 | N
+  float* root_dots;                  // [R]
+  unsigned long long* cta_lists;     // [scan_grid * KMAX]
+  int scan_grid;
+};
+
+// ---- launchers (search_kernels.cu); all asynchronous on `stream` ----
+cudaError_t launch_prepare_roots(const IndexView& ix, double* root_cn, double* root_defect, cudaStream_t stream);
+
+// One single-query search.  hierarchical != 0 runs root scan -> seed scan ->
+// bounds -> main scan; otherwise one flat scan over all rows.  Outputs k
+// results sorted by (score desc, row asc).  ev_scan0/1 (may be null) are
+// recorded around the main (dominant) scan kernel.
+cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float* q, int k, int hierarchical,
+                          float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
+                          cudaEvent_t ev_scan0, cudaEvent_t ev_scan1);
+
+int scan_smem_bytes(int D);
+int sm_count(int device);
+
+}  // namespace cb

@@ -1,0 +1,588 @@
+// Native index object and the C ABI of include/circuit.h.
+//
+// Replaces the reference's native host library:
+//   native/src/api.cpp:7-51          (entry points, NULL / -1 conventions)
+//   native/src/gpu_index.cpp:50-141  (mmap + header parse + upload + workspace)
+//   native/src/gpu_index.cpp:242-386 (host / device search)
+// Differences: every CUDA call is checked; the header is parsed as JSON; the
+// file is validated (sizes, offsets, child ranges) before any device work;
+// large tensors are uploaded through pinned double-buffered staging; pruning is
+// on; k is not clamped to 32.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <limits>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/circuit.h"
+#include "engine.h"
+#include "index_internal.h"
+#include "json_min.h"
+
+using cb::Workspace;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+}  // namespace
+
+namespace cb {
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+const char* get_error() { return g_last_error.c_str(); }
+
+bool cuda_ok(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return true;
+  set_error(std::string(what) + ": " + cudaGetErrorString(e));
+  return false;
+}
+
+}  // namespace cb
+
+using cb::cuda_ok;
+using cb::set_error;
+
+// ---------------------------------------------------------------- helpers
+static const char* kTensorNames[11] = {"root_centers",      "root_radii",       "bases",        "child_intervals_l",
+                                       "child_intervals_u", "child_radii",      "child_parent_ids",
+                                       "leaf_offsets",      "leaf_sizes",       "leaf_vectors", "original_ids"};
+
+void* circuit_index_opaque::dev_alloc(size_t bytes, const char* what) {
+  void* p = nullptr;
+  if (bytes == 0) bytes = 16;
+  if (!cuda_ok(cudaMalloc(&p, bytes), what)) return nullptr;
+  owned.push_back(p);
+  return p;
+}
+
+void circuit_index_opaque::release() {
+  if (device >= 0 && (stream || !owned.empty() || h_pinned)) cudaSetDevice(device);
+  if (stream) cudaStreamSynchronize(stream);
+  for (void* p : owned) cudaFree(p);
+  owned.clear();
+  if (h_pinned) cudaFreeHost(h_pinned);
+  h_pinned = nullptr;
+  if (stream) cudaStreamDestroy(stream);
+  stream = nullptr;
+  if (map_ptr && map_ptr != MAP_FAILED) munmap(map_ptr, map_size);
+  map_ptr = nullptr;
+  if (fd >= 0) close(fd);
+  fd = -1;
+}
+
+// Validates the small per-child arrays and builds the per-root CSR of
+// non-empty children (sorted by leaf offset) and the per-root row counts.
+bool circuit_index_opaque::build_host_tables(const int* parent, const int* offsets, const int* sizes,
+                                             std::vector<int>* ptr, std::vector<int>* list, std::vector<int>* rows) {
+  ptr->assign(R + 1, 0);
+  rows->assign(R, 0);
+  std::vector<std::pair<int64_t, int64_t>> spans;
+  spans.reserve(C);
+  int64_t covered = 0;
+  for (int c = 0; c < C; ++c) {
+    const int64_t sz = sizes[c], off = offsets[c];
+    if (sz < 0) { set_error("leaf_sizes has a negative entry"); return false; }
+    if (sz == 0) continue;
+    if (parent[c] < 0 || parent[c] >= R) { set_error("child_parent_ids out of range for a non-empty child"); return false; }
+    if (off < 0 || off + sz > N) { set_error("leaf_offsets/leaf_sizes reach outside leaf_vectors"); return false; }
+    (*ptr)[parent[c] + 1] += 1;
+    (*rows)[parent[c]] += (int)sz;
+    spans.emplace_back(off, sz);
+    covered += sz;
+  }
+  std::sort(spans.begin(), spans.end());
+  for (size_t i = 1; i < spans.size(); ++i)
+    if (spans[i - 1].first + spans[i - 1].second > spans[i].first) {
+      set_error("child leaf ranges overlap");
+      return false;
+    }
+  if (covered != N) {
+    set_error("children do not cover all N leaf rows (" + std::to_string(covered) + " of " + std::to_string(N) + ")");
+    return false;
+  }
+  for (int p = 0; p < R; ++p) (*ptr)[p + 1] += (*ptr)[p];
+  list->assign((*ptr)[R], 0);
+  std::vector<int> fill(ptr->begin(), ptr->end() - 1);
+  for (int c = 0; c < C; ++c)
+    if (sizes[c] > 0) (*list)[fill[parent[c]]++] = c;
+  for (int p = 0; p < R; ++p)
+    std::sort(list->begin() + (*ptr)[p], list->begin() + (*ptr)[p + 1],
+              [&](int a, int b) { return offsets[a] < offsets[b]; });
+  max_children = 0;
+  for (int p = 0; p < R; ++p) max_children = std::max(max_children, (*ptr)[p + 1] - (*ptr)[p]);
+  return true;
+}
+
+bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, const int* sizes) {
+  std::vector<int> ptr, list, rows;
+  if (!build_host_tables(parent, offsets, sizes, &ptr, &list, &rows)) return false;
+  int* d_ptr = (int*)dev_alloc(sizeof(int) * ptr.size(), "cudaMalloc(root_child_ptr)");
+  int* d_list = (int*)dev_alloc(sizeof(int) * std::max<size_t>(list.size(), 1), "cudaMalloc(root_child_list)");
+  int* d_rows = (int*)dev_alloc(sizeof(int) * rows.size(), "cudaMalloc(root_rows)");
+  double* d_cn = (double*)dev_alloc(sizeof(double) * R, "cudaMalloc(root_cn)");
+  double* d_def = (double*)dev_alloc(sizeof(double) * R, "cudaMalloc(root_defect)");
+  if (!d_ptr || !d_list || !d_rows || !d_cn || !d_def) return false;
+  if (!cuda_ok(cudaMemcpyAsync(d_ptr, ptr.data(), sizeof(int) * ptr.size(), cudaMemcpyHostToDevice, stream), "H2D ptr") ||
+      (!list.empty() && !cuda_ok(cudaMemcpyAsync(d_list, list.data(), sizeof(int) * list.size(),
+                                                 cudaMemcpyHostToDevice, stream),
+                                 "H2D list")) ||
+      !cuda_ok(cudaMemcpyAsync(d_rows, rows.data(), sizeof(int) * rows.size(), cudaMemcpyHostToDevice, stream), "H2D rows"))
+    return false;
+  view.root_child_ptr = d_ptr;
+  view.root_child_list = d_list;
+  view.root_rows = d_rows;
+  view.root_cn = d_cn;
+  view.root_defect = d_def;
+  if (!cuda_ok(cb::launch_prepare_roots(view, d_cn, d_def, stream), "prepare_roots")) return false;
+
+  // workspace
+  ws.scan_grid = cb::sm_count(device);
+  ws.ctrl = (cb::SearchCtrl*)dev_alloc(sizeof(cb::SearchCtrl), "cudaMalloc(ctrl)");
+  ws.seed_ranges = (int4*)dev_alloc(sizeof(int4) * std::max(max_children, 1), "cudaMalloc(seed_ranges)");
+  ws.main_ranges = (int4*)dev_alloc(sizeof(int4) * std::max(C, 1), "cudaMalloc(main_ranges)");
+  ws.flat_range = (int4*)dev_alloc(sizeof(int4), "cudaMalloc(flat_range)");
+  ws.flat_packed = (unsigned long long*)dev_alloc(sizeof(unsigned long long), "cudaMalloc(flat_packed)");
+  ws.root_dots = (float*)dev_alloc(sizeof(float) * R, "cudaMalloc(root_dots)");
+  ws.cta_lists = (unsigned long long*)dev_alloc(sizeof(unsigned long long) * (size_t)(ws.scan_grid + 1) * cb::KMAX,
+                                                "cudaMalloc(cta_lists)");
+  dev_query = (float*)dev_alloc(sizeof(float) * D, "cudaMalloc(query)");
+  dev_scores = (float*)dev_alloc(sizeof(float) * cb::KMAX, "cudaMalloc(scores)");
+  dev_ids = (int*)dev_alloc(sizeof(int) * cb::KMAX, "cudaMalloc(ids)");
+  if (!ws.ctrl || !ws.seed_ranges || !ws.main_ranges || !ws.flat_range || !ws.flat_packed || !ws.root_dots ||
+      !ws.cta_lists || !dev_query || !dev_scores || !dev_ids)
+    return false;
+  const int4 fr = make_int4(0, 0, N, -1);
+  const unsigned long long fp = (1ull << 32) | (unsigned long long)(uint32_t)N;
+  if (!cuda_ok(cudaMemcpyAsync(ws.flat_range, &fr, sizeof(fr), cudaMemcpyHostToDevice, stream), "H2D flat range") ||
+      !cuda_ok(cudaMemcpyAsync(ws.flat_packed, &fp, sizeof(fp), cudaMemcpyHostToDevice, stream), "H2D flat packed") ||
+      !cuda_ok(cudaMemsetAsync(ws.ctrl, 0, sizeof(cb::SearchCtrl), stream), "memset ctrl"))
+    return false;
+  // pinned host staging for the host-pointer search: query, scores, ids, ctrl header
+  const size_t pin_bytes = sizeof(float) * D + (sizeof(float) + sizeof(int)) * cb::KMAX + sizeof(cb::SearchCtrl);
+  if (!cuda_ok(cudaMallocHost(&h_pinned, pin_bytes), "cudaMallocHost")) return false;
+  h_query = (float*)h_pinned;
+  h_scores = h_query + D;
+  h_ids = (int*)(h_scores + cb::KMAX);
+  h_ctrl = (cb::SearchCtrl*)(h_ids + cb::KMAX);
+  if (!cuda_ok(cudaStreamSynchronize(stream), "index setup")) return false;
+  return true;
+}
+
+bool circuit_index_opaque::check_dims() {
+  if (D <= 0 || D % 4 != 0 || D > cb::MAX_DIM) {
+    set_error("dim must be a positive multiple of 4 and <= " + std::to_string(cb::MAX_DIM));
+    return false;
+  }
+  if (rank <= 0 || rank > cb::MAX_RANK) {
+    set_error("rank must be in [1, " + std::to_string(cb::MAX_RANK) + "]");
+    return false;
+  }
+  if (R <= 0 || C <= 0 || N <= 0) { set_error("num_roots, num_total_children and N must be positive"); return false; }
+  if (R >= (1 << 30)) { set_error("num_roots too large"); return false; }
+  view.D = D;
+  view.D4 = D / 4;
+  view.rank = rank;
+  view.R = R;
+  view.C = C;
+  view.N = N;
+  return true;
+}
+
+// ---------------------------------------------------------------- file loading
+namespace {
+struct TensorInfo {
+  std::string dtype;
+  std::vector<int64_t> shape;
+  int64_t offset = 0, nbytes = 0;
+};
+}  // namespace
+
+bool circuit_index_opaque::load_file(const char* path, int dev) {
+  device = dev;
+  if (!path) { set_error("null path"); return false; }
+  fd = open(path, O_RDONLY);
+  if (fd < 0) { set_error(std::string("cannot open ") + path); return false; }
+  struct stat sb;
+  if (fstat(fd, &sb) < 0) { set_error("fstat failed"); return false; }
+  map_size = (size_t)sb.st_size;
+  if (map_size < 12) { set_error("file too small for a .circuit header"); return false; }
+  map_ptr = mmap(nullptr, map_size, PROT_READ, MAP_SHARED, fd, 0);
+  if (map_ptr == MAP_FAILED) { map_ptr = nullptr; set_error("mmap failed"); return false; }
+  const char* base = static_cast<const char*>(map_ptr);
+  if (std::memcmp(base, "CIRCUIT1", 8) != 0) { set_error("invalid magic bytes"); return false; }
+  uint32_t header_len = 0;
+  std::memcpy(&header_len, base + 8, 4);
+  if ((size_t)header_len + 12 > map_size) { set_error("header length exceeds file size"); return false; }
+  cb::json::Value meta;
+  cb::json::Parser parser(base + 12, header_len);
+  if (!parser.parse(&meta) || meta.kind != cb::json::Value::Object) { set_error("header is not valid JSON"); return false; }
+  int64_t vals[5];
+  const char* keys[5] = {"dim", "rank", "num_roots", "num_total_children", "N"};
+  for (int i = 0; i < 5; ++i) {
+    const cb::json::Value* v = meta.get(keys[i]);
+    if (!v || !v->as_int64(&vals[i])) { set_error(std::string("header lacks integer ") + keys[i]); return false; }
+  }
+  if (vals[4] >= (int64_t)std::numeric_limits<int>::max()) { set_error("N must be < 2^31"); return false; }
+  D = (int)vals[0]; rank = (int)vals[1]; R = (int)vals[2]; C = (int)vals[3]; N = (int)vals[4];
+  if (!check_dims()) return false;
+  const cb::json::Value* tm = meta.get("tensor_meta");
+  if (!tm || tm->kind != cb::json::Value::Object) { set_error("header lacks tensor_meta"); return false; }
+  const int64_t expect_numel[11] = {(int64_t)R * D, R, (int64_t)R * D * rank, (int64_t)C * rank, (int64_t)C * rank,
+                                    C, C, C, C, (int64_t)N * D, N};
+  const bool is_int[11] = {false, false, false, false, false, false, true, true, true, false, true};
+  TensorInfo ti[11];
+  for (int t = 0; t < 11; ++t) {
+    const cb::json::Value* e = tm->get(kTensorNames[t]);
+    if (!e || e->kind != cb::json::Value::Object) { set_error(std::string("tensor_meta lacks ") + kTensorNames[t]); return false; }
+    const cb::json::Value* dt = e->get("dtype");
+    const cb::json::Value* sh = e->get("shape");
+    const cb::json::Value* off = e->get("offset");
+    const cb::json::Value* nb = e->get("nbytes");
+    if (!dt || dt->kind != cb::json::Value::String || !sh || sh->kind != cb::json::Value::Array || !off ||
+        !off->as_int64(&ti[t].offset) || !nb || !nb->as_int64(&ti[t].nbytes)) {
+      set_error(std::string("bad tensor_meta entry for ") + kTensorNames[t]);
+      return false;
+    }
+    ti[t].dtype = dt->str;
+    int64_t numel = 1;
+    for (const auto& d : sh->arr) {
+      int64_t x;
+      if (!d.as_int64(&x) || x < 0) { set_error(std::string("bad shape for ") + kTensorNames[t]); return false; }
+      ti[t].shape.push_back(x);
+      numel *= x;
+    }
+    if (ti[t].dtype != (is_int[t] ? "int32" : "float32")) { set_error(std::string("unexpected dtype for ") + kTensorNames[t]); return false; }
+    if (numel != expect_numel[t] || ti[t].nbytes != numel * 4) {
+      set_error(std::string("shape/nbytes mismatch for ") + kTensorNames[t]);
+      return false;
+    }
+    if (ti[t].offset < 12 + (int64_t)header_len || ti[t].offset + ti[t].nbytes > (int64_t)map_size) {
+      set_error(std::string("tensor data outside the file for ") + kTensorNames[t]);
+      return false;
+    }
+  }
+  // validate the child tables on the host copy before any device work.  The
+  // file only guarantees 4-byte alignment of tensor data (offsets are 12 mod
+  // 64 with the reference writer), so copy the small int arrays out first.
+  std::vector<int> parent(C), offsets(C), sizes(C);
+  std::memcpy(parent.data(), base + ti[6].offset, 4 * (size_t)C);
+  std::memcpy(offsets.data(), base + ti[7].offset, 4 * (size_t)C);
+  std::memcpy(sizes.data(), base + ti[8].offset, 4 * (size_t)C);
+  {
+    std::vector<int> p0, l0, r0;
+    if (!build_host_tables(parent.data(), offsets.data(), sizes.data(), &p0, &l0, &r0)) return false;
+  }
+  // the file is valid: only now touch the device
+  if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice")) return false;
+  if (!cuda_ok(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate")) return false;
+  void* dptr[11];
+  for (int t = 0; t < 11; ++t) {
+    dptr[t] = dev_alloc((size_t)ti[t].nbytes, "cudaMalloc(index tensor)");
+    if (!dptr[t]) return false;
+  }
+  // upload: pinned double-buffered staging in 64 MiB chunks
+  const size_t CH = 64ull << 20;
+  void* stage[2] = {nullptr, nullptr};
+  cudaEvent_t done[2] = {nullptr, nullptr};
+  bool ok = cuda_ok(cudaMallocHost(&stage[0], CH), "cudaMallocHost(stage)") &&
+            cuda_ok(cudaMallocHost(&stage[1], CH), "cudaMallocHost(stage)") &&
+            cuda_ok(cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming), "cudaEventCreate") &&
+            cuda_ok(cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming), "cudaEventCreate");
+  int slot = 0;
+  bool used[2] = {false, false};
+  for (int t = 0; t < 11 && ok; ++t) {
+    const char* src = base + ti[t].offset;
+    size_t left = (size_t)ti[t].nbytes, pos = 0;
+    while (left > 0 && ok) {
+      const size_t n = std::min(left, CH);
+      if (used[slot]) ok = cuda_ok(cudaEventSynchronize(done[slot]), "staging wait");
+      if (!ok) break;
+      std::memcpy(stage[slot], src + pos, n);
+      ok = cuda_ok(cudaMemcpyAsync((char*)dptr[t] + pos, stage[slot], n, cudaMemcpyHostToDevice, stream), "H2D tensor") &&
+           cuda_ok(cudaEventRecord(done[slot], stream), "cudaEventRecord");
+      used[slot] = true;
+      slot ^= 1;
+      pos += n;
+      left -= n;
+    }
+  }
+  if (ok) ok = cuda_ok(cudaStreamSynchronize(stream), "upload");
+  for (int i = 0; i < 2; ++i) {
+    if (done[i]) cudaEventDestroy(done[i]);
+    if (stage[i]) cudaFreeHost(stage[i]);
+  }
+  if (!ok) return false;
+  view.root_centers = (const float*)dptr[0];
+  view.root_radii = (const float*)dptr[1];
+  view.bases = (const float*)dptr[2];
+  view.child_l = (const float*)dptr[3];
+  view.child_u = (const float*)dptr[4];
+  view.child_radii = (const float*)dptr[5];
+  view.child_parent = (const int*)dptr[6];
+  view.leaf_offsets = (const int*)dptr[7];
+  view.leaf_sizes = (const int*)dptr[8];
+  view.leaf = (const float*)dptr[9];
+  view.original_ids = (const int*)dptr[10];
+  // the mapping is no longer needed once everything is on the device
+  munmap(map_ptr, map_size);
+  map_ptr = nullptr;
+  close(fd);
+  fd = -1;
+  return finish_setup(parent.data(), offsets.data(), sizes.data());
+}
+
+bool circuit_index_opaque::wrap_device(int dev, int dim, int rnk, int nr, int nc, int64_t n, const float* const* f,
+                                       const int* const* ints) {
+  device = dev;
+  if (n <= 0 || n >= (int64_t)std::numeric_limits<int>::max()) { set_error("N must be in [1, 2^31)"); return false; }
+  D = dim; rank = rnk; R = nr; C = nc; N = (int)n;
+  if (!check_dims()) return false;
+  if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice")) return false;
+  for (int i = 0; i < 7; ++i)
+    if (!f[i]) { set_error("null float array"); return false; }
+  for (int i = 0; i < 4; ++i)
+    if (!ints[i]) { set_error("null int array"); return false; }
+  if (((uintptr_t)f[6] & 15) || ((uintptr_t)f[0] & 15) || ((uintptr_t)f[2] & 15) || ((uintptr_t)f[3] & 15) ||
+      ((uintptr_t)f[4] & 15)) {
+    set_error("leaf_vectors, root_centers, bases and child intervals must be 16-byte aligned");
+    return false;
+  }
+  if (!cuda_ok(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate")) return false;
+  view.root_centers = f[0];
+  view.root_radii = f[1];
+  view.bases = f[2];
+  view.child_l = f[3];
+  view.child_u = f[4];
+  view.child_radii = f[5];
+  view.leaf = f[6];
+  view.child_parent = ints[0];
+  view.leaf_offsets = ints[1];
+  view.leaf_sizes = ints[2];
+  view.original_ids = ints[3];
+  std::vector<int> parent(C), offsets(C), sizes(C);
+  if (!cuda_ok(cudaMemcpy(parent.data(), ints[0], 4 * (size_t)C, cudaMemcpyDeviceToHost), "D2H child_parent_ids") ||
+      !cuda_ok(cudaMemcpy(offsets.data(), ints[1], 4 * (size_t)C, cudaMemcpyDeviceToHost), "D2H leaf_offsets") ||
+      !cuda_ok(cudaMemcpy(sizes.data(), ints[2], 4 * (size_t)C, cudaMemcpyDeviceToHost), "D2H leaf_sizes"))
+    return false;
+  return finish_setup(parent.data(), offsets.data(), sizes.data());
+}
+
+// ---------------------------------------------------------------- search
+int circuit_index_opaque::search_async(const float* dq, int k, int64_t min_hier, float* dscores, int* dids,
+                                       int64_t* drows, cudaStream_t st, cudaEvent_t e0, cudaEvent_t e1) {
+  if (k < 1 || k > cb::KMAX) { set_error("k must be in [1, " + std::to_string(cb::KMAX) + "]"); return CIRCUIT_ERR_ARG; }
+  if (!dq || !dscores) { set_error("null query or output pointer"); return CIRCUIT_ERR_ARG; }
+  if ((uintptr_t)dq & 15) { set_error("query must be 16-byte aligned"); return CIRCUIT_ERR_ARG; }
+  if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice")) return CIRCUIT_ERR_CUDA;
+  const int hier = ((int64_t)N < min_hier) ? 0 : 1;
+  cudaError_t e = cb::launch_search(view, ws, dq, k, hier, dscores, dids, (long long*)drows, st, e0, e1);
+  last_stream = st;
+  last_path = hier;
+  last_k = k;
+  if (e != cudaSuccess) { set_error(std::string("search launch: ") + cudaGetErrorString(e)); return CIRCUIT_ERR_CUDA; }
+  return CIRCUIT_OK;
+}
+
+void circuit_index_opaque::fill_trace(const cb::SearchCtrl& c, circuit_trace_ex_t* t) const {
+  std::memset(t, 0, sizeof(*t));
+  t->path = last_path;
+  t->vectors_total = N;
+  t->total_children = C;
+  t->device_error = c.error;
+  if (last_path) {
+    t->vectors_scored = (int64_t)(uint32_t)c.seed_packed + (int64_t)(uint32_t)c.main_packed;
+    t->surviving_roots = (int32_t)c.n_surv_roots;
+    t->surviving_children = (int32_t)c.n_surv_children;
+    t->best_root = c.best_root;
+    t->seed_threshold = c.seed_T_key ? key_to_float(c.seed_T_key) : -std::numeric_limits<float>::infinity();
+  } else {
+    t->vectors_scored = N;
+    t->surviving_roots = R;
+    t->surviving_children = -1;
+    t->best_root = -1;
+    t->seed_threshold = -std::numeric_limits<float>::infinity();
+  }
+}
+
+float circuit_index_opaque::key_to_float(uint32_t k) {
+  const uint32_t b = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  float f;
+  std::memcpy(&f, &b, 4);
+  return f;
+}
+
+int circuit_index_opaque::search_blocking(const float* query, bool host_ptrs, int k, float* out_scores, int* out_ids,
+                                          circuit_trace_t* trace) {
+  const auto t0 = std::chrono::steady_clock::now();
+  if (!query || !out_scores || !out_ids) { set_error("null query or output pointer"); return CIRCUIT_ERR_ARG; }
+  if (k < 1 || k > cb::KMAX) { set_error("k must be in [1, " + std::to_string(cb::KMAX) + "]"); return CIRCUIT_ERR_ARG; }
+  if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice")) return CIRCUIT_ERR_CUDA;
+  // reference routing: flat scan for N <= 10000 (gpu_index.cpp:151)
+  const int64_t min_hier = 10001;
+  if (host_ptrs) {
+    std::memcpy(h_query, query, sizeof(float) * D);
+    if (!cuda_ok(cudaMemcpyAsync(dev_query, h_query, sizeof(float) * D, cudaMemcpyHostToDevice, stream), "H2D query"))
+      return CIRCUIT_ERR_CUDA;
+  } else if (!cuda_ok(cudaMemcpyAsync(dev_query, query, sizeof(float) * D, cudaMemcpyDeviceToDevice, stream), "D2D query")) {
+    return CIRCUIT_ERR_CUDA;
+  }
+  int rc = search_async(dev_query, k, min_hier, dev_scores, dev_ids, nullptr, stream, nullptr, nullptr);
+  if (rc != CIRCUIT_OK) return rc;
+  const cudaMemcpyKind kind = host_ptrs ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+  float* sdst = host_ptrs ? h_scores : out_scores;
+  int* idst = host_ptrs ? h_ids : out_ids;
+  if (!cuda_ok(cudaMemcpyAsync(sdst, dev_scores, sizeof(float) * k, kind, stream), "copy scores") ||
+      !cuda_ok(cudaMemcpyAsync(idst, dev_ids, sizeof(int) * k, kind, stream), "copy ids") ||
+      !cuda_ok(cudaMemcpyAsync(h_ctrl, ws.ctrl, cb::CTRL_RESET_BYTES, cudaMemcpyDeviceToHost, stream), "copy ctrl") ||
+      !cuda_ok(cudaStreamSynchronize(stream), "search sync"))
+    return CIRCUIT_ERR_CUDA;
+  if (host_ptrs) {
+    std::memcpy(out_scores, h_scores, sizeof(float) * k);
+    std::memcpy(out_ids, h_ids, sizeof(int) * k);
+  }
+  have_host_ctrl = true;
+  if (h_ctrl->error) {
+    set_error("device-side wait timed out (error bits " + std::to_string(h_ctrl->error) + ")");
+    return CIRCUIT_ERR_TIMEOUT;
+  }
+  if (trace) {
+    circuit_trace_ex_t tx;
+    fill_trace(*h_ctrl, &tx);
+    trace->latency_us = (float)std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
+    trace->vectors_scored = (int)std::min<int64_t>(tx.vectors_scored, std::numeric_limits<int>::max());
+  }
+  return CIRCUIT_OK;
+}
+
+// ---------------------------------------------------------------- C ABI
+extern "C" {
+
+const char* circuit_last_error(void) { return cb::get_error(); }
+int circuit_abi_version(void) { return CIRCUIT_ABI_VERSION; }
+
+circuit_index_t circuit_load_index(const char* filepath, int device_id) {
+  auto* idx = new (std::nothrow) circuit_index_opaque();
+  if (!idx) { set_error("out of host memory"); return nullptr; }
+  if (!idx->load_file(filepath, device_id)) {
+    idx->release();
+    delete idx;
+    return nullptr;
+  }
+  return idx;
+}
+
+circuit_index_t circuit_index_from_device(int device_id, int dim, int rank, int num_roots, int num_total_children,
+                                          int64_t n, const float* root_centers, const float* root_radii,
+                                          const float* bases, const float* child_intervals_l,
+                                          const float* child_intervals_u, const float* child_radii,
+                                          const int* child_parent_ids, const int* leaf_offsets,
+                                          const int* leaf_sizes, const float* leaf_vectors,
+                                          const int* original_ids) {
+  auto* idx = new (std::nothrow) circuit_index_opaque();
+  if (!idx) { set_error("out of host memory"); return nullptr; }
+  const float* f[7] = {root_centers, root_radii, bases, child_intervals_l, child_intervals_u, child_radii, leaf_vectors};
+  const int* ints[4] = {child_parent_ids, leaf_offsets, leaf_sizes, original_ids};
+  if (!idx->wrap_device(device_id, dim, rank, num_roots, num_total_children, n, f, ints)) {
+    idx->release();
+    delete idx;
+    return nullptr;
+  }
+  return idx;
+}
+
+int circuit_index_info(circuit_index_t index, int64_t* info) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  if (!info) { set_error("null info"); return CIRCUIT_ERR_ARG; }
+  info[0] = index->D; info[1] = index->rank; info[2] = index->R; info[3] = index->C;
+  info[4] = index->N; info[5] = index->device; info[6] = index->ws.scan_grid; info[7] = cb::KMAX;
+  return CIRCUIT_OK;
+}
+
+int circuit_search(circuit_index_t index, const float* query, int k, float* out_scores, int* out_ids,
+                   circuit_trace_t* trace) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  return index->search_blocking(query, true, k, out_scores, out_ids, trace);
+}
+
+int circuit_search_device(circuit_index_t index, const float* dev_query, int k, float* dev_out_scores,
+                          int* dev_out_ids, circuit_trace_t* trace) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  return index->search_blocking(dev_query, false, k, dev_out_scores, dev_out_ids, trace);
+}
+
+int circuit_search_async(circuit_index_t index, const float* dev_query, int k, int64_t min_hierarchy_n,
+                         float* dev_out_scores, int* dev_out_ids, int64_t* dev_out_rows, void* stream,
+                         void* ev_scan_begin, void* ev_scan_end) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  cudaStream_t st = stream ? (cudaStream_t)stream : index->stream;
+  index->have_host_ctrl = false;
+  return index->search_async(dev_query, k, min_hierarchy_n, dev_out_scores, dev_out_ids, dev_out_rows, st,
+                             (cudaEvent_t)ev_scan_begin, (cudaEvent_t)ev_scan_end);
+}
+
+int circuit_last_trace(circuit_index_t index, circuit_trace_ex_t* out) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  if (!out) { set_error("null trace"); return CIRCUIT_ERR_ARG; }
+  if (!cuda_ok(cudaSetDevice(index->device), "cudaSetDevice")) return CIRCUIT_ERR_CUDA;
+  if (!index->have_host_ctrl) {
+    cudaStream_t st = index->last_stream ? index->last_stream : index->stream;
+    if (!cuda_ok(cudaMemcpyAsync(index->h_ctrl, index->ws.ctrl, cb::CTRL_RESET_BYTES, cudaMemcpyDeviceToHost, st),
+                 "copy ctrl") ||
+        !cuda_ok(cudaStreamSynchronize(st), "trace sync"))
+      return CIRCUIT_ERR_CUDA;
+    index->have_host_ctrl = true;
+  }
+  index->fill_trace(*index->h_ctrl, out);
+  if (index->h_ctrl->error) {
+    set_error("device-side wait timed out (error bits " + std::to_string(index->h_ctrl->error) + ")");
+    return CIRCUIT_ERR_TIMEOUT;
+  }
+  return CIRCUIT_OK;
+}
+
+int circuit_trace_snapshot_async(circuit_index_t index, void* dst, void* stream) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  if (!dst) { set_error("null snapshot buffer"); return CIRCUIT_ERR_ARG; }
+  static_assert(cb::CTRL_RESET_BYTES == CIRCUIT_TRACE_SNAPSHOT_BYTES, "snapshot size");
+  cudaStream_t st = stream ? (cudaStream_t)stream : index->stream;
+  if (!cuda_ok(cudaSetDevice(index->device), "cudaSetDevice") ||
+      !cuda_ok(cudaMemcpyAsync(dst, index->ws.ctrl, cb::CTRL_RESET_BYTES, cudaMemcpyDefault, st),
+               "trace snapshot"))
+    return CIRCUIT_ERR_CUDA;
+  return CIRCUIT_OK;
+}
+
+int circuit_trace_decode(circuit_index_t index, const void* snapshot, int path, circuit_trace_ex_t* out) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  if (!snapshot || !out) { set_error("null snapshot or trace"); return CIRCUIT_ERR_ARG; }
+  cb::SearchCtrl c;
+  std::memset(&c, 0, sizeof(c));
+  std::memcpy(&c, snapshot, cb::CTRL_RESET_BYTES);
+  const int saved = index->last_path;
+  index->last_path = path ? 1 : 0;
+  index->fill_trace(c, out);
+  index->last_path = saved;
+  if (c.error) {
+    set_error("device-side wait timed out (error bits " + std::to_string(c.error) + ")");
+    return CIRCUIT_ERR_TIMEOUT;
+  }
+  return CIRCUIT_OK;
+}
+
+void circuit_destroy_index(circuit_index_t index) {
+  if (!index) return;
+  index->release();
+  delete index;
+}
+
+}  // extern "C"

@@ -1,0 +1,63 @@
+// The object behind circuit_index_t (internal; see include/circuit.h).
+// Replaces reference native/include/circuit/gpu_index.hpp:15-67.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/circuit.h"
+#include "engine.h"
+
+namespace cb {
+void set_error(const std::string& msg);
+const char* get_error();
+bool cuda_ok(cudaError_t e, const char* what);
+}  // namespace cb
+
+struct circuit_index_opaque {
+  int device = -1;
+  int D = 0, rank = 0, R = 0, C = 0, N = 0;
+  int max_children = 0;
+
+  cb::IndexView view{};
+  cb::Workspace ws{};
+
+  // host-pointer search path
+  float* dev_query = nullptr;
+  float* dev_scores = nullptr;
+  int* dev_ids = nullptr;
+  void* h_pinned = nullptr;
+  float* h_query = nullptr;
+  float* h_scores = nullptr;
+  int* h_ids = nullptr;
+  cb::SearchCtrl* h_ctrl = nullptr;
+  bool have_host_ctrl = false;
+
+  cudaStream_t stream = nullptr;
+  cudaStream_t last_stream = nullptr;
+  int last_path = 0;
+  int last_k = 0;
+
+  std::vector<void*> owned;  // device allocations released by release()
+  int fd = -1;
+  void* map_ptr = nullptr;
+  size_t map_size = 0;
+
+  void* dev_alloc(size_t bytes, const char* what);
+  void release();
+  bool check_dims();
+  bool build_host_tables(const int* parent, const int* offsets, const int* sizes, std::vector<int>* ptr,
+                         std::vector<int>* list, std::vector<int>* rows);
+  bool finish_setup(const int* parent, const int* offsets, const int* sizes);
+  bool load_file(const char* path, int dev);
+  bool wrap_device(int dev, int dim, int rnk, int nr, int nc, int64_t n, const float* const* f, const int* const* ints);
+  int search_async(const float* dq, int k, int64_t min_hier, float* dscores, int* dids, int64_t* drows,
+                   cudaStream_t st, cudaEvent_t e0, cudaEvent_t e1);
+  int search_blocking(const float* query, bool host_ptrs, int k, float* out_scores, int* out_ids,
+                      circuit_trace_t* trace);
+  void fill_trace(const cb::SearchCtrl& c, circuit_trace_ex_t* t) const;
+  static float key_to_float(uint32_t k);
+};

@@ -1,0 +1,950 @@
+// Single-query exact top-k search kernels for B200 (sm_100a).
+//
+// Pipeline for one query (all on one stream, no host synchronisation):
+//   memset(ctrl header)
+//   k_root_scan   warp per root: q.c_r for every root, ||q||^2, argmax root
+//                 (the seed root); its last CTA writes the seed root's leaf
+//                 ranges.                       (reference: search.py:26-41,
+//                                                 root_bounds.cu:31-54)
+//   k_scan<seed>  streams the seed root's leaves, fused top-k; its last CTA
+//                 merges the per-CTA lists into the seed list and publishes
+//                 T = k-th best seed score on the device.
+//   k_bounds      warp per root: rigorous root bound, rank-r projection of q
+//                 (basis staged in shared memory by TMA), rigorous child box
+//                 bounds, compaction of surviving children into leaf ranges.
+//                                               (reference: parent_projection.cu:125-178,
+//                                                 child_bounds.cu:11-83)
+//   k_scan<final> streams the surviving leaves (TMA bulk copies into a
+//                 3..8-stage shared-memory ring, one producer warp, eight
+//                 consumer warps), fused top-k; its last CTA merges all lists
+//                 plus the seed list and writes scores / original ids.
+//                                               (reference: dense_score.cu:116-164,
+//                                                 topk.cu:56-170, search.py:77-84)
+// The flat path (small corpora) is the final scan over one range [0, N).
+#include <cmath>
+#include <cstdio>
+
+#include "common.cuh"
+#include "engine.h"
+
+namespace cb {
+
+// ============================================================ rounding model
+// u = 2^-24 (fp32 unit roundoff); gamma_n = n u / (1 - n u) bounds the error of
+// any fp32 dot product of length n, in any summation order, with or without FMA
+// (Higham, Accuracy and Stability of Numerical Algorithms, 2nd ed., sec. 3.1).
+__device__ __forceinline__ double gamma_n(int n) {
+  const double u = 5.9604644775390625e-08;
+  return n * u / (1.0 - n * u);
+}
+
+// ============================================================ block top-k select
+struct SelectScratch {
+  uint32_t hist[256];
+  unsigned long long prefix;
+  uint32_t need;
+  uint32_t count;
+  uint32_t nnz;
+  uint32_t pad;
+};
+
+template <bool GLOBAL>
+__device__ __forceinline__ unsigned long long ld_cand(const unsigned long long* p) {
+  if constexpr (GLOBAL) return __ldcg(p);
+  else return *p;
+}
+
+// Block-wide descending bitonic sort of a[0..n) (n a power of two) in shared memory.
+__device__ void block_bitonic_desc(unsigned long long* a, int n) {
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < (n >> 1); i += blockDim.x) {
+        const int lo = 2 * stride * (i / stride) + (i % stride);
+        const int hi = lo + stride;
+        const bool up = (lo & size) == 0;
+        const unsigned long long x = a[lo], y = a[hi];
+        if ((x < y) == up) { a[lo] = y; a[hi] = x; }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Warp-wide descending bitonic sort of a[0..n) (n a power of two) in shared memory.
+__device__ void warp_bitonic_desc(unsigned long long* a, int n, int lane) {
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = lane; i < (n >> 1); i += 32) {
+        const int lo = 2 * stride * (i / stride) + (i % stride);
+        const int hi = lo + stride;
+        const bool up = (lo & size) == 0;
+        const unsigned long long x = a[lo], y = a[hi];
+        if ((x < y) == up) { a[lo] = y; a[hi] = x; }
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// Selects the k largest non-zero packed candidates of src[0..M) (unique when
+// non-zero; zero = empty slot) by an 8 x 8-bit radix select over the 64-bit
+// packed value, then sorts them.  sel must hold selN >= k entries (power of 2).
+// Returns the number of selected candidates (min(k, non-zeros)); sel[0..ret) is
+// sorted descending and sel[ret..selN) is zero.  All threads of the block call it.
+template <bool GLOBAL>
+__device__ int block_select_topk(const unsigned long long* src, int M, int k, unsigned long long* sel,
+                                 int selN, SelectScratch* s) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) { s->nnz = 0; s->count = 0; s->prefix = 0; }
+  __syncthreads();
+  uint32_t local = 0;
+  for (int i = tid; i < M; i += blockDim.x) local += (ld_cand<GLOBAL>(src + i) != 0ull);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(FULL_MASK, local, o);
+  if (lane == 0 && local) atomicAdd(&s->nnz, local);
+  __syncthreads();
+  const int kk = min((int)s->nnz, k);
+  for (int i = tid; i < selN; i += blockDim.x) sel[i] = 0ull;
+  if (kk == 0) { __syncthreads(); return 0; }
+  if (tid == 0) s->need = (uint32_t)kk;
+  __syncthreads();
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    const unsigned long long prefix = s->prefix;
+    const uint32_t need = s->need;
+    const unsigned long long hmask = (shift == 56) ? 0ull : (~0ull << (shift + 8));
+    for (int i = tid; i < 256; i += blockDim.x) s->hist[i] = 0;
+    __syncthreads();
+    for (int i = tid; i < M; i += blockDim.x) {
+      const unsigned long long v = ld_cand<GLOBAL>(src + i);
+      if ((v & hmask) == prefix) atomicAdd(&s->hist[(v >> shift) & 255ull], 1u);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t c[8], sum = 0;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) { c[t] = s->hist[255 - (lane * 8 + t)]; sum += c[t]; }
+      uint32_t incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        uint32_t x = __shfl_up_sync(FULL_MASK, incl, o);
+        if (lane >= o) incl += x;
+      }
+      const uint32_t excl = incl - sum;
+      if (excl < need && incl >= need) {
+        uint32_t acc = excl;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          if (acc + c[t] >= need) {
+            const uint32_t d = 255 - (lane * 8 + t);
+            s->prefix = prefix | ((unsigned long long)d << shift);
+            s->need = need - acc;
+            break;
+          }
+          acc += c[t];
+        }
+      }
+    }
+    __syncthreads();
+  }
+  const unsigned long long kth = s->prefix;
+  for (int i = tid; i < M; i += blockDim.x) {
+    const unsigned long long v = ld_cand<GLOBAL>(src + i);
+    if (v != 0ull && v >= kth) {
+      const uint32_t pos = atomicAdd(&s->count, 1u);
+      if (pos < (uint32_t)selN) sel[pos] = v;
+    }
+  }
+  __syncthreads();
+  block_bitonic_desc(sel, selN);
+  return kk;
+}
+
+// ============================================================ leaf scan kernel
+struct ScanParams {
+  const float* leaf;                          // [N, D]
+  const float* q;                             // [D]
+  const int4* ranges;                         // {vbegin, row_begin, row_end, child}
+  const unsigned long long* packed_counts;    // n_ranges << 32 | n_rows
+  uint32_t* theta_key;                        // running global threshold (atomicMax)
+  unsigned long long* cta_lists;              // [(gridDim.x + 1) * k]
+  uint32_t* done;                             // last-CTA ticket
+  int* err;
+  int D4;
+  int row_bytes;
+  int k;
+  int stages;
+  int final_mode;                             // 0: seed merge, 1: final merge
+  int merge_seed;                             // final: also merge ctrl seed list
+  unsigned long long* seed_list;              // [k]
+  uint32_t* seed_T_key;
+  float* out_scores;
+  int* out_ids;
+  long long* out_rows;
+  const int* original_ids;
+};
+
+template <int VPL> struct ScanShape {
+  static constexpr int RPW = VPL <= 4 ? 4 : (VPL <= 8 ? 2 : 1);       // rows per consumer warp per stage
+  static constexpr int ROWS = SCAN_CONSUMER_WARPS * RPW;               // rows per stage
+};
+template <int KCAP> struct TopkShape {
+  static constexpr int BUF = 64;
+  static constexpr int SORTN = (KCAP + BUF <= 128) ? 128 : ((KCAP + BUF <= 256) ? 256 : 512);
+};
+constexpr int MAX_STAGES = 8;
+
+__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct ScanLayout {
+  size_t stage_bytes, stages_off, bars_off, rows_off, n_off, topk_off, sel_off, scratch_off, total;
+};
+__host__ __device__ inline ScanLayout scan_layout(int rows_per_stage, int row_bytes, int stages, int sortn,
+                                                  int kcap) {
+  ScanLayout L;
+  L.stage_bytes = align_up((size_t)rows_per_stage * row_bytes, 128);
+  L.stages_off = 0;
+  L.bars_off = align_up(L.stages_off + stages * L.stage_bytes, 128);
+  L.rows_off = L.bars_off + 2 * MAX_STAGES * sizeof(uint64_t);
+  L.n_off = L.rows_off + (size_t)MAX_STAGES * 32 * sizeof(int);
+  L.topk_off = align_up(L.n_off + MAX_STAGES * sizeof(int), 128);
+  L.sel_off = L.topk_off + (size_t)SCAN_CONSUMER_WARPS * sortn * 8;
+  L.scratch_off = align_up(L.sel_off + (size_t)kcap * 8, 128);
+  L.total = align_up(L.scratch_off + sizeof(SelectScratch) + 16, 128);
+  return L;
+}
+
+template <int VPL, int KCAP>
+__global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
+  using SS = ScanShape<VPL>;
+  using TS = TopkShape<KCAP>;
+  constexpr int RPW = SS::RPW, ROWS = SS::ROWS, SORTN = TS::SORTN, BUF = TS::BUF;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const ScanLayout L = scan_layout(ROWS, P.row_bytes, P.stages, SORTN, KCAP);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars_off);
+  uint64_t* empty = full + MAX_STAGES;
+  int* stage_rows = reinterpret_cast<int*>(smem + L.rows_off);
+  int* stage_n = reinterpret_cast<int*>(smem + L.n_off);
+  unsigned long long* topk_all = reinterpret_cast<unsigned long long*>(smem + L.topk_off);
+  unsigned long long* sel = reinterpret_cast<unsigned long long*>(smem + L.sel_off);
+  SelectScratch* scratch = reinterpret_cast<SelectScratch*>(smem + L.scratch_off);
+  __shared__ int s_is_last;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int STAGES = P.stages;
+  const int k = P.k;
+
+  for (int i = tid; i < SCAN_CONSUMER_WARPS * SORTN; i += blockDim.x) topk_all[i] = 0ull;
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], SCAN_CONSUMER_WARPS);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == SCAN_CONSUMER_WARPS) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t policy = policy_evict_first();
+      const unsigned long long pc = ld_volatile_u64(P.packed_counts);
+      const uint32_t n_ranges = (uint32_t)(pc >> 32), n_rows = (uint32_t)pc;
+      const uint32_t vb = (uint32_t)(((unsigned long long)blockIdx.x * n_rows) / gridDim.x);
+      const uint32_t ve = (uint32_t)(((unsigned long long)(blockIdx.x + 1) * n_rows) / gridDim.x);
+      int s = 0;
+      int4 rg = make_int4(0, 0, 0, 0);
+      if (vb < ve && n_ranges > 0) {
+        int lo = 0, hi = (int)n_ranges - 1;
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if ((uint32_t)__ldcg(&P.ranges[mid].x) <= vb) lo = mid; else hi = mid - 1;
+        }
+        s = lo;
+        rg = __ldcg(&P.ranges[s]);
+      }
+      uint32_t v = vb;
+      int it = 0;
+      bool ok = true;
+      const char* leaf_bytes = reinterpret_cast<const char*>(P.leaf);
+      while (v < ve) {
+        const int stage = it % STAGES, f = it / STAGES;
+        if (f > 0 && !mbar_wait(&empty[stage], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) { ok = false; break; }
+        int* srows = stage_rows + stage * 32;
+        int n = 0;
+        while (n < ROWS && v < ve) {
+          const uint32_t rlen = (uint32_t)(rg.z - rg.y);
+          if (v >= (uint32_t)rg.x + rlen) {
+            ++s;
+            if (s >= (int)n_ranges) { atomicOr(P.err, ERR_BAD_RANGE); v = ve; break; }
+            rg = __ldcg(&P.ranges[s]);
+            continue;
+          }
+          const uint32_t row = (uint32_t)rg.y + (v - (uint32_t)rg.x);
+          const uint32_t take = min(min((uint32_t)(ROWS - n), ve - v), (uint32_t)rg.z - row);
+          for (uint32_t i = 0; i < take; ++i) srows[n + i] = (int)(row + i);
+          n += (int)take;
+          v += take;
+        }
+        stage_n[stage] = n;
+        mbar_arrive_expect_tx(&full[stage], (uint32_t)n * (uint32_t)P.row_bytes);
+        unsigned char* dst = smem + L.stages_off + (size_t)stage * L.stage_bytes;
+        int i = 0;
+        while (i < n) {
+          int j = i + 1;
+          while (j < n && srows[j] == srows[j - 1] + 1) ++j;
+          tma_load_1d_stream(dst + (size_t)i * P.row_bytes, leaf_bytes + (size_t)srows[i] * P.row_bytes,
+                             (uint32_t)(j - i) * (uint32_t)P.row_bytes, &full[stage], policy);
+          i = j;
+        }
+        ++it;
+      }
+      const int stage = it % STAGES, f = it / STAGES;
+      if (ok && f > 0) mbar_wait(&empty[stage], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY);
+      stage_n[stage] = -1;
+      mbar_arrive(&full[stage]);
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    float4 qv[VPL];
+    const float4* q4 = reinterpret_cast<const float4*>(P.q);
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+      const int c = lane + 32 * v;
+      qv[v] = (c < P.D4) ? __ldg(q4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    unsigned long long* tk = topk_all + warp * SORTN;
+    uint32_t theta_w = 0;                                 // this warp's k-th best key
+    uint32_t theta = ld_volatile_u32(P.theta_key);        // filter key (max of both)
+    int cnt = 0;                                          // buffered candidates
+    uint32_t published = 0;
+
+    auto merge = [&]() {
+      __syncwarp();
+      warp_bitonic_desc(tk, SORTN, lane);
+      for (int i = KCAP + lane; i < SORTN; i += 32) tk[i] = 0ull;
+      __syncwarp();
+      cnt = 0;
+      const uint32_t kth = cand_key(tk[k - 1]);
+      if (kth > theta_w) {
+        theta_w = kth;
+        if (kth > published) {
+          if (lane == 0) atomicMax(P.theta_key, kth);
+          published = kth;
+        }
+      }
+      theta = max(theta, theta_w);
+      __syncwarp();
+    };
+
+    for (int it = 0;; ++it) {
+      const int stage = it % STAGES, f = it / STAGES;
+      if (!mbar_wait(&full[stage], f & 1, P.err, ERR_TIMEOUT_FULL)) break;
+      const int n = stage_n[stage];
+      if (n < 0) break;
+      {
+        uint32_t g = 0;
+        if (lane == 0) g = ld_volatile_u32(P.theta_key);
+        g = __shfl_sync(FULL_MASK, g, 0);
+        theta = max(theta, g);
+      }
+      const float4* stage_f4 =
+          reinterpret_cast<const float4*>(smem + L.stages_off + (size_t)stage * L.stage_bytes);
+      float acc[RPW];
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        acc[r] = 0.f;
+        const int slot = warp * RPW + r;
+        if (slot < n) {
+          const float4* row = stage_f4 + (size_t)slot * P.D4;
+#pragma unroll
+          for (int v = 0; v < VPL; ++v) {
+            const int c = lane + 32 * v;
+            if (c < P.D4) {
+              const float4 x = row[c];
+              acc[r] = fmaf(x.x, qv[v].x, acc[r]);
+              acc[r] = fmaf(x.y, qv[v].y, acc[r]);
+              acc[r] = fmaf(x.z, qv[v].z, acc[r]);
+              acc[r] = fmaf(x.w, qv[v].w, acc[r]);
+            }
+          }
+        }
+      }
+      // multi-row butterfly: every row is reduced with the same xor tree
+      // (16, 8, 4, 2, 1), so a row's score does not depend on its slot.
+      float score;
+      int rloc;
+      if constexpr (RPW == 4) {
+        const bool h16 = lane & 16, h8 = lane & 8;
+        const float t0 = __shfl_xor_sync(FULL_MASK, h16 ? acc[0] : acc[2], 16);
+        const float t1 = __shfl_xor_sync(FULL_MASK, h16 ? acc[1] : acc[3], 16);
+        const float b0 = (h16 ? acc[2] : acc[0]) + t0;
+        const float b1 = (h16 ? acc[3] : acc[1]) + t1;
+        const float t = __shfl_xor_sync(FULL_MASK, h8 ? b0 : b1, 8);
+        score = (h8 ? b1 : b0) + t;
+        score += __shfl_xor_sync(FULL_MASK, score, 4);
+        score += __shfl_xor_sync(FULL_MASK, score, 2);
+        score += __shfl_xor_sync(FULL_MASK, score, 1);
+        rloc = (h16 ? 2 : 0) + (h8 ? 1 : 0);
+      } else if constexpr (RPW == 2) {
+        const bool h16 = lane & 16;
+        const float t = __shfl_xor_sync(FULL_MASK, h16 ? acc[0] : acc[1], 16);
+        score = (h16 ? acc[1] : acc[0]) + t;
+        score += __shfl_xor_sync(FULL_MASK, score, 8);
+        score += __shfl_xor_sync(FULL_MASK, score, 4);
+        score += __shfl_xor_sync(FULL_MASK, score, 2);
+        score += __shfl_xor_sync(FULL_MASK, score, 1);
+        rloc = h16 ? 1 : 0;
+      } else {
+        score = acc[0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) score += __shfl_xor_sync(FULL_MASK, score, o);
+        rloc = 0;
+      }
+      const bool owner = (lane & (32 / RPW - 1)) == 0;
+      const int slot = warp * RPW + rloc;
+      const uint32_t key = f2key(score);
+      const bool cand = owner && slot < n && key >= theta;
+      int row = 0;
+      if (cand) row = stage_rows[stage * 32 + slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      const uint32_t bal = __ballot_sync(FULL_MASK, cand);
+      if (bal) {
+        const int nn = __popc(bal);
+        if (cnt + nn > BUF) merge();
+        if (cand) tk[KCAP + cnt + __popc(bal & lanemask_lt())] = pack_cand(key, (uint32_t)row);
+        cnt += nn;
+      }
+    }
+    if (cnt > 0) merge();
+  }
+  __syncthreads();
+
+  // ---------------------------------------------------------- CTA merge
+  const int selN = KCAP;  // KCAP is a power of two >= k
+  const int got = block_select_topk<false>(topk_all, SCAN_CONSUMER_WARPS * SORTN, k, sel, selN, scratch);
+  (void)got;
+  for (int i = tid; i < k; i += blockDim.x) P.cta_lists[(size_t)blockIdx.x * k + i] = sel[i];
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const uint32_t t = atomicAdd(P.done, 1u);
+    s_is_last = (t == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!s_is_last) return;
+  __threadfence();
+
+  // ---------------------------------------------------------- grid merge (last CTA)
+  int M = gridDim.x * k;
+  if (P.final_mode && P.merge_seed) {
+    for (int i = tid; i < k; i += blockDim.x) P.cta_lists[(size_t)gridDim.x * k + i] = P.seed_list[i];
+    M += k;
+    __threadfence_block();
+    __syncthreads();
+  }
+  const int cnt_sel = block_select_topk<true>(P.cta_lists, M, k, sel, selN, scratch);
+  if (!P.final_mode) {
+    for (int i = tid; i < k; i += blockDim.x) P.seed_list[i] = sel[i];
+    if (tid == 0) {
+      const uint32_t T = (cnt_sel == k) ? cand_key(sel[k - 1]) : 0u;
+      *P.seed_T_key = T;
+      if (T > *P.theta_key) *P.theta_key = T;
+    }
+  } else {
+    for (int i = tid; i < k; i += blockDim.x) {
+      const unsigned long long c = sel[i];
+      if (c != 0ull) {
+        const uint32_t row = cand_row(c);
+        P.out_scores[i] = key2f(cand_key(c));
+        if (P.out_ids) P.out_ids[i] = P.original_ids ? P.original_ids[row] : (int)row;
+        if (P.out_rows) P.out_rows[i] = (long long)row;
+      } else {
+        P.out_scores[i] = -INFINITY;
+        if (P.out_ids) P.out_ids[i] = -1;
+        if (P.out_rows) P.out_rows[i] = -1;
+      }
+    }
+  }
+}
+
+// ============================================================ root scan (K1)
+__global__ void __launch_bounds__(ROOT_SCAN_WARPS * 32) k_root_scan(IndexView ix, const float* __restrict__ q,
+                                                                     SearchCtrl* ctrl, float* __restrict__ root_dots,
+                                                                     int4* __restrict__ seed_ranges, int k) {
+  __shared__ unsigned long long s_best[ROOT_SCAN_WARPS];
+  __shared__ int s_last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int p = blockIdx.x * ROOT_SCAN_WARPS + warp;
+  const float4* q4 = reinterpret_cast<const float4*>(q);
+  unsigned long long packed = 0ull;
+  if (p < ix.R) {
+    const float4* c4 = reinterpret_cast<const float4*>(ix.root_centers + (size_t)p * ix.D);
+    float acc = 0.f;
+    for (int c = lane; c < ix.D4; c += 32) {
+      const float4 a = __ldg(q4 + c), b = __ldg(c4 + c);
+      acc = fmaf(a.x, b.x, acc);
+      acc = fmaf(a.y, b.y, acc);
+      acc = fmaf(a.z, b.z, acc);
+      acc = fmaf(a.w, b.w, acc);
+    }
+    const float dot = warp_sum(acc);
+    if (lane == 0) root_dots[p] = dot;
+    const int rows = ix.root_rows[p];
+    const unsigned long long prio = rows >= k ? 2ull : (rows > 0 ? 1ull : 0ull);
+    packed = (prio << 62) | ((unsigned long long)f2key(dot) << 30) | (unsigned long long)(0x3fffffff - p);
+  }
+  if (blockIdx.x == 0 && warp == 0) {
+    float acc = 0.f;
+    for (int c = lane; c < ix.D4; c += 32) {
+      const float4 a = __ldg(q4 + c);
+      acc = fmaf(a.x, a.x, acc);
+      acc = fmaf(a.y, a.y, acc);
+      acc = fmaf(a.z, a.z, acc);
+      acc = fmaf(a.w, a.w, acc);
+    }
+    const float qn2 = warp_sum(acc);
+    if (lane == 0) ctrl->qn2 = qn2;
+  }
+  if (lane == 0) s_best[warp] = packed;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long b = 0ull;
+    for (int w = 0; w < ROOT_SCAN_WARPS; ++w) b = max(b, s_best[w]);
+    if (b) atomicMax(&ctrl->best_packed, b);
+    __threadfence();
+    const uint32_t t = atomicAdd(&ctrl->k1_done, 1u);
+    s_last = (t == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!s_last || warp != 0) return;
+  __threadfence();
+  const unsigned long long best = ld_volatile_u64(&ctrl->best_packed);
+  int pb = 0x3fffffff - (int)(best & 0x3fffffffull);
+  if (pb < 0 || pb >= ix.R) pb = 0;  // only reachable with NaN scores; keeps the CSR reads in bounds
+  const int cb = ix.root_child_ptr[pb], ce = ix.root_child_ptr[pb + 1];
+  uint32_t n = 0, vrow = 0;
+  for (int c0 = cb; c0 < ce; c0 += 32) {
+    const int ci = c0 + lane;
+    int c = -1, off = 0, size = 0;
+    if (ci < ce) {
+      c = ix.root_child_list[ci];
+      off = ix.leaf_offsets[c];
+      size = ix.leaf_sizes[c];
+    }
+    const int incl = warp_incl_scan(size, lane);
+    if (ci < ce) seed_ranges[n + lane] = make_int4((int)vrow + incl - size, off, off + size, c);
+    n += (uint32_t)min(32, ce - c0);
+    vrow += (uint32_t)__shfl_sync(FULL_MASK, incl, 31);
+  }
+  if (lane == 0) {
+    ctrl->best_root = pb;
+    ctrl->seed_packed = ((unsigned long long)n << 32) | vrow;
+    ctrl->n_surv_children = n;
+  }
+}
+
+// ============================================================ bounds (K3)
+struct BoundsLayout {
+  size_t q_off, warp_off, chunk_bytes, warp_bytes, total;
+};
+__host__ __device__ inline BoundsLayout bounds_layout(int D, int rank, int chunk_rows) {
+  BoundsLayout L;
+  L.q_off = 0;
+  L.chunk_bytes = align_up((size_t)chunk_rows * rank * 4, 128);
+  L.warp_off = align_up((size_t)D * 4, 128);
+  // 2 chunk buffers + 64 red(a) + 64 red(s)... + a[64] + s[64] + 2 mbarriers
+  L.warp_bytes = align_up(2 * L.chunk_bytes + (64 + 64 + 64 + 64) * 4 + 2 * 8, 128);
+  L.total = L.warp_off + BOUNDS_WARPS * L.warp_bytes;
+  return L;
+}
+
+__global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, const float* __restrict__ q,
+                                                               SearchCtrl* ctrl, const float* __restrict__ root_dots,
+                                                               int4* __restrict__ main_ranges, int chunk_rows) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int D = ix.D, r = ix.rank;
+  const BoundsLayout L = bounds_layout(D, r, chunk_rows);
+  float* sq = reinterpret_cast<float*>(smem + L.q_off);
+  unsigned char* wb = smem + L.warp_off + (size_t)warp * L.warp_bytes;
+  float* buf0 = reinterpret_cast<float*>(wb);
+  float* buf1 = reinterpret_cast<float*>(wb + L.chunk_bytes);
+  float* red = reinterpret_cast<float*>(wb + 2 * L.chunk_bytes);  // [64] a partials, [64] s partials
+  float* sa = red + 128;                                           // [64]
+  float* ss = sa + 64;                                             // [64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ss + 64);
+
+  for (int i = threadIdx.x; i < D; i += blockDim.x) sq[i] = q[i];
+  if (lane == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const uint32_t Tkey = ctrl->seed_T_key;
+  const double T = Tkey ? (double)key2f(Tkey) : -INFINITY;
+  const int best = ctrl->best_root;
+  const double gD = gamma_n(D);
+  const double QN = sqrt((double)ctrl->qn2 / (1.0 - gD)) * (1.0 + 1e-15);
+  const int n_chunks = (D + chunk_rows - 1) / chunk_rows;
+  uint32_t ph0 = 0, ph1 = 0;
+  uint32_t surv_roots = 0, surv_children = 0;
+  bool abort_all = false;
+
+  for (int p = blockIdx.x * BOUNDS_WARPS + warp; p < ix.R && !abort_all; p += gridDim.x * BOUNDS_WARPS) {
+    if (p == best) { ++surv_roots; continue; }
+    if (ix.root_rows[p] == 0) continue;
+    const double dot = (double)root_dots[p];
+    const double cn = ix.root_cn[p];
+    const double rad = (double)ix.root_radii[p];
+    const double e_dot = gD * QN * cn;            // |fl(q.c) - q.c|
+    const double e_leaf = gD * QN * (cn + rad);   // |fl(q.x) - q.x| for ||x|| <= ||c|| + rad
+    double ub_root = dot + e_dot + QN * rad + e_leaf;
+    ub_root += 1e-12 * (fabs(dot) + QN * rad + e_dot + e_leaf);
+    if (ub_root < T) continue;
+    ++surv_roots;
+
+    // ---- projection a = V^T q (and s = |V|^T |q|) with the basis staged by TMA
+    const char* Vp = reinterpret_cast<const char*>(ix.bases + (size_t)p * D * r);
+    if (lane == 0) {
+      const int nr0 = min(chunk_rows, D);
+      mbar_arrive_expect_tx(&bars[0], (uint32_t)(nr0 * r * 4));
+      tma_load_1d(buf0, Vp, (uint32_t)(nr0 * r * 4), &bars[0]);
+      if (n_chunks > 1) {
+        const int nr1 = min(chunk_rows, D - chunk_rows);
+        mbar_arrive_expect_tx(&bars[1], (uint32_t)(nr1 * r * 4));
+        tma_load_1d(buf1, Vp + (size_t)chunk_rows * r * 4, (uint32_t)(nr1 * r * 4), &bars[1]);
+      }
+    }
+    float a0 = 0.f, a1 = 0.f, s0 = 0.f, s1 = 0.f;
+    for (int ch = 0; ch < n_chunks; ++ch) {
+      const int b = ch & 1;
+      const bool ok = b ? mbar_wait(&bars[1], ph1, &ctrl->error, ERR_TIMEOUT_BASIS)
+                        : mbar_wait(&bars[0], ph0, &ctrl->error, ERR_TIMEOUT_BASIS);
+      if (!ok) { abort_all = true; break; }
+      if (b) ph1 ^= 1u; else ph0 ^= 1u;
+      const float* Vc = b ? buf1 : buf0;
+      const int d0 = ch * chunk_rows;
+      const int nr = min(chunk_rows, D - d0);
+      if (r <= 32) {
+        const int G = 32 / r, g = lane / r, j = lane - g * r;
+        if (g < G) {
+          for (int dl = g; dl < nr; dl += G) {
+            const float v = Vc[dl * r + j], qq = sq[d0 + dl];
+            a0 = fmaf(v, qq, a0);
+            s0 = fmaf(fabsf(v), fabsf(qq), s0);
+          }
+        }
+      } else {
+        const bool two = lane + 32 < r;
+        for (int dl = 0; dl < nr; ++dl) {
+          const float qq = sq[d0 + dl];
+          const float v0 = Vc[dl * r + lane];
+          a0 = fmaf(v0, qq, a0);
+          s0 = fmaf(fabsf(v0), fabsf(qq), s0);
+          if (two) {
+            const float v1 = Vc[dl * r + lane + 32];
+            a1 = fmaf(v1, qq, a1);
+            s1 = fmaf(fabsf(v1), fabsf(qq), s1);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0 && ch + 2 < n_chunks) {
+        const int d2 = (ch + 2) * chunk_rows;
+        const int nr2 = min(chunk_rows, D - d2);
+        uint64_t* bar = b ? &bars[1] : &bars[0];
+        mbar_arrive_expect_tx(bar, (uint32_t)(nr2 * r * 4));
+        tma_load_1d(b ? buf1 : buf0, Vp + (size_t)d2 * r * 4, (uint32_t)(nr2 * r * 4), bar);
+      }
+    }
+    if (abort_all) break;
+    if (r <= 32) {
+      red[lane] = a0;
+      red[64 + lane] = s0;
+      __syncwarp();
+      if (lane < r) {
+        const int G = 32 / r;
+        float A = 0.f, S = 0.f;
+        for (int g = 0; g < G; ++g) { A += red[g * r + lane]; S += red[64 + g * r + lane]; }
+        sa[lane] = A;
+        ss[lane] = S;
+      }
+    } else {
+      sa[lane] = a0;
+      ss[lane] = s0;
+      if (lane + 32 < r) { sa[lane + 32] = a1; ss[lane + 32] = s1; }
+    }
+    __syncwarp();
+
+    // ---- rigorous residual norm ||q - V a|| (upper bound), see DESIGN notes
+    double an2 = 0.0, sad = 0.0;
+    for (int j = 0; j < r; ++j) {
+      const double aj = sa[j];
+      an2 += aj * aj;
+      sad += fabs(aj) * gD * (double)ss[j] * (1.0 + 2.0 * gD);
+    }
+    an2 *= (1.0 + 1e-15);
+    const double E = ix.root_defect[p];
+    const double perp_sq = QN * QN - an2 + 2.0 * sad + E * an2;
+    const double perp = sqrt(fmax(perp_sq, 0.0)) * (1.0 + 1e-15);
+    const double an = sqrt(an2) * (1.0 + 1e-15);
+
+    // ---- children: lane per child
+    const int cb = ix.root_child_ptr[p], ce = ix.root_child_ptr[p + 1];
+    for (int c0 = cb; c0 < ce; c0 += 32) {
+      const int ci = c0 + lane;
+      bool surv = false;
+      int c = -1, off = 0, size = 0;
+      if (ci < ce) {
+        c = ix.root_child_list[ci];
+        off = ix.leaf_offsets[c];
+        size = ix.leaf_sizes[c];
+        const float* lp = ix.child_l + (size_t)c * r;
+        const float* up = ix.child_u + (size_t)c * r;
+        double box = 0.0, ebox = 0.0, wn2 = 0.0;
+        if ((r & 3) == 0) {
+          for (int j = 0; j < r; j += 4) {
+            const float4 l4 = __ldg(reinterpret_cast<const float4*>(lp + j));
+            const float4 u4 = __ldg(reinterpret_cast<const float4*>(up + j));
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const double aj = sa[j + t];
+              box += fmax(aj * lv[t], aj * uv[t]);
+              const double w = fmax(fabs((double)lv[t]), fabs((double)uv[t]));
+              ebox += (double)ss[j + t] * w;
+              wn2 += w * w;
+            }
+          }
+        } else {
+          for (int j = 0; j < r; ++j) {
+            const double aj = sa[j];
+            const double lv = lp[j], uv = up[j];
+            box += fmax(aj * lv, aj * uv);
+            const double w = fmax(fabs(lv), fabs(uv));
+            ebox += (double)ss[j] * w;
+            wn2 += w * w;
+          }
+        }
+        ebox *= gD * (1.0 + 2.0 * gD);
+        const double rho = (double)ix.child_radii[c];
+        double ub = dot + e_dot + box + ebox + an * E * sqrt(wn2) * (1.0 + 1e-15) + perp * rho + e_leaf;
+        ub += 1e-12 * (fabs(dot) + fabs(box) + perp * rho + e_dot + e_leaf + ebox);
+        surv = !(ub < T);
+      }
+      const uint32_t bal = __ballot_sync(FULL_MASK, surv);
+      const int rows_l = surv ? size : 0;
+      const int incl = warp_incl_scan(rows_l, lane);
+      const int total = __shfl_sync(FULL_MASK, incl, 31);
+      const int nsurv = __popc(bal);
+      unsigned long long old = 0ull;
+      if (lane == 0 && nsurv)
+        old = atomicAdd(&ctrl->main_packed, ((unsigned long long)nsurv << 32) | (unsigned long long)(uint32_t)total);
+      old = __shfl_sync(FULL_MASK, old, 0);
+      if (surv) {
+        const uint32_t slot = (uint32_t)(old >> 32) + __popc(bal & lanemask_lt());
+        const uint32_t vbegin = (uint32_t)old + (uint32_t)(incl - size);
+        main_ranges[slot] = make_int4((int)vbegin, off, off + size, c);
+      }
+      surv_children += (uint32_t)nsurv;
+    }
+  }
+  if (lane == 0) {
+    if (surv_roots) atomicAdd(&ctrl->n_surv_roots, surv_roots);
+    if (surv_children) atomicAdd(&ctrl->n_surv_children, surv_children);
+  }
+}
+
+// ============================================================ index preparation
+// Per root: an upper bound of ||c_r|| and of ||V_r^T V_r - I||_2 (Frobenius norm
+// of the Gram defect, accumulated in fp64 with an absolute slack per entry).
+__global__ void k_prepare_roots(IndexView ix, double* __restrict__ root_cn, double* __restrict__ root_defect) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int p = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (p >= ix.R) return;
+  const int D = ix.D, r = ix.rank;
+  const float* c = ix.root_centers + (size_t)p * D;
+  double acc = 0.0;
+  for (int d = lane; d < D; d += 32) acc += (double)c[d] * (double)c[d];
+  acc = warp_sum_d(acc);
+  const float* V = ix.bases + (size_t)p * D * r;
+  double fro = 0.0;
+  const int npairs = r * (r + 1) / 2;
+  for (int t = lane; t < npairs; t += 32) {
+    int j = 0, rem = t;
+    while (rem >= r - j) { rem -= r - j; ++j; }
+    const int kk = j + rem;
+    double g = 0.0, ga = 0.0;
+    for (int d = 0; d < D; ++d) {
+      const double x = (double)V[(size_t)d * r + j] * (double)V[(size_t)d * r + kk];
+      g += x;
+      ga += fabs(x);
+    }
+    const double e = fabs(g - (j == kk ? 1.0 : 0.0)) + 1e-13 * (1.0 + ga);
+    fro += (j == kk ? 1.0 : 2.0) * e * e;
+  }
+  fro = warp_sum_d(fro);
+  if (lane == 0) {
+    root_cn[p] = sqrt(acc) * (1.0 + 1e-12) + 1e-30;
+    root_defect[p] = sqrt(fro) * (1.0 + 1e-12) + 1e-30;
+  }
+}
+
+// ============================================================ host launchers
+int sm_count(int device) {
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0) n = 148;
+  return n;
+}
+
+static int vpl_bucket(int D4) {
+  const int v = (D4 + 31) / 32;
+  if (v <= 1) return 1;
+  if (v <= 2) return 2;
+  if (v <= 3) return 3;
+  if (v <= 4) return 4;
+  if (v <= 6) return 6;
+  if (v <= 8) return 8;
+  if (v <= 12) return 12;
+  return 16;
+}
+static int kcap_bucket(int k) { return k <= 32 ? 32 : (k <= 128 ? 128 : 256); }
+static int rows_per_stage(int vpl) { return vpl <= 4 ? 32 : (vpl <= 8 ? 16 : 8); }
+static int sortn_for(int kcap) { return kcap + 64 <= 128 ? 128 : (kcap + 64 <= 256 ? 256 : 512); }
+static int stages_for(int vpl, int row_bytes) {
+  const size_t sb = align_up((size_t)rows_per_stage(vpl) * row_bytes, 128);
+  int s = (int)(147456 / sb);
+  return s < 2 ? 2 : (s > MAX_STAGES ? MAX_STAGES : s);
+}
+
+int scan_smem_bytes(int D) {
+  const int vpl = vpl_bucket(D / 4);
+  const ScanLayout L = scan_layout(rows_per_stage(vpl), D * 4, stages_for(vpl, D * 4), sortn_for(256), 256);
+  return (int)L.total;
+}
+
+template <int VPL, int KCAP>
+static cudaError_t launch_scan_t(const ScanParams& P, int grid, cudaStream_t stream) {
+  const ScanLayout L = scan_layout(ScanShape<VPL>::ROWS, P.row_bytes, P.stages, TopkShape<KCAP>::SORTN, KCAP);
+  static int configured_bytes = 0;  // per instantiation; the attribute is process-wide
+  if ((int)L.total > configured_bytes) {
+    cudaError_t e = cudaFuncSetAttribute(k_scan<VPL, KCAP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+    if (e != cudaSuccess) return e;
+    configured_bytes = (int)L.total;
+  }
+  k_scan<VPL, KCAP><<<grid, SCAN_THREADS, L.total, stream>>>(P);
+  return cudaGetLastError();
+}
+
+template <int VPL>
+static cudaError_t launch_scan_v(const ScanParams& P, int grid, cudaStream_t stream) {
+  const int kc = kcap_bucket(P.k);
+  if (kc == 32) return launch_scan_t<VPL, 32>(P, grid, stream);
+  if (kc == 128) return launch_scan_t<VPL, 128>(P, grid, stream);
+  return launch_scan_t<VPL, 256>(P, grid, stream);
+}
+
+static cudaError_t launch_scan(const ScanParams& P, int grid, cudaStream_t stream) {
+  switch (vpl_bucket(P.D4)) {
+    case 1: return launch_scan_v<1>(P, grid, stream);
+    case 2: return launch_scan_v<2>(P, grid, stream);
+    case 3: return launch_scan_v<3>(P, grid, stream);
+    case 4: return launch_scan_v<4>(P, grid, stream);
+    case 6: return launch_scan_v<6>(P, grid, stream);
+    case 8: return launch_scan_v<8>(P, grid, stream);
+    case 12: return launch_scan_v<12>(P, grid, stream);
+    default: return launch_scan_v<16>(P, grid, stream);
+  }
+}
+
+static int bounds_chunk_rows(int D, int rank) {
+  int rows = (12288 / (rank * 4)) & ~3;
+  if (rows < 4) rows = 4;
+  const int Dr = (D + 3) & ~3;
+  return rows > Dr ? Dr : rows;
+}
+
+cudaError_t launch_prepare_roots(const IndexView& ix, double* root_cn, double* root_defect, cudaStream_t stream) {
+  const int warps = 4;
+  k_prepare_roots<<<(ix.R + warps - 1) / warps, warps * 32, 0, stream>>>(ix, root_cn, root_defect);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float* q, int k, int hierarchical,
+                          float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
+                          cudaEvent_t ev_scan0, cudaEvent_t ev_scan1) {
+  cudaError_t e = cudaMemsetAsync(ws.ctrl, 0, CTRL_RESET_BYTES, stream);
+  if (e != cudaSuccess) return e;
+  const int vpl = vpl_bucket(ix.D4);
+  ScanParams P{};
+  P.leaf = ix.leaf;
+  P.q = q;
+  P.theta_key = &ws.ctrl->theta_key;
+  P.cta_lists = ws.cta_lists;
+  P.err = &ws.ctrl->error;
+  P.D4 = ix.D4;
+  P.row_bytes = ix.D * 4;
+  P.k = k;
+  P.stages = stages_for(vpl, P.row_bytes);
+  P.seed_list = ws.ctrl->seed_list;
+  P.seed_T_key = &ws.ctrl->seed_T_key;
+  P.out_scores = out_scores;
+  P.out_ids = out_ids;
+  P.out_rows = out_rows;
+  P.original_ids = ix.original_ids;
+
+  if (hierarchical) {
+    k_root_scan<<<(ix.R + ROOT_SCAN_WARPS - 1) / ROOT_SCAN_WARPS, ROOT_SCAN_WARPS * 32, 0, stream>>>(
+        ix, q, ws.ctrl, ws.root_dots, ws.seed_ranges, k);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    ScanParams S = P;
+    S.ranges = ws.seed_ranges;
+    S.packed_counts = &ws.ctrl->seed_packed;
+    S.done = &ws.ctrl->seed_done;
+    S.final_mode = 0;
+    S.merge_seed = 0;
+    if ((e = launch_scan(S, ws.scan_grid, stream)) != cudaSuccess) return e;
+
+    const int chunk_rows = bounds_chunk_rows(ix.D, ix.rank);
+    const BoundsLayout BL = bounds_layout(ix.D, ix.rank, chunk_rows);
+    static int bounds_configured = 0;
+    if ((int)BL.total > bounds_configured) {
+      if ((e = cudaFuncSetAttribute(k_bounds, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BL.total)) !=
+          cudaSuccess)
+        return e;
+      bounds_configured = (int)BL.total;
+    }
+    int grid_b = (ix.R + BOUNDS_WARPS - 1) / BOUNDS_WARPS;
+    if (grid_b > 2 * ws.scan_grid) grid_b = 2 * ws.scan_grid;
+    k_bounds<<<grid_b, BOUNDS_WARPS * 32, BL.total, stream>>>(ix, q, ws.ctrl, ws.root_dots, ws.main_ranges,
+                                                               chunk_rows);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+
+    ScanParams M = P;
+    M.ranges = ws.main_ranges;
+    M.packed_counts = &ws.ctrl->main_packed;
+    M.done = &ws.ctrl->main_done;
+    M.final_mode = 1;
+    M.merge_seed = 1;
+    if (ev_scan0) cudaEventRecord(ev_scan0, stream);
+    e = launch_scan(M, ws.scan_grid, stream);
+    if (ev_scan1) cudaEventRecord(ev_scan1, stream);
+    return e;
+  }
+  ScanParams F = P;
+  F.ranges = ws.flat_range;
+  F.packed_counts = ws.flat_packed;
+  F.done = &ws.ctrl->main_done;
+  F.final_mode = 1;
+  F.merge_seed = 0;
+  if (ev_scan0) cudaEventRecord(ev_scan0, stream);
+  e = launch_scan(F, ws.scan_grid, stream);
+  if (ev_scan1) cudaEventRecord(ev_scan1, stream);
+  return e;
+}
+
+}  // namespace cb

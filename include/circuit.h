@@ -1,0 +1,152 @@
+/*
+ * circuit-b200 C ABI: exact top-k inner-product search over a .circuit index on
+ * one B200 (sm_100a) per process.
+ *
+ * Every entry point takes plain pointers and sizes; no torch or C++ types cross
+ * this boundary.  The first four functions and the two structs keep the exact
+ * names, argument meaning, layout and error behaviour of the reference's native
+ * library, so existing callers (e.g. circuit_bench) relink unchanged:
+ *
+ *   reference native/include/circuit/circuit.h:8-46  (declarations)
+ *   reference native/src/api.cpp:7-51                (NULL / -1 conventions)
+ *
+ * Differences a caller can observe (all deliberate):
+ *   - k is not clamped to 32; any 1 <= k <= CIRCUIT_MAX_K (and k <= N) works.
+ *     (reference clamps at gpu_index.cpp:243, :334)
+ *   - pruning is on: the hierarchical path seeds an on-device threshold and
+ *     prunes with rigorously inflated bounds; the reference native path runs
+ *     with threshold -1e9 (gpu_index.cpp:279) and never prunes.  Results are
+ *     identical to brute force in both.
+ *   - circuit_trace_t.vectors_scored counts the leaf rows actually scored
+ *     (reference always reports N, gpu_index.cpp:326).
+ *   - errors return a negative CIRCUIT_ERR_* code (reference returns 0 even
+ *     when CUDA calls fail); circuit_last_error() describes the last one.
+ *
+ * Threading: one in-flight search per index handle (the handle owns one
+ * device workspace), as in the reference.  Use one handle per thread/stream.
+ */
+#ifndef CIRCUIT_H
+#define CIRCUIT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CIRCUIT_ABI_VERSION 1
+#define CIRCUIT_MAX_K 256
+#define CIRCUIT_MAX_RANK 64
+#define CIRCUIT_MAX_DIM 2048
+
+/* error codes (0 = success) */
+#define CIRCUIT_OK 0
+#define CIRCUIT_ERR_NULL (-1)        /* null index handle (reference api.cpp:28-29, :41-42) */
+#define CIRCUIT_ERR_ARG (-2)         /* bad argument: k, pointer, size, alignment */
+#define CIRCUIT_ERR_CUDA (-3)        /* a CUDA runtime call failed */
+#define CIRCUIT_ERR_TIMEOUT (-4)     /* a bounded device-side wait gave up */
+#define CIRCUIT_ERR_IO (-5)          /* file open / read / mmap failed */
+#define CIRCUIT_ERR_FORMAT (-6)      /* malformed .circuit file or index arrays */
+#define CIRCUIT_ERR_UNSUPPORTED (-7) /* dim / rank / k outside the supported range */
+
+typedef struct circuit_index_opaque* circuit_index_t;
+
+/* reference circuit.h:10-14 (declared there, unused there and here) */
+typedef struct {
+  int top_k;
+  float threshold;
+  int use_cuda_graph;
+} circuit_search_config_t;
+
+/* reference circuit.h:16-19 */
+typedef struct {
+  float latency_us;
+  int vectors_scored;
+} circuit_trace_t;
+
+/* Extended per-search statistics (no reference counterpart). */
+typedef struct {
+  float latency_us;            /* host wall time of the call (0 for async calls) */
+  int32_t path;                /* 0 = flat scan, 1 = hierarchical */
+  int64_t vectors_scored;      /* leaf rows whose score was computed */
+  int64_t vectors_total;       /* N */
+  int32_t surviving_roots;     /* roots not pruned (seed root included) */
+  int32_t surviving_children;  /* non-empty children scanned */
+  int32_t total_children;      /* num_total_children */
+  int32_t best_root;           /* the seed root */
+  float seed_threshold;        /* k-th best score among the seed root's rows (-inf if none) */
+  int32_t device_error;        /* device error bits of the last search (0 = none) */
+} circuit_trace_ex_t;
+
+/* ------------------------------------------------------------------ reference ABI */
+
+/* Load a .circuit file onto device `device_id`.  NULL on failure.
+ * reference: circuit.h:22, api.cpp:7-19, gpu_index.cpp:50-141 */
+circuit_index_t circuit_load_index(const char* filepath, int device_id);
+
+/* Host query [dim] -> host out_scores[k] (descending), out_ids[k] (original ids).
+ * Blocking.  reference: circuit.h:25-32, gpu_index.cpp:242-330 */
+int circuit_search(circuit_index_t index, const float* query, int k, float* out_scores, int* out_ids,
+                   circuit_trace_t* trace);
+
+/* Device query -> device outputs.  Blocking (synchronises the handle's stream).
+ * reference: circuit.h:36-43, gpu_index.cpp:333-386 */
+int circuit_search_device(circuit_index_t index, const float* dev_query, int k, float* dev_out_scores,
+                          int* dev_out_ids, circuit_trace_t* trace);
+
+/* Free device memory, the mapping and the handle.  reference: circuit.h:46, api.cpp:47-51 */
+void circuit_destroy_index(circuit_index_t index);
+
+/* ------------------------------------------------------------------ extensions */
+
+/* Description of the last error on this thread ("" if none). */
+const char* circuit_last_error(void);
+int circuit_abi_version(void);
+
+/* Wrap index arrays that already live on `device_id` (borrowed: the caller keeps
+ * them alive and unmodified until circuit_destroy_index).  Shapes as in the
+ * .circuit format: root_centers [R,D], root_radii [R], bases [R,D,rank],
+ * child_intervals_l/u [C,rank], child_radii [C], child_parent_ids [C],
+ * leaf_offsets [C], leaf_sizes [C], leaf_vectors [N,D], original_ids [N].
+ * The small int arrays are read back once to build the per-root child lists.
+ * Backs the Python CircuitIndex (reference circuit_rag/hierarchy/build.py:7-49). */
+circuit_index_t circuit_index_from_device(int device_id, int dim, int rank, int num_roots, int num_total_children,
+                                          int64_t n, const float* root_centers, const float* root_radii,
+                                          const float* bases, const float* child_intervals_l,
+                                          const float* child_intervals_u, const float* child_radii,
+                                          const int* child_parent_ids, const int* leaf_offsets,
+                                          const int* leaf_sizes, const float* leaf_vectors,
+                                          const int* original_ids);
+
+/* info[0..7] = dim, rank, num_roots, num_total_children, N, device, scan CTAs, max k */
+int circuit_index_info(circuit_index_t index, int64_t* info);
+
+/* Asynchronous single-query search on `stream` (a cudaStream_t; NULL = the
+ * handle's own stream).  Routes to the flat scan when N < min_hierarchy_n
+ * (reference circuit_rag/search.py:55-57), else the hierarchical pipeline.
+ * dev_out_rows (optional, int64 [k]) receives leaf-row positions.
+ * ev_scan_begin / ev_scan_end (optional cudaEvent_t) are recorded on `stream`
+ * around the dominant leaf-scan kernel.  No host synchronisation. */
+int circuit_search_async(circuit_index_t index, const float* dev_query, int k, int64_t min_hierarchy_n,
+                         float* dev_out_scores, int* dev_out_ids, int64_t* dev_out_rows, void* stream,
+                         void* ev_scan_begin, void* ev_scan_end);
+
+/* Statistics of the last search on this handle (synchronises the stream it ran on). */
+int circuit_last_trace(circuit_index_t index, circuit_trace_ex_t* out);
+
+/* Non-blocking trace capture: enqueue on `stream` a copy of the last search's
+ * CIRCUIT_TRACE_SNAPSHOT_BYTES of device statistics into `dst` (device memory
+ * or pinned host memory).  Once those bytes are on the host,
+ * circuit_trace_decode turns them into a circuit_trace_ex_t (path: 0 flat,
+ * 1 hierarchical).
+ * Lets a caller keep per-query traces without a host sync per query. */
+#define CIRCUIT_TRACE_SNAPSHOT_BYTES 96
+int circuit_trace_snapshot_async(circuit_index_t index, void* dst, void* stream);
+int circuit_trace_decode(circuit_index_t index, const void* snapshot, int path, circuit_trace_ex_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CIRCUIT_H */

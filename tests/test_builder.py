@@ -1,0 +1,59 @@
+"""Builder invariants that the search's pruning relies on (CPU)."""
+import numpy as np
+import pytest
+import torch
+
+from circuit_rag import build_circuit_index, circuit_search
+from circuit_rag.synthetic import WORKLOADS
+
+
+def _check_invariants(idx, X):
+    lv = idx.leaf_vectors.double()
+    assert torch.equal(idx.leaf_vectors, torch.from_numpy(X)[idx.original_ids.long()])
+    assert sorted(idx.original_ids.tolist()) == list(range(len(X)))
+    covered = 0
+    for c in range(idx.num_total_children):
+        n = int(idx.leaf_sizes[c])
+        if n == 0:
+            continue
+        o, p = int(idx.leaf_offsets[c]), int(idx.child_parent_ids[c])
+        x = lv[o:o + n]
+        cP = idx.root_centers[p].double()
+        V = idx.bases[p].double()
+        d = x - cP
+        assert (d.norm(dim=1) <= idx.root_radii[p].double()).all()
+        z = d @ V
+        assert (z >= idx.child_intervals_l[c].double()).all() and (z <= idx.child_intervals_u[c].double()).all()
+        r = d - z @ V.T
+        assert (r.norm(dim=1) <= idx.child_radii[c].double()).all()
+        covered += n
+    assert covered == len(X)
+    # root-major, child-contiguous layout
+    offs = idx.leaf_offsets[idx.leaf_sizes > 0]
+    assert torch.all(offs[1:] > offs[:-1])
+
+
+@pytest.mark.parametrize("rank", [1, 8, 64])
+def test_certificates_hold_exactly(rank):
+    X = WORKLOADS["clustered-50k"].corpus(0, 3000).numpy()
+    idx = build_circuit_index(X, num_roots=8, children_per_root=4, rank=rank, device="cpu")
+    _check_invariants(idx, X)
+    V = idx.bases[0].double()
+    assert torch.allclose(V.T @ V, torch.eye(rank, dtype=torch.float64), atol=1e-5)
+
+
+def test_rank_limits():
+    X = np.random.default_rng(0).normal(size=(200, 8)).astype(np.float32)
+    with pytest.raises(ValueError):
+        build_circuit_index(X, num_roots=4, children_per_root=2, rank=65, device="cpu")
+    with pytest.raises(ValueError):
+        build_circuit_index(X, num_roots=4, children_per_root=2, rank=0, device="cpu")
+
+
+def test_search_requires_cuda_and_validates_shape():
+    X = np.random.default_rng(0).normal(size=(300, 8)).astype(np.float32)
+    idx = build_circuit_index(X, num_roots=4, children_per_root=2, rank=2, device="cpu")
+    with pytest.raises(ValueError):
+        circuit_search(torch.zeros(7), idx)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        circuit_search(torch.zeros(8), idx)
