@@ -55,11 +55,11 @@ def parse():
     return ap.parse_args()
 
 
-def dist_setup(n_gpus):
+def dist_setup(n_gpus, collectives=True):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
+    if world > 1 and collectives:
         import datetime
 
         import torch.distributed as dist
@@ -173,7 +173,7 @@ def run_reference(args, world, rank):
 
 def main():
     args = parse()
-    world, rank, local = dist_setup(args.gpus)
+    world, rank, local = dist_setup(args.gpus, collectives=args.impl == "ours")
     if args.impl == "reference":
         run_reference(args, world, rank)
         return
@@ -210,6 +210,9 @@ def main():
     out_i = torch.empty((steps, k), dtype=torch.int32, device=dev)
     q_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     s_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for pair in s_ev:  # torch creates the CUDA event on first record; the C ABI records them afterwards
+        for e in pair:
+            e.record(stream)
 
     def one(i, timed):
         q = Q[i]

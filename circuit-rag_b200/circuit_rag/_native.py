@@ -1,4 +1,4 @@
-"""ctypes binding of libcircuit.so (include/circuit.h and include/circuit_ops.h).
+"""ctypes binding of libcircuit.so (include/circuit.h, circuit_ops.h, circuit_shard.h).
 
 The library is built in-tree next to this file (``make -C circuit-rag_b200/csrc``
 or ``__graft_entry__.build()``).  There is no fallback: if the shared library is
@@ -36,6 +36,8 @@ EXPORTED_SYMBOLS = (
     "circuit_op_score_surviving_leaves",
     "circuit_op_flat_exact_score",
     "circuit_op_hierarchical_search",
+    "circuit_merge_topk",
+    "circuit_plan_shards",
 )
 
 
@@ -94,6 +96,8 @@ def _declare(lib):
         "circuit_op_score_surviving_leaves": (_I, [_P, _P, _P, _P, _P, _I, _I64, _I, _P, _P]),
         "circuit_op_flat_exact_score": (_I, [_P, _P, _I64, _I, _P, _P]),
         "circuit_op_hierarchical_search": (_I, [_P] * 21 + [_I, _I, _I64, _I, _F, _I, _F, _P]),
+        "circuit_merge_topk": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+        "circuit_plan_shards": (_I, [_P, _I, _I, _P, _P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -1,0 +1,172 @@
+"""Multi-GPU exact search: the corpus sharded by root cluster, one process per GPU.
+
+* ``plan_shards`` assigns roots to ranks by longest-processing-time on leaf rows
+  (Zipf-sized clusters make round-robin unbalanced).
+* ``load_shard`` reads a .circuit file and keeps only the roots one rank owns:
+  their centres, bases, children and leaf rows (read as byte ranges of the
+  file, never the whole corpus) with their global original ids.
+* ``ShardedSearcher.search`` runs the local exact search on the rank's GPU,
+  all-gathers the k (score, id) candidates of every rank (NCCL over
+  NVLink/NVSwitch; gloo works for CPU tests) and merges them on the device
+  (``circuit_merge_topk``).  Every rank returns the identical global top-k.
+
+Exactness: each shard's top-k contains every global top-k row it holds, so the
+merge of all shard lists is the global top-k (same (score desc, id asc) order).
+"""
+import ctypes
+import datetime
+import mmap
+from typing import Callable, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+
+from circuit_rag import _native
+from circuit_rag.hierarchy.build import CircuitIndex
+from circuit_rag.storage.format import TENSOR_ORDER, read_header
+
+
+def plan_shards(root_rows: Sequence[int], world: int) -> np.ndarray:
+    """root -> rank by longest-processing-time on leaf rows (circuit_plan_shards)."""
+    rows = np.ascontiguousarray(root_rows, dtype=np.int64)
+    out = np.empty(len(rows), dtype=np.int32)
+    _native.check(_native.lib().circuit_plan_shards(rows.ctypes.data, len(rows), int(world), out.ctypes.data, None),
+                  "plan_shards")
+    return out
+
+
+def _root_rows(parent: np.ndarray, sizes: np.ndarray, num_roots: int) -> np.ndarray:
+    live = sizes > 0
+    return np.bincount(parent[live], weights=sizes[live].astype(np.int64), minlength=num_roots).astype(np.int64)
+
+
+def load_shard(filepath: str, rank: int, world: int, device: str = "cuda") -> CircuitIndex:
+    """The part of a .circuit index that `rank` of `world` owns (complete roots)."""
+    meta = read_header(filepath)
+    R, C, D, r = (int(meta[k]) for k in ("num_roots", "num_total_children", "dim", "rank"))
+    with open(filepath, "rb") as f:
+        mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
+    try:
+        def arr(name):
+            info = meta["tensor_meta"][name]
+            return np.ndarray(buffer=mm, dtype=np.dtype(info["dtype"]), offset=int(info["offset"]),
+                              shape=tuple(info["shape"]))
+
+        parent, offsets, sizes = (arr(n).copy() for n in ("child_parent_ids", "leaf_offsets", "leaf_sizes"))
+        owner = plan_shards(_root_rows(parent, sizes, R), world)
+        roots = np.nonzero(owner == rank)[0]
+        live = sizes > 0
+        kids = [np.nonzero(live & (parent == p))[0] for p in roots]
+        kids = [k[np.argsort(offsets[k], kind="stable")] for k in kids]
+        cpr = max([len(k) for k in kids] + [1])
+        Rs, Cs = len(roots), max(1, len(roots)) * cpr
+        n_rows = int(sum(int(sizes[k].sum()) for k in kids))
+        leaf_src, ids_src = arr("leaf_vectors"), arr("original_ids")
+        leaf = np.empty((n_rows, D), np.float32)
+        ids = np.empty(n_rows, np.int32)
+        cl, cu, crad = arr("child_intervals_l"), arr("child_intervals_u"), arr("child_radii")
+        new = {
+            "child_intervals_l": np.zeros((Cs, r), np.float32), "child_intervals_u": np.zeros((Cs, r), np.float32),
+            "child_radii": np.zeros(Cs, np.float32), "child_parent_ids": np.zeros(Cs, np.int32),
+            "leaf_offsets": np.zeros(Cs, np.int32), "leaf_sizes": np.zeros(Cs, np.int32),
+        }
+        cur = 0
+        for i, (p, ks) in enumerate(zip(roots, kids)):
+            for j, c in enumerate(ks):
+                g = i * cpr + j
+                o, n = int(offsets[c]), int(sizes[c])
+                leaf[cur:cur + n] = leaf_src[o:o + n]
+                ids[cur:cur + n] = ids_src[o:o + n]
+                new["child_intervals_l"][g] = cl[c]
+                new["child_intervals_u"][g] = cu[c]
+                new["child_radii"][g] = crad[c]
+                new["child_parent_ids"][g] = i
+                new["leaf_offsets"][g] = cur
+                new["leaf_sizes"][g] = n
+                cur += n
+            for j in range(len(ks), cpr):
+                new["child_parent_ids"][i * cpr + j] = i
+        centers, radii, bases = arr("root_centers")[roots].copy(), arr("root_radii")[roots].copy(), \
+            arr("bases")[roots].copy()
+    finally:
+        mm.close()
+    if Rs == 0:
+        raise ValueError(f"rank {rank} owns no roots (world {world} > non-empty roots)")
+    return CircuitIndex(root_centers=centers, root_radii=radii, bases=bases, leaf_vectors=leaf, original_ids=ids,
+                        dim=D, rank=r, device=device, **new)
+
+
+def merge_topk(scores: torch.Tensor, ids: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Global top-k of gathered candidates on the device (circuit_merge_topk)."""
+    scores = scores.to(torch.float32).contiguous()
+    ids = ids.to(torch.int32).contiguous()
+    out_s = torch.empty(k, dtype=torch.float32, device=scores.device)
+    out_i = torch.empty(k, dtype=torch.int32, device=scores.device)
+    rc = _native.lib().circuit_merge_topk(scores.data_ptr(), ids.data_ptr(), scores.numel(), int(k), out_s.data_ptr(),
+                                          out_i.data_ptr(), torch.cuda.current_stream(scores.device).cuda_stream)
+    _native.check(rc, "merge_topk")
+    return out_s, out_i
+
+
+def merge_topk_host(scores: torch.Tensor, ids: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The same merge on host tensors (used with the gloo backend)."""
+    s = scores.double().numpy()
+    i = ids.numpy().astype(np.int64)
+    live = i >= 0
+    s, i = s[live], i[live]
+    order = np.lexsort((i, -s))[:k]
+    out_s = torch.full((k,), float("-inf"))
+    out_i = torch.full((k,), -1, dtype=torch.int32)
+    out_s[:len(order)] = torch.from_numpy(s[order]).float()
+    out_i[:len(order)] = torch.from_numpy(i[order]).int()
+    return out_s, out_i
+
+
+class ShardedSearcher:
+    """Exact top-k over a corpus sharded across the ranks of a process group."""
+
+    def __init__(self, index: Optional[CircuitIndex], group=None,
+                 local_search: Optional[Callable] = None, merge: Optional[Callable] = None):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.index = index
+        self._local = local_search or self._native_local
+        self._merge = merge or merge_topk
+
+    def _native_local(self, query: torch.Tensor, k: int, min_hierarchy_n: int):
+        from circuit_rag.search import circuit_search
+
+        s, i, _ = circuit_search(query, self.index, k=min(k, self.index.N), min_hierarchy_n=min_hierarchy_n)
+        if len(i) < k:  # a shard smaller than k: pad with empty slots
+            s = torch.cat([s, s.new_full((k - len(s),), float("-inf"))])
+            i = torch.cat([i, i.new_full((k - len(i),), -1)])
+        return s, i
+
+    def search(self, query: torch.Tensor, k: int = 10, min_hierarchy_n: int = 10000):
+        s, i = self._local(query, k, min_hierarchy_n)
+        gs = s.new_empty(self.world * k)
+        gi = i.new_empty(self.world * k)
+        self.dist.all_gather_into_tensor(gs, s.contiguous(), group=self.group)
+        self.dist.all_gather_into_tensor(gi, i.contiguous(), group=self.group)
+        return self._merge(gs, gi, k)
+
+
+def init_process_group(backend: str = "nccl", timeout_s: float = 120.0):
+    """One process per GPU (torchrun env vars); a short timeout turns a lost rank
+    into an error on the survivors' next collective instead of a hang."""
+    import os
+
+    import torch.distributed as dist
+
+    if backend == "nccl":
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s),
+                                device_id=torch.device("cuda", local))
+    else:
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
+    return dist.get_rank(), dist.get_world_size()

@@ -524,7 +524,7 @@ int circuit_search_async(circuit_index_t index, const float* dev_query, int k, i
                          float* dev_out_scores, int* dev_out_ids, int64_t* dev_out_rows, void* stream,
                          void* ev_scan_begin, void* ev_scan_end) {
   if (!index) return CIRCUIT_ERR_NULL;
-  cudaStream_t st = stream ? (cudaStream_t)stream : index->stream;
+  cudaStream_t st = (cudaStream_t)stream;  // NULL = the legacy default stream, as everywhere in CUDA
   index->have_host_ctrl = false;
   return index->search_async(dev_query, k, min_hierarchy_n, dev_out_scores, dev_out_ids, dev_out_rows, st,
                              (cudaEvent_t)ev_scan_begin, (cudaEvent_t)ev_scan_end);
@@ -535,7 +535,7 @@ int circuit_last_trace(circuit_index_t index, circuit_trace_ex_t* out) {
   if (!out) { set_error("null trace"); return CIRCUIT_ERR_ARG; }
   if (!cuda_ok(cudaSetDevice(index->device), "cudaSetDevice")) return CIRCUIT_ERR_CUDA;
   if (!index->have_host_ctrl) {
-    cudaStream_t st = index->last_stream ? index->last_stream : index->stream;
+    cudaStream_t st = index->last_stream;
     if (!cuda_ok(cudaMemcpyAsync(index->h_ctrl, index->ws.ctrl, cb::CTRL_RESET_BYTES, cudaMemcpyDeviceToHost, st),
                  "copy ctrl") ||
         !cuda_ok(cudaStreamSynchronize(st), "trace sync"))
@@ -554,7 +554,7 @@ int circuit_trace_snapshot_async(circuit_index_t index, void* dst, void* stream)
   if (!index) return CIRCUIT_ERR_NULL;
   if (!dst) { set_error("null snapshot buffer"); return CIRCUIT_ERR_ARG; }
   static_assert(cb::CTRL_RESET_BYTES == CIRCUIT_TRACE_SNAPSHOT_BYTES, "snapshot size");
-  cudaStream_t st = stream ? (cudaStream_t)stream : index->stream;
+  cudaStream_t st = (cudaStream_t)stream;
   if (!cuda_ok(cudaSetDevice(index->device), "cudaSetDevice") ||
       !cuda_ok(cudaMemcpyAsync(dst, index->ws.ctrl, cb::CTRL_RESET_BYTES, cudaMemcpyDefault, st),
                "trace snapshot"))

@@ -1,0 +1,93 @@
+// Cross-shard top-k merge (multi-GPU search): the k candidates of each of the
+// W shards, gathered on every rank by one NCCL all-gather, are reduced to the
+// global top-k on the device.  Ordering is (score desc, original id asc), the
+// same total order every shard used locally, so the merged result does not
+// depend on the number of shards.  Also the root-to-rank shard plan (host).
+#include <algorithm>
+#include <numeric>
+#include <string>
+#include <vector>
+
+#include "../../include/circuit_shard.h"
+#include "common.cuh"
+#include "engine.h"
+#include "index_internal.h"
+#include "topk.cuh"
+
+namespace cb {
+
+constexpr int MERGE_THREADS = 256;
+constexpr int MERGE_MAX_N = 16384;
+
+__global__ void __launch_bounds__(MERGE_THREADS) k_merge_topk(const float* __restrict__ scores,
+                                                                const int* __restrict__ ids, int n, int k,
+                                                                int selN, float* __restrict__ out_scores,
+                                                                int* __restrict__ out_ids) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem);
+  unsigned long long* sel = cand + n;
+  SelectScratch* scratch = reinterpret_cast<SelectScratch*>(sel + selN);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int id = ids[i];
+    cand[i] = id >= 0 ? pack_cand(f2key(scores[i]), (uint32_t)id) : 0ull;
+  }
+  __syncthreads();
+  block_select_topk<false>(cand, n, k, sel, selN, scratch);
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const unsigned long long c = sel[i];
+    out_scores[i] = c ? key2f(cand_key(c)) : -INFINITY;
+    out_ids[i] = c ? (int)cand_row(c) : -1;
+  }
+}
+
+}  // namespace cb
+
+extern "C" {
+
+int circuit_merge_topk(const float* scores, const int* ids, int n, int k, float* out_scores, int* out_ids,
+                       void* stream) {
+  if (!scores || !ids || !out_scores || !out_ids) {
+    cb::set_error("merge_topk: null pointer");
+    return CIRCUIT_ERR_ARG;
+  }
+  if (n < 1 || n > cb::MERGE_MAX_N || k < 1 || k > cb::KMAX) {
+    cb::set_error("merge_topk: need 1 <= n <= 16384 and 1 <= k <= 256");
+    return CIRCUIT_ERR_ARG;
+  }
+  int selN = 1;
+  while (selN < k) selN <<= 1;
+  const size_t smem = sizeof(unsigned long long) * (size_t)(n + selN) + sizeof(cb::SelectScratch) + 16;
+  static size_t configured = 0;
+  if (smem > 48 * 1024 && smem > configured) {
+    if (!cb::cuda_ok(cudaFuncSetAttribute(cb::k_merge_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                     "merge smem"))
+      return CIRCUIT_ERR_CUDA;
+    configured = smem;
+  }
+  cb::k_merge_topk<<<1, cb::MERGE_THREADS, smem, (cudaStream_t)stream>>>(scores, ids, n, k, selN, out_scores, out_ids);
+  return cb::cuda_ok(cudaGetLastError(), "merge_topk launch") ? CIRCUIT_OK : CIRCUIT_ERR_CUDA;
+}
+
+int circuit_plan_shards(const int64_t* root_rows, int num_roots, int world, int* root_to_rank, int64_t* rank_rows) {
+  if (!root_rows || !root_to_rank || num_roots < 1 || world < 1) {
+    cb::set_error("plan_shards: bad arguments");
+    return CIRCUIT_ERR_ARG;
+  }
+  // longest-processing-time first: heaviest root to the currently lightest rank
+  std::vector<int> order(num_roots);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return root_rows[a] > root_rows[b]; });
+  std::vector<int64_t> load(world, 0);
+  for (int r : order) {
+    int best = 0;
+    for (int w = 1; w < world; ++w)
+      if (load[w] < load[best]) best = w;
+    root_to_rank[r] = best;
+    load[best] += root_rows[r];
+  }
+  if (rank_rows)
+    for (int w = 0; w < world; ++w) rank_rows[w] = load[w];
+  return CIRCUIT_OK;
+}
+
+}  // extern "C"

@@ -123,7 +123,7 @@ circuit_index_t circuit_index_from_device(int device_id, int dim, int rank, int 
 int circuit_index_info(circuit_index_t index, int64_t* info);
 
 /* Asynchronous single-query search on `stream` (a cudaStream_t; NULL = the
- * handle's own stream).  Routes to the flat scan when N < min_hierarchy_n
+ * legacy default stream, as in the CUDA runtime).  Routes to the flat scan when N < min_hierarchy_n
  * (reference circuit_rag/search.py:55-57), else the hierarchical pipeline.
  * dev_out_rows (optional, int64 [k]) receives leaf-row positions.
  * ev_scan_begin / ev_scan_end (optional cudaEvent_t) are recorded on `stream`

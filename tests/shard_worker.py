@@ -1,0 +1,58 @@
+"""Worker processes for the multi-process (gloo, CPU) shard tests."""
+import json
+import os
+import sys
+
+
+def _paths(root):
+    for p in (os.path.join(root, "circuit-rag_b200"), root):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+
+
+def search_worker(rank, world, port, root, index_path, queries_path, out_path, k, fail_rank=-1):
+    _paths(root)
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from circuit_rag.shard import ShardedSearcher, load_shard, merge_topk_host
+    from oracle import oracle
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    import datetime
+
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=4))
+    result = {"rank": rank}
+    try:
+        idx = load_shard(index_path, rank, world, device="cpu")
+        X = idx.leaf_vectors.numpy()
+        gid = idx.original_ids.numpy()
+        if rank == fail_rank:
+            raise SystemExit(3)  # a rank that dies before its first collective
+
+        def local(q, kk, _mh):
+            s, rows = oracle.brute_topk(X, q.numpy(), min(kk, len(X)))
+            out_s = torch.full((kk,), float("-inf"))
+            out_i = torch.full((kk,), -1, dtype=torch.int32)
+            out_s[:len(s)] = torch.from_numpy(s).float()
+            out_i[:len(s)] = torch.from_numpy(gid[rows]).int()
+            return out_s, out_i
+
+        srch = ShardedSearcher(None, local_search=local, merge=merge_topk_host)
+        Q = np.load(queries_path)
+        res = []
+        for q in Q:
+            s, i = srch.search(torch.from_numpy(q), k=k)
+            res.append({"scores": s.tolist(), "ids": i.tolist()})
+        result.update(ok=True, results=res, shard_rows=int(len(X)), shard_ids=gid.tolist())
+    except SystemExit:
+        raise
+    except Exception as e:  # the survivor of a lost rank lands here
+        result.update(ok=False, error=f"{type(e).__name__}: {e}")
+    with open(out_path, "w") as f:
+        json.dump(result, f)
+    try:
+        dist.destroy_process_group()
+    except Exception:
+        pass

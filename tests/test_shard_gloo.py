@@ -1,0 +1,114 @@
+"""Multi-rank host logic of the sharded search on CPU (gloo, world size 2-3):
+root plan, partial shard loads, all-gather + merge exactness, and a lost rank."""
+import json
+import multiprocessing as mp
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from circuit_rag import build_circuit_index
+from circuit_rag.shard import load_shard, merge_topk_host, plan_shards
+from circuit_rag.synthetic import WORKLOADS
+from oracle import oracle
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.fixture(scope="module")
+def index_file(tmp_path_factory):
+    w = WORKLOADS["zipf-10m"]
+    X = w.corpus(0, 6000).numpy()
+    idx = build_circuit_index(X, num_roots=12, children_per_root=4, rank=6, device="cpu")
+    p = str(tmp_path_factory.mktemp("shard") / "z.circuit")
+    idx.save(p)
+    return p, X
+
+
+def test_plan_shards_is_balanced_lpt():
+    rows = np.array([100, 5, 60, 60, 30, 1, 0, 44])
+    plan = plan_shards(rows, 3)
+    loads = np.bincount(plan, weights=rows, minlength=3)
+    assert loads.sum() == rows.sum() and loads.max() - loads.min() <= rows.max()
+    assert plan[0] != plan[2] or plan[0] != plan[3]
+    assert (plan_shards(rows, 1) == 0).all()
+
+
+@pytest.mark.parametrize("world", [1, 2, 3])
+def test_shards_partition_the_index(index_file, world):
+    path, X = index_file
+    seen = []
+    for r in range(world):
+        sh = load_shard(path, r, world, device="cpu")
+        ids = sh.original_ids.numpy()
+        assert np.array_equal(sh.leaf_vectors.numpy(), X[ids])
+        seen.append(ids)
+        # every non-empty child lies inside its parent's rows and the parent ids are local
+        sizes, offs, par = sh.leaf_sizes.numpy(), sh.leaf_offsets.numpy(), sh.child_parent_ids.numpy()
+        assert par.max() < sh.num_roots and (offs + sizes).max() <= sh.N
+    allids = np.concatenate(seen)
+    assert len(allids) == len(X) and len(np.unique(allids)) == len(X)
+
+
+def test_merge_host_matches_brute_force():
+    import torch
+
+    rng = np.random.default_rng(3)
+    exact = rng.normal(size=500)
+    parts = np.array_split(np.arange(500), 4)
+    S, I = [], []
+    for p in parts:
+        top = p[np.argsort(-exact[p])[:10]]
+        S.append(exact[top])
+        I.append(top)
+    s, i = merge_topk_host(torch.tensor(np.concatenate(S)), torch.tensor(np.concatenate(I), dtype=torch.int32), 10)
+    oracle.check_topk(exact, 10, s.numpy(), i.numpy(), score_rel=1e-6)
+
+
+def _run(world, index_path, tmp_path, k=10, fail_rank=-1, nq=5):
+    Q = WORKLOADS["zipf-10m"].query_batch(nq).numpy()
+    qp = str(tmp_path / "q.npy")
+    np.save(qp, Q)
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    from shard_worker import search_worker
+
+    outs = [str(tmp_path / f"out{r}.json") for r in range(world)]
+    procs = [ctx.Process(target=search_worker, args=(r, world, port, ROOT, index_path, qp, outs[r], k, fail_rank))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("worker did not finish")
+    res = [json.load(open(o)) if os.path.exists(o) else None for o in outs]
+    return Q, procs, res
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_search_is_exact(index_file, tmp_path, world):
+    path, X = index_file
+    Q, procs, res = _run(world, path, tmp_path)
+    assert all(p.exitcode == 0 for p in procs)
+    assert all(r["ok"] for r in res)
+    for qi, q in enumerate(Q):
+        exact = oracle.exact_scores(X, q)
+        for r in res:  # every rank returns the same global answer
+            oracle.check_topk(exact, 10, r["results"][qi]["scores"], r["results"][qi]["ids"])
+        assert res[0]["results"][qi]["ids"] == res[-1]["results"][qi]["ids"]
+
+
+def test_lost_rank_becomes_an_error_not_a_hang(index_file, tmp_path):
+    path, _ = index_file
+    _, procs, res = _run(2, path, tmp_path, fail_rank=1, nq=1)
+    assert procs[1].exitcode == 3
+    assert res[0] is not None and not res[0]["ok"], res[0]
