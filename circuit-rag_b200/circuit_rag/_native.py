@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "circuit_op_hierarchical_search",
     "circuit_merge_topk",
     "circuit_plan_shards",
+    "circuit_flat_search_noalloc",
 )
 
 
@@ -98,6 +99,7 @@ def _declare(lib):
         "circuit_op_hierarchical_search": (_I, [_P] * 21 + [_I, _I, _I64, _I, _F, _I, _F, _P]),
         "circuit_merge_topk": (_I, [_P, _P, _I, _I, _P, _P, _P]),
         "circuit_plan_shards": (_I, [_P, _I, _I, _P, _P]),
+        "circuit_flat_search_noalloc": (_I, [_P, _I64, _I, _P, _I, _P, _P, _P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -85,6 +85,14 @@ cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float*
                           float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
                           cudaEvent_t ev_scan0, cudaEvent_t ev_scan1);
 
+// Flat exact top-k of leaf[0..N) . q with caller-provided scratch: ctrl (its
+// first CTRL_RESET_BYTES zeroed by the caller), range = {0, 0, N, -1},
+// packed = 1 << 32 | N, cta_lists >= (grid + 1) * k entries.  Output ids are
+// row numbers.
+cudaError_t launch_flat_scan(const float* leaf, int D, int N, const float* q, int k, int grid, SearchCtrl* ctrl,
+                             const int4* range, const unsigned long long* packed, unsigned long long* cta_lists,
+                             float* out_scores, int* out_ids, cudaStream_t stream);
+
 int scan_smem_bytes(int D);
 int sm_count(int device);
 

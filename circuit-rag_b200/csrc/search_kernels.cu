@@ -827,4 +827,33 @@ cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float*
   return e;
 }
 
+cudaError_t launch_flat_scan(const float* leaf, int D, int N, const float* q, int k, int grid, SearchCtrl* ctrl,
+                             const int4* range, const unsigned long long* packed, unsigned long long* cta_lists,
+                             float* out_scores, int* out_ids, cudaStream_t stream) {
+  const int vpl = vpl_bucket(D / 4);
+  ScanParams F{};
+  F.leaf = leaf;
+  F.q = q;
+  F.ranges = range;
+  F.packed_counts = packed;
+  F.theta_key = &ctrl->theta_key;
+  F.cta_lists = cta_lists;
+  F.done = &ctrl->main_done;
+  F.err = &ctrl->error;
+  F.D4 = D / 4;
+  F.row_bytes = D * 4;
+  F.k = k;
+  F.stages = stages_for(vpl, F.row_bytes);
+  F.final_mode = 1;
+  F.merge_seed = 0;
+  F.seed_list = ctrl->seed_list;
+  F.seed_T_key = &ctrl->seed_T_key;
+  F.out_scores = out_scores;
+  F.out_ids = out_ids;
+  F.out_rows = nullptr;
+  F.original_ids = nullptr;
+  (void)N;
+  return launch_scan(F, grid, stream);
+}
+
 }  // namespace cb

@@ -145,6 +145,23 @@ int circuit_last_trace(circuit_index_t index, circuit_trace_ex_t* out);
 int circuit_trace_snapshot_async(circuit_index_t index, void* dst, void* stream);
 int circuit_trace_decode(circuit_index_t index, const void* snapshot, int path, circuit_trace_ex_t* out);
 
+/* Exact top-k of corpus[n, dim] . query that allocates no device memory (no
+ * counterpart in the reference).  For callers that cannot call cudaMalloc: an
+ * engine plugin whose host framework owns all device memory, a serving loop
+ * that must not touch the allocator after start-up.  The caller passes the
+ * device corpus (row-major float32, 16-byte aligned, dim % 4 == 0), the query
+ * and the outputs (scores[k] descending, ids[k] = row numbers); the scan's
+ * scratch is a fixed 256 KiB array inside the library's device image, held by
+ * every GPU that loads the library until the process exits.  Limits: k <= 128,
+ * n < 2^31, dim <= 2048 (larger values return CIRCUIT_ERR_ARG /
+ * CIRCUIT_ERR_UNSUPPORTED with a message).  The first call on a device looks up
+ * that array's device address with the device current; make that first call
+ * before any stream capture.  All calls share the array: calls that overlap on
+ * the GPU race and must be serialised by the caller.  Asynchronous on `stream`
+ * (NULL = legacy default stream). */
+int circuit_flat_search_noalloc(const float* dev_corpus, int64_t n, int dim, const float* dev_query, int k,
+                                float* dev_out_scores, int* dev_out_ids, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
