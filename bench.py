@@ -281,8 +281,8 @@ def main():
         for j in range(min(3, steps)):
             q = Q[warm + j].double()
             ex = torch.empty(n_local, dtype=torch.float64, device=dev)
-            for a in range(0, n_local, 1 << 22):
-                ex[a:a + (1 << 22)] = leaf[a:a + (1 << 22)].double() @ q
+            for a in range(0, n_local, 1 << 20):
+                ex[a:a + (1 << 20)] = leaf[a:a + (1 << 20)].double() @ q
             exact = torch.empty_like(ex)
             exact[idx.original_ids.long() - start] = ex
             try:

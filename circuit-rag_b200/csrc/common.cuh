@@ -113,6 +113,11 @@ __device__ __forceinline__ void tma_load_1d_stream(void* dst_smem, const void* s
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// Bulk prefetch of [src, src + bytes) into L2 (no shared memory, no completion
+// to wait for): keeps DRAM busy ahead of the shared-memory ring.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

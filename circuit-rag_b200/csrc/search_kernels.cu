@@ -84,9 +84,9 @@ __host__ __device__ inline ScanLayout scan_layout(int rows_per_stage, int row_by
   L.stage_bytes = align_up((size_t)rows_per_stage * row_bytes, 128);
   L.stages_off = 0;
   L.bars_off = align_up(L.stages_off + stages * L.stage_bytes, 128);
-  L.rows_off = L.bars_off + 2 * MAX_STAGES * sizeof(uint64_t);
-  L.n_off = L.rows_off + (size_t)MAX_STAGES * 32 * sizeof(int);
-  L.topk_off = align_up(L.n_off + MAX_STAGES * sizeof(int), 128);
+  L.rows_off = L.bars_off + 2 * MAX_STAGES * sizeof(uint64_t);           // runs: [stage][32] int2
+  L.n_off = L.rows_off + (size_t)MAX_STAGES * 32 * sizeof(int2);          // rows, runs per stage
+  L.topk_off = align_up(L.n_off + 2 * MAX_STAGES * sizeof(int), 128);
   L.sel_off = L.topk_off + (size_t)SCAN_CONSUMER_WARPS * sortn * 8;
   L.scratch_off = align_up(L.sel_off + (size_t)kcap * 8, 128);
   L.total = align_up(L.scratch_off + sizeof(SelectScratch) + 16, 128);
@@ -102,8 +102,12 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
   const ScanLayout L = scan_layout(ROWS, P.row_bytes, P.stages, SORTN, KCAP);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars_off);
   uint64_t* empty = full + MAX_STAGES;
-  int* stage_rows = reinterpret_cast<int*>(smem + L.rows_off);
+  // A stage holds up to ROWS rows made of runs of consecutive leaf rows:
+  // stage_runs[stage][i] = {first slot, first row}, stage_n[stage] = rows
+  // (-1 = end of stream), stage_nr[stage] = runs.
+  int2* stage_runs = reinterpret_cast<int2*>(smem + L.rows_off);
   int* stage_n = reinterpret_cast<int*>(smem + L.n_off);
+  int* stage_nr = stage_n + MAX_STAGES;
   unsigned long long* topk_all = reinterpret_cast<unsigned long long*>(smem + L.topk_off);
   unsigned long long* sel = reinterpret_cast<unsigned long long*>(smem + L.sel_off);
   SelectScratch* scratch = reinterpret_cast<SelectScratch*>(smem + L.scratch_off);
@@ -146,35 +150,40 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       int it = 0;
       bool ok = true;
       const char* leaf_bytes = reinterpret_cast<const char*>(P.leaf);
+      // the next range entry is loaded one transition ahead, so walking from
+      // one child's rows to the next never waits on L2
+      int4 rg_next = (s + 1 < (int)n_ranges && vb < ve) ? __ldcg(&P.ranges[s + 1]) : make_int4(0, 0, 0, 0);
       while (v < ve) {
         const int stage = it % STAGES, f = it / STAGES;
         if (f > 0 && !mbar_wait(&empty[stage], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) { ok = false; break; }
-        int* srows = stage_rows + stage * 32;
-        int n = 0;
+        int2* runs = stage_runs + stage * 32;
+        int n = 0, nr = 0;
+        uint32_t run_end = 0xffffffffu;  // leaf row just past the open run
         while (n < ROWS && v < ve) {
           const uint32_t rlen = (uint32_t)(rg.z - rg.y);
           if (v >= (uint32_t)rg.x + rlen) {
             ++s;
             if (s >= (int)n_ranges) { atomicOr(P.err, ERR_BAD_RANGE); v = ve; break; }
-            rg = __ldcg(&P.ranges[s]);
+            rg = rg_next;
+            if (s + 1 < (int)n_ranges) rg_next = __ldcg(&P.ranges[s + 1]);
             continue;
           }
           const uint32_t row = (uint32_t)rg.y + (v - (uint32_t)rg.x);
           const uint32_t take = min(min((uint32_t)(ROWS - n), ve - v), (uint32_t)rg.z - row);
-          for (uint32_t i = 0; i < take; ++i) srows[n + i] = (int)(row + i);
+          if (row != run_end) runs[nr++] = make_int2(n, (int)row);  // adjacent children extend the open run
+          run_end = row + take;
           n += (int)take;
           v += take;
         }
         stage_n[stage] = n;
+        stage_nr[stage] = nr;
         mbar_arrive_expect_tx(&full[stage], (uint32_t)n * (uint32_t)P.row_bytes);
         unsigned char* dst = smem + L.stages_off + (size_t)stage * L.stage_bytes;
-        int i = 0;
-        while (i < n) {
-          int j = i + 1;
-          while (j < n && srows[j] == srows[j - 1] + 1) ++j;
-          tma_load_1d_stream(dst + (size_t)i * P.row_bytes, leaf_bytes + (size_t)srows[i] * P.row_bytes,
-                             (uint32_t)(j - i) * (uint32_t)P.row_bytes, &full[stage], policy);
-          i = j;
+        for (int i = 0; i < nr; ++i) {
+          const int2 r0 = runs[i];
+          const int slot_end = (i + 1 < nr) ? runs[i + 1].x : n;
+          tma_load_1d_stream(dst + (size_t)r0.x * P.row_bytes, leaf_bytes + (size_t)r0.y * P.row_bytes,
+                             (uint32_t)(slot_end - r0.x) * (uint32_t)P.row_bytes, &full[stage], policy);
         }
         ++it;
       }
@@ -195,6 +204,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     unsigned long long* tk = topk_all + warp * SORTN;
     uint32_t theta_w = 0;                                 // this warp's k-th best key
     uint32_t theta = ld_volatile_u32(P.theta_key);        // filter key (max of both)
+    uint32_t g_pending = theta;                           // global key loaded one stage ahead
     int cnt = 0;                                          // buffered candidates
     uint32_t published = 0;
 
@@ -222,10 +232,10 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       const int n = stage_n[stage];
       if (n < 0) break;
       {
-        uint32_t g = 0;
-        if (lane == 0) g = ld_volatile_u32(P.theta_key);
-        g = __shfl_sync(FULL_MASK, g, 0);
-        theta = max(theta, g);
+        // use the global threshold read during the previous stage and issue the
+        // next read now: its L2 round trip overlaps this stage and the next wait
+        theta = max(theta, __shfl_sync(FULL_MASK, g_pending, 0));
+        if (lane == 0) g_pending = ld_volatile_u32(P.theta_key);
       }
       const float4* stage_f4 =
           reinterpret_cast<const float4*>(smem + L.stages_off + (size_t)stage * L.stage_bytes);
@@ -285,7 +295,12 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       const uint32_t key = f2key(score);
       const bool cand = owner && slot < n && key >= theta;
       int row = 0;
-      if (cand) row = stage_rows[stage * 32 + slot];
+      if (cand) {  // rare: map the slot back to its leaf row through the stage's runs
+        const int2* runs = stage_runs + stage * 32;
+        int i = stage_nr[stage] - 1;
+        while (i > 0 && runs[i].x > slot) --i;
+        row = runs[i].y + (slot - runs[i].x);
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[stage]);
       const uint32_t bal = __ballot_sync(FULL_MASK, cand);
@@ -317,14 +332,25 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
   __threadfence();
 
   // ---------------------------------------------------------- grid merge (last CTA)
-  int M = gridDim.x * k;
-  if (P.final_mode && P.merge_seed) {
-    for (int i = tid; i < k; i += blockDim.x) P.cta_lists[(size_t)gridDim.x * k + i] = P.seed_list[i];
-    M += k;
-    __threadfence_block();
+  // The ring is idle now: stage the gathered lists in its shared memory when
+  // they fit, so the radix passes run on shared memory instead of L2.
+  const int M = gridDim.x * k + ((P.final_mode && P.merge_seed) ? k : 0);
+  int cnt_sel;
+  if ((size_t)M * 8 <= (size_t)STAGES * L.stage_bytes) {
+    unsigned long long* buf = reinterpret_cast<unsigned long long*>(smem + L.stages_off);
+    const int mg = gridDim.x * k;
+    for (int i = tid; i < mg; i += blockDim.x) buf[i] = __ldcg(P.cta_lists + i);
+    for (int i = mg + tid; i < M; i += blockDim.x) buf[i] = P.seed_list[i - mg];
     __syncthreads();
+    cnt_sel = block_select_topk<false>(buf, M, k, sel, selN, scratch);
+  } else {
+    if (P.final_mode && P.merge_seed) {
+      for (int i = tid; i < k; i += blockDim.x) P.cta_lists[(size_t)gridDim.x * k + i] = P.seed_list[i];
+      __threadfence_block();
+      __syncthreads();
+    }
+    cnt_sel = block_select_topk<true>(P.cta_lists, M, k, sel, selN, scratch);
   }
-  const int cnt_sel = block_select_topk<true>(P.cta_lists, M, k, sel, selN, scratch);
   if (!P.final_mode) {
     for (int i = tid; i < k; i += blockDim.x) P.seed_list[i] = sel[i];
     if (tid == 0) {
@@ -708,7 +734,14 @@ int scan_smem_bytes(int D) {
 }
 
 template <int VPL, int KCAP>
-static cudaError_t launch_scan_t(const ScanParams& P, int grid, cudaStream_t stream) {
+static cudaError_t launch_scan_t(const ScanParams& P0, int grid, cudaStream_t stream) {
+  // as many ring stages as the shared-memory budget leaves after the top-k areas
+  constexpr size_t SMEM_BUDGET = 225 * 1024;
+  ScanParams P = P0;
+  const size_t fixed = scan_layout(ScanShape<VPL>::ROWS, P.row_bytes, 0, TopkShape<KCAP>::SORTN, KCAP).total;
+  const size_t sb = align_up((size_t)ScanShape<VPL>::ROWS * P.row_bytes, 128);
+  int st = (int)((SMEM_BUDGET - fixed) / sb);
+  P.stages = st < 2 ? 2 : (st > MAX_STAGES ? MAX_STAGES : st);
   const ScanLayout L = scan_layout(ScanShape<VPL>::ROWS, P.row_bytes, P.stages, TopkShape<KCAP>::SORTN, KCAP);
   static int configured_bytes = 0;  // per instantiation; the attribute is process-wide
   if ((int)L.total > configured_bytes) {
