@@ -12,6 +12,8 @@ LIB_PATH = os.path.join(_HERE, "libcircuit.so")
 
 CIRCUIT_OK = 0
 CIRCUIT_MAX_K = 256
+CIRCUIT_BATCH_MAX_K = 32
+CIRCUIT_BATCH_MAX_DIM = 384
 CIRCUIT_MAX_RANK = 64
 CIRCUIT_MAX_DIM = 2048
 TRACE_SNAPSHOT_BYTES = 96
@@ -39,6 +41,9 @@ EXPORTED_SYMBOLS = (
     "circuit_merge_topk",
     "circuit_plan_shards",
     "circuit_flat_search_noalloc",
+    "circuit_search_batch_async",
+    "circuit_batch_overflow",
+    "circuit_search_batch",
 )
 
 
@@ -100,6 +105,9 @@ def _declare(lib):
         "circuit_merge_topk": (_I, [_P, _P, _I, _I, _P, _P, _P]),
         "circuit_plan_shards": (_I, [_P, _I, _I, _P, _P]),
         "circuit_flat_search_noalloc": (_I, [_P, _I64, _I, _P, _I, _P, _P, _P]),
+        "circuit_search_batch_async": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+        "circuit_batch_overflow": (_I, [_P, _P]),
+        "circuit_search_batch": (_I, [_P, _P, _I, _I, _P, _P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -124,3 +124,47 @@ def circuit_search(query: torch.Tensor, index: CircuitIndex, k: int = 10,
         ev2.record(stream)
         trace._pending = (index, snap, 1 if hier else 0, ev0, ev1, ev2)
     return scores, ids, trace
+
+
+def circuit_search_batch(queries: torch.Tensor, index: CircuitIndex, k: int = 10) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Exact top-k for a batch of queries [B, dim] on the tensor cores.
+
+    No reference counterpart (the reference answers one query per call); the
+    results equal B calls of circuit_search: a tf32 tcgen05 pass over every
+    leaf row keeps each query's rows within a rigorous error band of its running
+    k-th best, and those rows are rescored exactly in fp32.  Returns (scores
+    [B, k] float32 descending, original ids [B, k] int32).  Needs dim <= 384,
+    dim % 4 == 0 and 1 <= k <= 32.  A query whose candidate list overflows
+    (more than 8192 rows inside the band, e.g. thousands of near-identical
+    rows) is answered by circuit_search."""
+    if queries.ndim != 2 or queries.shape[1] != index.dim:
+        raise ValueError("queries must have shape [B, index.dim]")
+    if not index.is_cuda:
+        raise RuntimeError("circuit-b200 searches run on a CUDA device (no CPU path); load or build the index "
+                           "with device='cuda'")
+    k = min(int(k), index.N)
+    if k < 1 or k > _native.CIRCUIT_BATCH_MAX_K:
+        raise ValueError(f"batched k must be in [1, {_native.CIRCUIT_BATCH_MAX_K}]")
+    B = queries.shape[0]
+    dev = index.leaf_vectors.device
+    queries = queries.to(device=dev, dtype=torch.float32).contiguous()
+    if queries.data_ptr() % 16:
+        queries = queries.clone()
+    handle = index.native_handle()
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream()
+        scores = torch.empty(B, k, dtype=torch.float32, device=dev)
+        ids = torch.empty(B, k, dtype=torch.int32, device=dev)
+        if B == 0:
+            return scores, ids
+        rc = _native.lib().circuit_search_batch_async(handle, queries.data_ptr(), B, k, scores.data_ptr(),
+                                                      ids.data_ptr(), stream.cuda_stream)
+        _native.check(rc, "circuit_search_batch")
+        n_over = ctypes.c_int(0)
+        _native.check(_native.lib().circuit_batch_overflow(handle, ctypes.byref(n_over)), "circuit_batch_overflow")
+        if n_over.value:
+            for q in torch.nonzero(ids[:, 0] == -2).flatten().tolist():
+                s1, i1, _ = circuit_search(queries[q], index, k)
+                scores[q] = s1
+                ids[q] = i1
+    return scores, ids

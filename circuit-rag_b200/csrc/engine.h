@@ -93,6 +93,33 @@ cudaError_t launch_flat_scan(const float* leaf, int D, int N, const float* q, in
                              const int4* range, const unsigned long long* packed, unsigned long long* cta_lists,
                              float* out_scores, int* out_ids, cudaStream_t stream);
 
+// ---- batched search (batch_kernels.cu) ----
+constexpr int BATCH_MAX_DIM = 384;   // 128 query rows of D fp32 columns + 2 x 64 accumulator columns in TMEM
+constexpr int BATCH_MAX_K = 32;
+constexpr int BATCH_CAND_CAP = 16384;  // candidate rows appended per query
+
+struct BatchWorkspace {
+  uint32_t* theta = nullptr;      // [capacity] running k-th best keys
+  int* cand_count = nullptr;      // [capacity]
+  unsigned long long* cand = nullptr;  // [capacity * cap] tf32 key << 32 | row
+  int* overflow = nullptr;        // queries whose candidate list overflowed
+  int* err = nullptr;
+  float* queries = nullptr;       // [capacity * D] staging for host queries
+  float* out_scores = nullptr;    // [capacity * BATCH_MAX_K]
+  int* out_ids = nullptr;
+  int cap = BATCH_CAND_CAP;
+  int capacity = 0;
+  float xmax = 0.f;               // upper bound of max ||x|| over the leaf rows
+  int sms = 0;
+  alignas(64) unsigned char tmap[128];  // CUtensorMap of leaf_vectors, boxes of 64 rows x 32 columns
+};
+
+bool make_leaf_tensor_map(const float* leaf, int N, int D, void* out_map);
+cudaError_t launch_max_row_norm(const float* leaf, int N, int D, unsigned int* out_key, int sms, cudaStream_t st);
+// queries [B, D] (device) -> out_scores / out_ids [B, k], original ids, (score desc, row asc).
+cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, const float* Q, int B, int k,
+                                float* out_scores, int* out_ids, cudaStream_t st);
+
 int scan_smem_bytes(int D);
 int sm_count(int device);
 

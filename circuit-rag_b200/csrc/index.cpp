@@ -70,6 +70,8 @@ void circuit_index_opaque::release() {
   if (stream) cudaStreamSynchronize(stream);
   for (void* p : owned) cudaFree(p);
   owned.clear();
+  for (void* p : batch_owned) cudaFree(p);
+  batch_owned.clear();
   if (h_pinned) cudaFreeHost(h_pinned);
   h_pinned = nullptr;
   if (stream) cudaStreamDestroy(stream);
@@ -464,8 +466,139 @@ int circuit_index_opaque::search_blocking(const float* query, bool host_ptrs, in
   return CIRCUIT_OK;
 }
 
+// ---------------------------------------------------------------- batched search
+int circuit_index_opaque::ensure_batch(int B) {
+  if (!batch_ready) {
+    if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice")) return CIRCUIT_ERR_CUDA;
+    bw.sms = cb::sm_count(device);
+    unsigned int* d_key = nullptr;
+    if (!cuda_ok(cudaMalloc(&d_key, sizeof(unsigned int)), "cudaMalloc(xmax)")) return CIRCUIT_ERR_CUDA;
+    owned.push_back(d_key);
+    int* d_err = nullptr;
+    if (!cuda_ok(cudaMalloc(&d_err, sizeof(int)), "cudaMalloc(batch err)")) return CIRCUIT_ERR_CUDA;
+    owned.push_back(d_err);
+    unsigned int key = 0;
+    if (!cuda_ok(cb::launch_max_row_norm(view.leaf, N, D, d_key, bw.sms, stream), "max row norm") ||
+        !cuda_ok(cudaMemcpyAsync(&key, d_key, sizeof(key), cudaMemcpyDeviceToHost, stream), "D2H xmax") ||
+        !cuda_ok(cudaMemsetAsync(d_err, 0, sizeof(int), stream), "memset err") ||
+        !cuda_ok(cudaStreamSynchronize(stream), "xmax sync"))
+      return CIRCUIT_ERR_CUDA;
+    float mx2;
+    std::memcpy(&mx2, &key, 4);
+    bw.xmax = std::sqrt(mx2) * 1.0001f + 1e-30f;
+    bw.err = d_err;
+    if (!cb::make_leaf_tensor_map(view.leaf, N, D, bw.tmap)) {
+      set_error("cuTensorMapEncodeTiled failed for leaf_vectors");
+      return CIRCUIT_ERR_CUDA;
+    }
+    batch_ready = true;
+  }
+  if (B > bw.capacity) {
+    if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice")) return CIRCUIT_ERR_CUDA;
+    cudaDeviceSynchronize();
+    for (void* p : batch_owned) cudaFree(p);
+    batch_owned.clear();
+    const int cap_B = ((B + 1023) / 1024) * 1024;
+    auto grab = [&](size_t bytes, const char* what) -> void* {
+      void* p = nullptr;
+      if (!cuda_ok(cudaMalloc(&p, bytes), what)) return nullptr;
+      batch_owned.push_back(p);
+      return p;
+    };
+    bw.theta = (uint32_t*)grab(sizeof(uint32_t) * cap_B, "cudaMalloc(theta)");
+    bw.cand_count = (int*)grab(sizeof(int) * cap_B, "cudaMalloc(cand_count)");
+    bw.cand = (unsigned long long*)grab(sizeof(unsigned long long) * (size_t)cap_B * bw.cap, "cudaMalloc(cand)");
+    bw.overflow = (int*)grab(sizeof(int), "cudaMalloc(overflow)");
+    bw.queries = (float*)grab(sizeof(float) * (size_t)cap_B * D, "cudaMalloc(batch queries)");
+    bw.out_scores = (float*)grab(sizeof(float) * (size_t)cap_B * cb::BATCH_MAX_K, "cudaMalloc(batch scores)");
+    bw.out_ids = (int*)grab(sizeof(int) * (size_t)cap_B * cb::BATCH_MAX_K, "cudaMalloc(batch ids)");
+    if (!bw.theta || !bw.cand_count || !bw.cand || !bw.overflow || !bw.queries || !bw.out_scores ||
+        !bw.out_ids) {
+      bw.capacity = 0;
+      return CIRCUIT_ERR_CUDA;
+    }
+    bw.capacity = cap_B;
+  }
+  return CIRCUIT_OK;
+}
+
+int circuit_index_opaque::search_batch_async(const float* dq, int B, int k, float* dscores, int* dids,
+                                             cudaStream_t st) {
+  if (B < 1) { set_error("num_queries must be >= 1"); return CIRCUIT_ERR_ARG; }
+  if (k < 1 || k > cb::BATCH_MAX_K) {
+    set_error("batched search supports 1 <= k <= " + std::to_string(cb::BATCH_MAX_K));
+    return CIRCUIT_ERR_UNSUPPORTED;
+  }
+  if (D > cb::BATCH_MAX_DIM || D % 4 != 0) {
+    set_error("batched search supports dim <= " + std::to_string(cb::BATCH_MAX_DIM) + " with dim % 4 == 0");
+    return CIRCUIT_ERR_UNSUPPORTED;
+  }
+  if (!dq || !dscores || !dids || ((uintptr_t)dq & 15)) {
+    set_error("null or misaligned batch pointer");
+    return CIRCUIT_ERR_ARG;
+  }
+  int rc = ensure_batch(B);
+  if (rc != CIRCUIT_OK) return rc;
+  if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice")) return CIRCUIT_ERR_CUDA;
+  cudaError_t e = cb::launch_batch_search(view, bw, dq, B, k, dscores, dids, st);
+  last_stream = st;
+  if (e != cudaSuccess) { set_error(std::string("batch launch: ") + cudaGetErrorString(e)); return CIRCUIT_ERR_CUDA; }
+  return CIRCUIT_OK;
+}
+
 // ---------------------------------------------------------------- C ABI
 extern "C" {
+
+int circuit_search_batch_async(circuit_index_t index, const float* dev_queries, int num_queries, int k,
+                               float* dev_out_scores, int* dev_out_ids, void* stream) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  return index->search_batch_async(dev_queries, num_queries, k, dev_out_scores, dev_out_ids, (cudaStream_t)stream);
+}
+
+int circuit_batch_overflow(circuit_index_t index, int* out_count) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  if (!out_count) { set_error("null out_count"); return CIRCUIT_ERR_ARG; }
+  *out_count = 0;
+  if (!index->batch_ready || !index->bw.overflow) return CIRCUIT_OK;
+  if (!cuda_ok(cudaSetDevice(index->device), "cudaSetDevice") ||
+      !cuda_ok(cudaMemcpyAsync(out_count, index->bw.overflow, sizeof(int), cudaMemcpyDeviceToHost, index->last_stream),
+               "D2H overflow") ||
+      !cuda_ok(cudaStreamSynchronize(index->last_stream), "overflow sync"))
+    return CIRCUIT_ERR_CUDA;
+  return CIRCUIT_OK;
+}
+
+int circuit_search_batch(circuit_index_t index, const float* host_queries, int num_queries, int k,
+                         float* host_scores, int* host_ids) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  if (!host_queries || !host_scores || !host_ids || num_queries < 1) {
+    set_error("null batch pointer or num_queries < 1");
+    return CIRCUIT_ERR_ARG;
+  }
+  int rc = index->ensure_batch(num_queries);
+  if (rc != CIRCUIT_OK) return rc;
+  const size_t qbytes = sizeof(float) * (size_t)num_queries * index->D;
+  cudaStream_t st = index->stream;
+  if (!cuda_ok(cudaMemcpyAsync(index->bw.queries, host_queries, qbytes, cudaMemcpyHostToDevice, st), "H2D queries"))
+    return CIRCUIT_ERR_CUDA;
+  rc = index->search_batch_async(index->bw.queries, num_queries, k, index->bw.out_scores, index->bw.out_ids, st);
+  if (rc != CIRCUIT_OK) return rc;
+  const size_t ob = (size_t)num_queries * k;
+  if (!cuda_ok(cudaMemcpyAsync(host_scores, index->bw.out_scores, sizeof(float) * ob, cudaMemcpyDeviceToHost, st),
+               "D2H scores") ||
+      !cuda_ok(cudaMemcpyAsync(host_ids, index->bw.out_ids, sizeof(int) * ob, cudaMemcpyDeviceToHost, st), "D2H ids") ||
+      !cuda_ok(cudaStreamSynchronize(st), "batch sync"))
+    return CIRCUIT_ERR_CUDA;
+  // a query whose candidate list overflowed is answered by the single-query search
+  for (int q = 0; q < num_queries; ++q) {
+    if (host_ids[(size_t)q * k] != -2) continue;
+    rc = index->search_blocking(host_queries + (size_t)q * index->D, true, k, host_scores + (size_t)q * k,
+                                host_ids + (size_t)q * k, nullptr);
+    if (rc != CIRCUIT_OK) return rc;
+  }
+  return CIRCUIT_OK;
+}
+
 
 const char* circuit_last_error(void) { return cb::get_error(); }
 int circuit_abi_version(void) { return CIRCUIT_ABI_VERSION; }

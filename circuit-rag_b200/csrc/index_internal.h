@@ -41,6 +41,10 @@ struct circuit_index_opaque {
   int last_path = 0;
   int last_k = 0;
 
+  cb::BatchWorkspace bw{};
+  bool batch_ready = false;
+  std::vector<void*> batch_owned;  // batch buffers, regrown with the batch size
+
   std::vector<void*> owned;  // device allocations released by release()
   int fd = -1;
   void* map_ptr = nullptr;
@@ -59,5 +63,7 @@ struct circuit_index_opaque {
   int search_blocking(const float* query, bool host_ptrs, int k, float* out_scores, int* out_ids,
                       circuit_trace_t* trace);
   void fill_trace(const cb::SearchCtrl& c, circuit_trace_ex_t* t) const;
+  int ensure_batch(int B);
+  int search_batch_async(const float* dq, int B, int k, float* dscores, int* dids, cudaStream_t st);
   static float key_to_float(uint32_t k);
 };

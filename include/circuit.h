@@ -145,6 +145,28 @@ int circuit_last_trace(circuit_index_t index, circuit_trace_ex_t* out);
 int circuit_trace_snapshot_async(circuit_index_t index, void* dst, void* stream);
 int circuit_trace_decode(circuit_index_t index, const void* snapshot, int path, circuit_trace_ex_t* out);
 
+/* Batched exact top-k on the tensor cores (no reference counterpart: the
+ * reference searches one query at a time).  dev_queries [num_queries, dim]
+ * (device, 16-byte aligned) -> dev_out_scores / dev_out_ids [num_queries, k]
+ * (original ids, scores descending).  One tf32 tcgen05 pass over all leaf rows
+ * selects candidates within a rigorous error band of each query's running
+ * k-th best; the candidates are rescored exactly in fp32, so results equal
+ * the single-query search's.  Limits: dim <= 384 with dim % 4 == 0, 1 <= k <= 32
+ * (CIRCUIT_ERR_UNSUPPORTED otherwise).  A query with more than 16384 rows
+ * appended, or more than 8192 rows inside the band of its final threshold
+ * (thousands of near-identical rows), gets id -2 in its first slot;
+ * circuit_batch_overflow counts them and circuit_search_batch answers them
+ * with the single-query search.
+ * Asynchronous on `stream`; the first call per handle allocates its batch
+ * workspace and synchronises once. */
+int circuit_search_batch_async(circuit_index_t index, const float* dev_queries, int num_queries, int k,
+                               float* dev_out_scores, int* dev_out_ids, void* stream);
+/* Queries of the last batch whose candidate list overflowed (synchronises its stream). */
+int circuit_batch_overflow(circuit_index_t index, int* out_count);
+/* Blocking host-buffer variant of circuit_search_batch_async (host_scores / host_ids [num_queries, k]). */
+int circuit_search_batch(circuit_index_t index, const float* host_queries, int num_queries, int k, float* host_scores,
+                         int* host_ids);
+
 /* Exact top-k of corpus[n, dim] . query that allocates no device memory (no
  * counterpart in the reference).  For callers that cannot call cudaMalloc: an
  * engine plugin whose host framework owns all device memory, a serving loop

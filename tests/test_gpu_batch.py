@@ -1,0 +1,145 @@
+"""GPU parity of the batched tensor-core search (circuit_search_batch and the
+C ABI circuit_search_batch_async / circuit_search_batch).
+
+Each query of a batch must return exactly what circuit_search returns for it
+(bit-identical fp32 scores: the exact rescoring uses the single-query scan's
+arithmetic) and must pass the oracle's top-k rule against float64 brute force
+(ids identical except among scores tied within 1e-6; scores within 1e-5
+relative)."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from circuit_rag import build_circuit_index, circuit_search, circuit_search_batch
+from circuit_rag import _native
+from circuit_rag.synthetic import WORKLOADS
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _unit_rows(n, dim, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(n, dim, generator=g)
+    return (x / x.norm(dim=1, keepdim=True)).to(DEV)
+
+
+def _check_batch(X, Q, index, k, scores, ids, compare_single=True):
+    exact = (Q.double() @ X.double().T).cpu().numpy()
+    s_np, i_np = scores.cpu().numpy(), ids.cpu().numpy()
+    for b in range(Q.shape[0]):
+        oracle.check_topk(exact[b], k, s_np[b], i_np[b])
+        if compare_single:
+            s1, i1, _ = circuit_search(Q[b], index, k)
+            assert torch.equal(scores[b], s1), (b, scores[b], s1)
+            assert torch.equal(ids[b], i1), (b, ids[b], i1)
+
+
+def test_batch_many_ties_within_capacity():
+    """6,000 identical rows: every one is inside the band, fewer than the
+    rescore's 8,192, so the batch answers without the fallback."""
+    base = _unit_rows(1, 64, 41)
+    X = torch.cat([base.repeat(6000, 1), _unit_rows(700, 64, 42)])
+    index = build_circuit_index(X, num_roots=4, children_per_root=2, rank=2, device=DEV)
+    Q = torch.cat([base, _unit_rows(5, 64, 43)])
+    scores, ids = circuit_search_batch(Q, index, 10)
+    n_over = ctypes.c_int(-1)
+    assert _native.lib().circuit_batch_overflow(index.native_handle(), ctypes.byref(n_over)) == 0
+    assert n_over.value == 0
+    _check_batch(X, Q, index, 10, scores, ids, compare_single=False)
+
+
+@pytest.mark.parametrize("name,n,dim", [
+    ("mixed-100m", 30_000, 384),
+    ("clustered-50k", 20_011, 128),
+    (None, 9_000, 100),
+])
+@pytest.mark.parametrize("k", [1, 10, 32])
+def test_batch_matches_single_query_and_oracle(name, n, dim, k):
+    if name is None:
+        X = _unit_rows(n, dim, 5)
+        Q = _unit_rows(131, dim, 6)
+    else:
+        w = WORKLOADS[name]
+        X = w.corpus(0, n, device=DEV)
+        Q = w.query_batch(131, device=DEV)
+    index = build_circuit_index(X, num_roots=16, children_per_root=4, rank=8, device=DEV)
+    scores, ids = circuit_search_batch(Q, index, k)
+    assert scores.shape == (131, k) and ids.shape == (131, k)
+    _check_batch(X, Q, index, k, scores, ids, compare_single=(k == 10 or name is None))
+
+
+def test_batch_ragged_edges():
+    """N smaller than one leaf tile, batch of one, k clamped to N."""
+    X = _unit_rows(37, 64, 11)
+    index = build_circuit_index(X, num_roots=2, children_per_root=2, rank=2, device=DEV)
+    Q = _unit_rows(1, 64, 12)
+    scores, ids = circuit_search_batch(Q, index, 32)
+    _check_batch(X, Q, index, 32, scores, ids, compare_single=False)
+    X2 = _unit_rows(20, 64, 13)
+    index2 = build_circuit_index(X2, num_roots=2, children_per_root=2, rank=2, device=DEV)
+    scores, ids = circuit_search_batch(Q, index2, 50)  # k > N -> N results
+    assert ids.shape == (1, 20)
+    assert sorted(ids[0].tolist()) == list(range(20))
+
+
+def test_batch_overflow_falls_back_to_single_query():
+    """17,000 identical rows all sit inside the error band of a query equal to
+    them: its candidate list (16,384 rows appended, 8,192 after the final
+    threshold) overflows, the async call marks it with id -2, and
+    circuit_search_batch answers it with circuit_search."""
+    base = _unit_rows(1, 64, 21)
+    X = torch.cat([base.repeat(17000, 1), _unit_rows(500, 64, 22)])
+    index = build_circuit_index(X, num_roots=4, children_per_root=2, rank=2, device=DEV)
+    Q = torch.cat([base, _unit_rows(3, 64, 23)])
+    handle = index.native_handle()
+    s = torch.empty(4, 10, device=DEV)
+    i = torch.empty(4, 10, dtype=torch.int32, device=DEV)
+    rc = _native.lib().circuit_search_batch_async(handle, Q.data_ptr(), 4, 10, s.data_ptr(), i.data_ptr(),
+                                                  torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    n_over = ctypes.c_int(-1)
+    assert _native.lib().circuit_batch_overflow(handle, ctypes.byref(n_over)) == 0
+    assert n_over.value >= 1
+    assert int(i[0, 0]) == -2
+    scores, ids = circuit_search_batch(Q, index, 10)
+    assert int(ids.min()) >= 0
+    _check_batch(X, Q, index, 10, scores, ids, compare_single=False)
+
+
+def test_batch_host_buffers_through_c_abi():
+    w = WORKLOADS["spread-5k"]
+    X = w.corpus(0, 5183, device=DEV)
+    index = build_circuit_index(X, num_roots=8, children_per_root=4, rank=8, device=DEV)
+    Qh = w.query_batch(200).contiguous()
+    s = np.zeros((200, 10), np.float32)
+    i = np.zeros((200, 10), np.int32)
+    torch.cuda.synchronize()
+    rc = _native.lib().circuit_search_batch(index.native_handle(), Qh.data_ptr(), 200, 10, s.ctypes.data,
+                                            i.ctypes.data)
+    assert rc == 0, _native.last_error()
+    _check_batch(X, Qh.to(DEV), index, 10, torch.from_numpy(s).to(DEV), torch.from_numpy(i).to(DEV))
+
+
+def test_batch_rejects_unsupported():
+    X = _unit_rows(500, 64, 31)
+    index = build_circuit_index(X, num_roots=2, children_per_root=2, rank=2, device=DEV)
+    Q = _unit_rows(4, 64, 32)
+    with pytest.raises(ValueError):
+        circuit_search_batch(Q, index, 33)
+    with pytest.raises(ValueError):
+        circuit_search_batch(Q[:, :32], index, 10)
+    s = torch.empty(4, 33, device=DEV)
+    i = torch.empty(4, 33, dtype=torch.int32, device=DEV)
+    rc = _native.lib().circuit_search_batch_async(index.native_handle(), Q.data_ptr(), 4, 33, s.data_ptr(),
+                                                  i.data_ptr(), None)
+    assert rc == -7
+    X2 = _unit_rows(300, 392, 33)
+    index2 = build_circuit_index(X2, num_roots=2, children_per_root=2, rank=2, device=DEV)
+    rc = _native.lib().circuit_search_batch_async(index2.native_handle(), X2.data_ptr(), 4, 10, s.data_ptr(),
+                                                  i.data_ptr(), None)
+    assert rc == -7
