@@ -1,23 +1,32 @@
 // Batched exact top-k search on the B200 tensor cores.
 //
-// k_batch_scan  one persistent CTA per SM.  A work unit is (query tile of 128
-//               queries, slice of 8,192 leaf rows); units are dealt round-robin
-//               in slice-major order so the CTAs in flight read the same slices
-//               and the leaf rows come from HBM once, then from L2.
-//               - 4 epilogue warps write the 128 query rows (fp32 = tf32 bits)
-//                 into TMEM columns [0, D) as the MMA A operand;
-//               - a TMA warp streams 64-row leaf tiles (fp32, 128-byte swizzle,
-//                 boxes of 32 columns) through a shared-memory ring (2 stages
-//                 at D = 384, up to 4 for smaller D);
-//               - an MMA warp issues tcgen05.mma kind::tf32 (M=128 queries,
-//                 N=64 rows, K=8) into one of two TMEM accumulators
-//                 (columns 384-447 / 448-511) and commits to mbarriers;
-//               - each epilogue thread owns one query: it reads its 64 scores
-//                 with tcgen05.ld, keeps its k best tf32 scores in registers,
-//                 and appends every row whose tf32 score is within `band` of
-//                 the running k-th best (max of its own and the query's global
-//                 atomicMax threshold) to the query's candidate list, with
-//                 its tf32 score.
+// k_batch_scan  persistent CTA pairs (clusters of 2, one CTA per SM) computing
+//               the score matrix Q X^T tile by tile with 2-SM tcgen05 MMAs
+//               (cta_group::2, kind::tf32, M = 256 queries, N = 256 leaf rows,
+//               K = 8) and filtering it in the epilogue; no score matrix is
+//               ever written.  A work unit is (query tile of 256 queries, slice
+//               of 8,192 leaf rows); units are dealt round-robin in slice-major
+//               order so the pairs in flight read the same slices and the leaf
+//               rows come from HBM once, then from L2.
+//               - a TMA warp per CTA streams 32-column K-chunks of its 128
+//                 queries and of its 128 leaf rows of the tile (fp32, 128-byte
+//                 swizzle) through a 6-stage shared-memory ring; completion is
+//                 counted on the even CTA's barrier;
+//               - the even CTA's MMA warp issues the pair's MMAs (both operands
+//                 from shared memory) into one of two 256-column TMEM
+//                 accumulators and commits to the barriers of both CTAs, so the
+//                 epilogue of tile t overlaps the MMAs of tile t + 1;
+//               - each epilogue thread owns one query: it reads its 256 scores
+//                 in four 64-column passes with tcgen05.ld, keeps its k best
+//                 tf32 scores in registers, and appends every row whose tf32
+//                 score is within `band` of the running k-th best (max of its
+//                 own and the query's global atomicMax threshold) to the
+//                 query's candidate list, with its tf32 score.
+//               Dependent MMAs into one accumulator are latency-bound, so a
+//               1-SM design that keeps the queries resident in TMEM (384 of 512
+//               columns at D = 384) is capped near half the tensor peak by the
+//               128 accumulator columns left; streaming both operands frees all
+//               512 columns for two N = 256 accumulators.
 // k_batch_rescore  one CTA per query: drops the candidates below the final
 //               threshold minus the band, scores the rest exactly in fp32 (the
 //               same arithmetic as the single-query scan, so both paths return
@@ -31,6 +40,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cmath>
 #include <string>
 
@@ -41,20 +51,23 @@
 
 namespace cb {
 
-constexpr int BQ = 128;              // queries per tile (UMMA M)
-constexpr int BN = 64;               // leaf rows per tile (UMMA N)
-constexpr int BATCH_THREADS = 192;   // warps 0-3 epilogue, 4 TMA, 5 MMA
-constexpr int BATCH_MAX_STAGES = 4;
-constexpr int SLICE_ROWS = 8192;     // rows per work unit
-constexpr int BOX_BYTES = BN * 128;  // one 64 x 32-float box, 128-byte rows
-constexpr uint32_t ACC_COL = 384;    // accumulators at columns 384 and 448
+constexpr int BQ = 128;                  // queries per CTA (UMMA M = 256 per CTA pair)
+constexpr int BN = 256;                  // leaf rows per tile (UMMA N); each CTA loads 128
+constexpr int HALF_N = BN / 2;
+constexpr int EPI_COLS = 64;             // accumulator columns per epilogue pass
+constexpr int BATCH_THREADS = 192;       // warps 0-3 epilogue, 4 TMA, 5 MMA
+constexpr int BATCH_MAX_STAGES = 8;
+constexpr int SLICE_ROWS = 8192;         // rows per work unit
+constexpr int A_BYTES = BQ * 128;        // 128 query rows x 32 floats
+constexpr int B_BYTES = HALF_N * 128;    // 128 leaf rows x 32 floats
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 
 struct BatchScanParams {
   const float* Q;        // [B, D]
   int B, D, N, k;
-  int kb;                // boxes of 32 columns = ceil(D / 32)
+  int kb;                // K-chunks of 32 columns = ceil(D / 32)
   int stages;            // shared-memory ring depth (<= BATCH_MAX_STAGES)
-  int QT, units;         // query tiles, work units
+  int QP, units;         // query pair-tiles (256 queries), work units
   float band_scale;      // band = band_scale * ||q||
   uint32_t* theta;       // [B] order-preserving keys of the running k-th best
   int* cand_count;       // [B]
@@ -63,20 +76,83 @@ struct BatchScanParams {
   int* err;
 };
 
+// One epilogue pass over 64 accumulator columns (leaf rows row_base + i) of this
+// thread's query.  Returns nothing; updates the running state in place.
+template <int KB>
+__device__ __forceinline__ void epi_pass(const uint32_t (&sc0)[32], const uint32_t (&sc1)[32], int row_base, int nrow,
+                                         float band, float& theta, float& theta_local, float (&top)[KB], int q,
+                                         float* stash, const BatchScanParams& P) {
+  const float lim = theta - band;
+  uint64_t mask = 0ull;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    mask |= (uint64_t)(__uint_as_float(sc0[i]) >= lim) << i;
+    mask |= (uint64_t)(__uint_as_float(sc1[i]) >= lim) << (32 + i);
+  }
+  if (nrow < EPI_COLS) mask &= nrow > 0 ? (1ull << nrow) - 1ull : 0ull;
+  if (!mask) return;
+  // rare: stage the scores ([column][thread], conflict-free), first raise the
+  // k best with them, then append the rows still within the band
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    stash[i * BQ + threadIdx.x] = __uint_as_float(sc0[i]);
+    stash[(32 + i) * BQ + threadIdx.x] = __uint_as_float(sc1[i]);
+  }
+  for (uint64_t m = mask; m; m &= m - 1ull) {
+    const int i = __ffsll((long long)m) - 1;
+    const float sv = stash[i * BQ + threadIdx.x];
+    if (sv > theta_local) {
+      float x = sv;
+#pragma unroll
+      for (int j = 0; j < KB; ++j) {
+        const float t = top[j];
+        const bool gt = x > t;
+        top[j] = gt ? x : t;
+        x = gt ? t : x;
+      }
+      float kth = top[0];
+#pragma unroll
+      for (int j = 0; j < KB; ++j)
+        if (j == P.k - 1) kth = top[j];
+      theta_local = kth;
+    }
+  }
+  theta = fmaxf(theta, theta_local);
+  const float lim2 = theta - band;
+  for (uint64_t m = mask; m; m &= m - 1ull) {
+    const int i = __ffsll((long long)m) - 1;
+    const float sv = stash[i * BQ + threadIdx.x];
+    if (sv >= lim2) {
+      const int slot = atomicAdd(P.cand_count + q, 1);
+      if (slot < P.cap)
+        P.cand[(size_t)q * P.cap + slot] = ((unsigned long long)f2key(sv) << 32) | (uint32_t)(row_base + i);
+    }
+  }
+}
+
+// Launched as clusters of 2 CTAs.  CTA rank r of the pair loads queries
+// [256 qp + 128 r, +128) and leaf rows [row0 + 128 r, +128) of every tile; the
+// pair's accumulator holds, in CTA r's TMEM lanes, its 128 queries against all
+// 256 rows of the tile (columns 0-127: rows loaded by the even CTA, 128-255:
+// by the odd CTA).
 template <int KB>
 __global__ void __launch_bounds__(BATCH_THREADS, 1)
-    k_batch_scan(const __grid_constant__ CUtensorMap xmap, BatchScanParams P) {
+    k_batch_scan(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap xmap,
+                 BatchScanParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  __shared__ uint64_t full[BATCH_MAX_STAGES], empty[BATCH_MAX_STAGES], acc_full[2], acc_empty[2], a_full, a_empty;
+  // full / acc_empty are used in the even CTA only; empty / acc_full in both
+  // (multicast commits).
+  __shared__ uint64_t full[BATCH_MAX_STAGES], empty[BATCH_MAX_STAGES], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int stage_bytes = P.kb * BOX_BYTES;
+  const uint32_t rank = tc::cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int S = P.stages;
-  float* stash = reinterpret_cast<float*>(smem + (size_t)S * stage_bytes);  // [BN][BQ] scores
+  float* stash = reinterpret_cast<float*>(smem + (size_t)S * STAGE_BYTES);  // [64][BQ] scores
 
-  if (warp == 5) tc::tmem_alloc(&tmem_base, 512);
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
@@ -84,97 +160,90 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], BQ);
+      mbar_init(&acc_empty[b], 8);  // one lane of each epilogue warp of both CTAs
     }
-    mbar_init(&a_full, BQ);
-    mbar_init(&a_empty, 1);
-    fence_mbar_init();
+    tc::fence_mbar_init_cluster();
   }
+  if (warp == 5) tc::tmem_alloc_pair(&tmem_base, 512);
   tc::fence_before();
-  __syncthreads();
+  tc::cluster_sync();  // barriers and the pair's TMEM exist before any remote access
   tc::fence_after();
   const uint32_t tmem = tmem_base;
+  const uint32_t lead_full = tc::mapa_shared(smem_u32(&full[0]), 0);
+  const uint32_t lead_acc_empty = tc::mapa_shared(smem_u32(&acc_empty[0]), 0);
 
   if (warp == 4) {
-    // ---------------------------------------------------------- TMA producer
+    // ---------------------------------------------------------- TMA producer (both CTAs)
     if (lane == 0) {
-      int it = 0;
+      int c = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
-        const int slice = u / P.QT;
+      for (int u = pair; u < P.units && ok; u += npairs) {
+        const int qp = u % P.QP, slice = u / P.QP;
+        const int qrow = qp * (2 * BQ) + (int)rank * BQ;
         const int r0 = slice * SLICE_ROWS, r1 = min(P.N, r0 + SLICE_ROWS);
-        for (int row = r0; row < r1; row += BN, ++it) {
-          const int s = it % S, f = it / S;
-          if (f > 0 && !mbar_wait(&empty[s], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[s], (uint32_t)stage_bytes);
-          unsigned char* dst = smem + (size_t)s * stage_bytes;
-          for (int j = 0; j < P.kb; ++j) tc::tma_load_2d(dst + j * BOX_BYTES, &xmap, 32 * j, row, &full[s]);
+        for (int row0 = r0; row0 < r1 && ok; row0 += BN) {
+          for (int j = 0; j < P.kb; ++j, ++c) {
+            const int s = c % S, f = c / S;
+            if (f > 0 && !mbar_wait(&empty[s], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) { ok = false; break; }
+            if (leader) mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * STAGE_BYTES));
+            unsigned char* dst = smem + (size_t)s * STAGE_BYTES;
+            const uint32_t bar = lead_full + 8u * (uint32_t)s;
+            tc::tma_load_2d_pair(dst, &qmap, 32 * j, qrow, bar);
+            tc::tma_load_2d_pair(dst + A_BYTES, &xmap, 32 * j, row0 + (int)rank * HALF_N, bar);
+          }
         }
       }
+      // the last commits to this CTA's empty barriers have landed before it exits
+      for (int t = c > S ? c - S : 0; t < c && ok; ++t)
+        ok = mbar_wait(&empty[t % S], (t / S) & 1, P.err, ERR_TIMEOUT_EMPTY);
     }
   } else if (warp == 5) {
-    // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = tc::idesc_tf32(BQ, BN);
+    // ---------------------------------------------------------- MMA issuer (even CTA)
+    if (leader && lane == 0) {
+      const uint32_t idesc = tc::idesc_tf32(2 * BQ, BN);
       const uint32_t sbase = smem_u32(smem);
-      int it = 0, ui = 0;
+      int c = 0, it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < P.units && ok; u += gridDim.x, ++ui) {
-        if (!mbar_wait(&a_full, ui & 1, P.err, ERR_TIMEOUT_FULL)) break;
-        tc::fence_after();
-        const int slice = u / P.QT;
+      for (int u = pair; u < P.units && ok; u += npairs) {
+        const int slice = u / P.QP;
         const int r0 = slice * SLICE_ROWS, r1 = min(P.N, r0 + SLICE_ROWS);
-        for (int row = r0; row < r1; row += BN, ++it) {
-          const int s = it % S, f = it / S;
+        for (int row0 = r0; row0 < r1 && ok; row0 += BN, ++it) {
           const int b = it & 1, fb = it >> 1;
-          if (!mbar_wait(&full[s], f & 1, P.err, ERR_TIMEOUT_FULL)) { ok = false; break; }
-          if (fb > 0 && !mbar_wait(&acc_empty[b], (fb - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) { ok = false; break; }
-          tc::fence_after();
-          const uint32_t acc = tmem + ACC_COL + (uint32_t)(b * BN);
-          const uint32_t stage = sbase + (uint32_t)(s * stage_bytes);
-          for (int j = 0; j < P.kb; ++j) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              tc::mma_tf32_ts(acc, tmem + (uint32_t)(32 * j + 8 * kk),
-                              tc::sdesc_k_sw128(stage + (uint32_t)(j * BOX_BYTES + kk * 32)), idesc,
-                              (j | kk) ? 1u : 0u);
-            }
+          if (fb > 0 && !tc::mbar_wait_cluster(&acc_empty[b], (fb - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) {
+            ok = false;
+            break;
           }
-          tc::commit(&empty[s]);
-          tc::commit(&acc_full[b]);
+          tc::fence_after();
+          const uint32_t acc = tmem + (uint32_t)(b * BN);
+          for (int j = 0; j < P.kb; ++j, ++c) {
+            const int s = c % S, f = c / S;
+            if (!mbar_wait(&full[s], f & 1, P.err, ERR_TIMEOUT_FULL)) { ok = false; break; }
+            tc::fence_after();
+            const uint32_t sa = sbase + (uint32_t)(s * STAGE_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              tc::mma_tf32_ss_pair(acc, tc::sdesc_k_sw128(sa + (uint32_t)(kk * 32)),
+                                   tc::sdesc_k_sw128(sa + (uint32_t)(A_BYTES + kk * 32)), idesc, (j | kk) ? 1u : 0u);
+            tc::commit_pair(&empty[s], 0x3);  // the stage refills once these MMAs have read it
+          }
+          if (ok) tc::commit_pair(&acc_full[b], 0x3);
         }
-        tc::commit(&a_empty);  // A may be overwritten once every MMA of this unit is done
       }
     }
   } else {
     // ---------------------------------------------------------- epilogue (one query per thread)
     const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-    int it = 0, ui = 0;
+    int it = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < P.units && ok; u += gridDim.x, ++ui) {
-      const int qt = u % P.QT, slice = u / P.QT;
-      const int q = qt * BQ + 32 * warp + lane;
+    for (int u = pair; u < P.units && ok; u += npairs) {
+      const int qp = u % P.QP, slice = u / P.QP;
+      const int q = qp * (2 * BQ) + (int)rank * BQ + 32 * warp + lane;
       const bool qv = q < P.B;
-      if (ui > 0 && !mbar_wait(&a_empty, (ui - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) break;
-      tc::fence_after();
-      // query row -> TMEM lane, columns [0, 32 kb) (zeros past D and for padding queries)
       float qn2 = 0.f;
-      const float* qrow = P.Q + (size_t)(qv ? q : 0) * P.D;
-      for (int j = 0; j < P.kb; ++j) {
-        uint32_t v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int c = 32 * j + i;
-          const float x = (qv && c < P.D) ? __ldg(qrow + c) : 0.f;
-          qn2 = fmaf(x, x, qn2);
-          v[i] = __float_as_uint(x);
-        }
-        tc::st_32x32b_x32(tmem + lane_base + (uint32_t)(32 * j), v);
+      if (qv) {
+        const float* qrow = P.Q + (size_t)q * P.D;
+        for (int c = 0; c < P.D; ++c) qn2 = fmaf(__ldg(qrow + c), __ldg(qrow + c), qn2);
       }
-      tc::wait_st();
-      tc::fence_before();
-      mbar_arrive(&a_full);
-
       const float band = P.band_scale * sqrtf(qn2) * 1.0001f;
       float top[KB];
 #pragma unroll
@@ -190,66 +259,44 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
         const int b = it & 1, fb = it >> 1;
         if (!mbar_wait(&acc_full[b], fb & 1, P.err, ERR_TIMEOUT_FULL)) { ok = false; break; }
         tc::fence_after();
-        uint32_t sc0[32], sc1[32];
-        tc::ld_32x32b_x32(tmem + lane_base + ACC_COL + (uint32_t)(b * BN), sc0);
-        tc::ld_32x32b_x32(tmem + lane_base + ACC_COL + (uint32_t)(b * BN + 32), sc1);
-        tc::wait_ld();
-        tc::fence_before();
-        mbar_arrive(&acc_empty[b]);
-        if (!qv) continue;
-        // global threshold read one tile ahead (its latency overlaps this tile)
-        if (g_pending) theta = fmaxf(theta, key2f(g_pending));
-        g_pending = ld_volatile_u32(P.theta + q);
-        const int nrow = min(BN, r1 - row0);
-        // common case, constant register indices: which rows can still matter?
-        const float lim = theta - band;
-        uint64_t mask = 0ull;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          mask |= (uint64_t)(__uint_as_float(sc0[i]) >= lim) << i;
-          mask |= (uint64_t)(__uint_as_float(sc1[i]) >= lim) << (32 + i);
+        if (qv) {
+          // global threshold read one tile ahead (its latency overlaps this tile)
+          if (g_pending) theta = fmaxf(theta, key2f(g_pending));
+          g_pending = ld_volatile_u32(P.theta + q);
         }
-        if (nrow < BN) mask &= (1ull << nrow) - 1ull;
-        if (mask) {
-          // rare: stage the scores ([row][thread], conflict-free), first raise the
-          // k best with them, then append the rows still within the band
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            stash[i * BQ + threadIdx.x] = __uint_as_float(sc0[i]);
-            stash[(32 + i) * BQ + threadIdx.x] = __uint_as_float(sc1[i]);
+        // two halves of 128 columns: all four loads of a half issued before one
+        // wait; the common case is one max per score and one compare per half
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          uint32_t sa[32], sb[32], sc[32], sd[32];
+          const uint32_t col = tmem + lane_base + (uint32_t)(b * BN + half * 128);
+          tc::ld_32x32b_x32(col, sa);
+          tc::ld_32x32b_x32(col + 32, sb);
+          tc::ld_32x32b_x32(col + 64, sc);
+          tc::ld_32x32b_x32(col + 96, sd);
+          tc::wait_ld();
+          if (half == 1) {
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive_remote(lead_acc_empty + 8u * (uint32_t)b);
           }
-          for (uint64_t m = mask; m; m &= m - 1ull) {
-            const int i = __ffsll((long long)m) - 1;
-            const float sv = stash[i * BQ + threadIdx.x];
-            if (sv > theta_local) {
-              float x = sv;
+          if (!qv) continue;
+          float mx[32];
 #pragma unroll
-              for (int j = 0; j < KB; ++j) {
-                const float t = top[j];
-                const bool gt = x > t;
-                top[j] = gt ? x : t;
-                x = gt ? t : x;
-              }
-              float kth = top[0];
+          for (int i = 0; i < 32; ++i)
+            mx[i] = fmaxf(fmaxf(__uint_as_float(sa[i]), __uint_as_float(sb[i])),
+                          fmaxf(__uint_as_float(sc[i]), __uint_as_float(sd[i])));
 #pragma unroll
-              for (int j = 0; j < KB; ++j)
-                if (j == P.k - 1) kth = top[j];
-              theta_local = kth;
-            }
-          }
-          theta = fmaxf(theta, theta_local);
-          const float lim2 = theta - band;
-          for (uint64_t m = mask; m; m &= m - 1ull) {
-            const int i = __ffsll((long long)m) - 1;
-            if (stash[i * BQ + threadIdx.x] >= lim2) {
-              const int slot = atomicAdd(P.cand_count + q, 1);
-              if (slot < P.cap)
-                P.cand[(size_t)q * P.cap + slot] =
-                    ((unsigned long long)f2key(stash[i * BQ + threadIdx.x]) << 32) | (uint32_t)(row0 + i);
-            }
+          for (int w = 16; w > 0; w >>= 1)
+#pragma unroll
+            for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
+          if (mx[0] >= theta - band) {
+            const int rb = row0 + half * 128;
+            epi_pass<KB>(sa, sb, rb, r1 - rb, band, theta, theta_local, top, q, stash, P);
+            epi_pass<KB>(sc, sd, rb + 64, r1 - rb - 64, band, theta, theta_local, top, q, stash, P);
           }
         }
-        if ((tiles & 7) == 7 && theta_local > -INFINITY) {
+        if (qv && (tiles & 1) == 1 && theta_local > -INFINITY) {
           const uint32_t key = f2key(theta_local);
           if (key > published) {
             atomicMax(P.theta + q, key);
@@ -263,9 +310,12 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
       }
     }
   }
+  // Every MMA has completed (each epilogue waited for its last accumulator) and
+  // no CTA touches its peer after this point.
   tc::fence_before();
-  __syncthreads();
-  if (warp == 5) tc::tmem_dealloc(tmem, 512);
+  tc::cluster_sync();
+  tc::fence_after();
+  if (warp == 5) tc::tmem_dealloc_pair(tmem, 512);
 }
 
 // One CTA per query.  The candidate list was appended against running
@@ -389,16 +439,21 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-bool make_leaf_tensor_map(const float* leaf, int N, int D, void* out_map) {
+// [rows, D] fp32 row-major -> boxes of 128 rows x 32 columns, 128-byte swizzle.
+static bool make_rows_tensor_map(const float* base, int rows, int D, void* out_map) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (!enc) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)N};
+  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)D * 4};
-  cuuint32_t box[2] = {32, (cuuint32_t)BN};
+  cuuint32_t box[2] = {32, 128};
   cuuint32_t estr[2] = {1, 1};
-  return enc(reinterpret_cast<CUtensorMap*>(out_map), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(leaf),
+  return enc(reinterpret_cast<CUtensorMap*>(out_map), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base),
              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_leaf_tensor_map(const float* leaf, int N, int D, void* out_map) {
+  return make_rows_tensor_map(leaf, N, D, out_map);
 }
 
 cudaError_t launch_max_row_norm(const float* leaf, int N, int D, unsigned int* out_key, int sms, cudaStream_t st) {
@@ -411,26 +466,52 @@ cudaError_t launch_max_row_norm(const float* leaf, int N, int D, unsigned int* o
 // Ring depth from the shared-memory budget; at least 120 KB is requested so that
 // one CTA (and one 512-column TMEM allocation) occupies each SM.
 static constexpr int BATCH_SMEM_BUDGET = 227 * 1024 - 1024;
-static int batch_stages(int kb) {
-  const int s = (BATCH_SMEM_BUDGET - BN * BQ * 4 - 1024) / (kb * BOX_BYTES);
+static int batch_stages() {
+  const int s = (BATCH_SMEM_BUDGET - EPI_COLS * BQ * 4 - 1024) / STAGE_BYTES;
   return s < BATCH_MAX_STAGES ? s : BATCH_MAX_STAGES;
 }
-static int batch_scan_smem(int kb, int stages) {
-  const int b = stages * kb * BOX_BYTES + BN * BQ * 4 + 1024;
+static int batch_scan_smem(int stages) {
+  const int b = stages * STAGE_BYTES + EPI_COLS * BQ * 4 + 1024;
   return b < 120 * 1024 ? 120 * 1024 : b;
 }
 
 template <int KB>
-static cudaError_t launch_batch_scan_t(const void* map, const BatchScanParams& P, int grid, cudaStream_t st) {
-  const int smem = batch_scan_smem(P.kb, P.stages);
+static cudaError_t launch_batch_scan_t(const void* qmap, const void* xmap, const BatchScanParams& P, int max_pairs,
+                                       cudaStream_t st) {
+  const int smem = batch_scan_smem(P.stages);
   static int configured = 0;
   if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(k_batch_scan<KB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     configured = smem;
   }
-  k_batch_scan<KB><<<grid, BATCH_THREADS, smem, st>>>(*reinterpret_cast<const CUtensorMap*>(map), P);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(BATCH_THREADS);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // pairs that can be resident at once: a persistent grid larger than that
+  // would leave late pairs a second wave
+  static int resident = 0, resident_smem = 0;
+  if (resident_smem != smem) {
+    cfg.gridDim = dim3(2 * max_pairs);
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxActiveClusters(&n, k_batch_scan<KB>, &cfg);
+    if (e != cudaSuccess) return e;
+    if (n < 1) return cudaErrorInvalidConfiguration;
+    resident = n;
+    resident_smem = smem;
+  }
+  const int pairs = std::min(std::min(P.units, max_pairs), resident);
+  cfg.gridDim = dim3(2 * pairs);
+  return cudaLaunchKernelEx(&cfg, k_batch_scan<KB>, *reinterpret_cast<const CUtensorMap*>(qmap),
+                            *reinterpret_cast<const CUtensorMap*>(xmap), P);
 }
 
 template <int VPL>
@@ -461,11 +542,11 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   P.N = ix.N;
   P.k = k;
   P.kb = (ix.D + 31) / 32;
-  P.stages = batch_stages(P.kb);
+  P.stages = batch_stages();
   if (P.stages < 2 || ix.D % 4 != 0 || ix.D > BATCH_MAX_DIM || k < 1 || k > BATCH_MAX_K) return cudaErrorInvalidValue;
-  P.QT = (B + BQ - 1) / BQ;
+  P.QP = (B + 2 * BQ - 1) / (2 * BQ);
   const int slices = (ix.N + SLICE_ROWS - 1) / SLICE_ROWS;
-  P.units = P.QT * slices;
+  P.units = P.QP * slices;
   // eps = (2^-9 + 2^-20 + 2 D 2^-23 + gamma_D) ||q|| max||x||, padded; band = 2 eps
   const double u = 5.9604644775390625e-08;
   const double gD = ix.D * u / (1.0 - ix.D * u);
@@ -476,8 +557,11 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   P.cand = bw.cand;
   P.cap = bw.cap;
   P.err = bw.err;
-  const int grid = P.units < bw.sms ? P.units : bw.sms;
-  e = (k <= 16) ? launch_batch_scan_t<16>(bw.tmap, P, grid, st) : launch_batch_scan_t<32>(bw.tmap, P, grid, st);
+  alignas(64) unsigned char qmap[128];
+  if (!make_rows_tensor_map(Q, B, ix.D, qmap)) return cudaErrorInvalidValue;
+  const int max_pairs = bw.sms / 2;
+  e = (k <= 16) ? launch_batch_scan_t<16>(qmap, bw.tmap, P, max_pairs, st)
+                : launch_batch_scan_t<32>(qmap, bw.tmap, P, max_pairs, st);
   if (e != cudaSuccess) return e;
   const int vpl = (ix.D / 4 + 31) / 32;
   switch (vpl) {
