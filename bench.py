@@ -19,6 +19,13 @@ D2H results per query) at N = 1, or the torch-level equivalent with an NCCL
 merge at N > 1.  Inputs (19-154 GB per GPU) exceed the 126 MB L2, so no flush
 is needed between steps.
 
+The line's `batched` object measures the batched path on the same index:
+--batch (4096) queries per step answered together by circuit_search_batch_async
+(one 2-SM tcgen05 tf32 filter GEMM over every row of the shard with a
+rigorous error band, then exact fp32 rescoring of the candidates), one
+all-gather of [B, k] and a per-query merge at N > 1.  Its roofline is the scan
+kernel's tf32 FLOP rate against a cuBLAS tf32 GEMM measured in the same run.
+
 `--impl reference` times the reference's own CPU search path (brute force
 ``topk(X @ q)``, circuit_rag/search.py:58-61) -- the oracle port -- on the host
 cores, on a bounded row sample of the same workload, rank 0 only.
@@ -58,6 +65,9 @@ def parse():
     ap.add_argument("--rows", type=int, default=0, help="total rows (default: the workload's N)")
     ap.add_argument("--e2e-steps", type=int, default=0)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--batch", type=int, default=4096, help="queries per batch of the batched search (0: skip it)")
+    ap.add_argument("--batch-steps", type=int, default=3)
+    ap.add_argument("--batch-warmup", type=int, default=2)
     return ap.parse_args()
 
 
@@ -175,6 +185,188 @@ def run_reference(args, world, rank):
         "e2e": {"value": cb["value"], "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def tf32_gemm_peak(dev, seconds=2.0):
+    """cuBLAS tf32 8192^3 GEMM on this GPU: best of 5 (burst) and the mean of a
+    back-to-back loop of about `seconds` (sustained, under the power cap)."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    n = 8192
+    a = torch.randn(n, n, device=dev)
+    b = torch.randn(n, n, device=dev)
+    c = torch.empty(n, n, device=dev)
+    for _ in range(3):
+        torch.matmul(a, b, out=c)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = 1e30
+    for _ in range(5):
+        e0.record()
+        torch.matmul(a, b, out=c)
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    reps = max(3, int(seconds * 1000.0 / best))
+    e0.record()
+    for _ in range(reps):
+        torch.matmul(a, b, out=c)
+    e1.record()
+    torch.cuda.synchronize()
+    mean = e0.elapsed_time(e1) / reps
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b, c
+    torch.cuda.empty_cache()
+    fl = 2.0 * n ** 3
+    return fl / best / 1e9, fl / mean / 1e9  # ms -> TFLOP/s
+
+
+def run_batched(args, w, idx, dev, world, rank, n_total, n_local, start, k, D):
+    """Batched exact search (tensor-core scan + exact rescoring) of --batch
+    queries per step on every rank's shard, one all-gather of [B, k] per step,
+    per-query merge.  Overflowed queries are answered by the single-query
+    search inside the timed region."""
+    import torch.distributed as dist
+
+    from circuit_rag import _native
+    from circuit_rag.search import _launch
+    from circuit_rag.shard import merge_topk_batch
+
+    L = _native.lib()
+    handle = idx.native_handle()
+    stream = torch.cuda.current_stream()
+    Bq, bsteps, bwarm = args.batch, args.batch_steps, max(1, args.batch_warmup)
+    QB = w.query_batch(Bq * (bwarm + bsteps), device=dev).view(bwarm + bsteps, Bq, D)
+    s = torch.empty(Bq, k, device=dev)
+    i = torch.empty(Bq, k, dtype=torch.int32, device=dev)
+    gs = torch.empty(world * Bq, k, device=dev) if world > 1 else None
+    gi = torch.empty(world * Bq, k, dtype=torch.int32, device=dev) if world > 1 else None
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(bsteps)]
+    for pair in ev:
+        for e in pair:
+            e.record(stream)
+    n_over = ctypes.c_int(0)
+    fallbacks = [0]
+    res = [None]
+
+    def step(j, timed):
+        e0, e1 = ev[j - bwarm] if timed else (None, None)
+        rc = L.circuit_search_batch_async(handle, QB[j].data_ptr(), Bq, k, s.data_ptr(), i.data_ptr(),
+                                          stream.cuda_stream, e0.cuda_event if e0 else None,
+                                          e1.cuda_event if e1 else None)
+        assert rc == 0, _native.last_error()
+        assert L.circuit_batch_overflow(handle, ctypes.byref(n_over)) == 0
+        if n_over.value:
+            for q in torch.nonzero(i[:, 0] == -2).flatten().tolist():
+                _launch(handle, QB[j, q], k, 0, s[q], i[q], None, stream)
+                fallbacks[0] += 1
+        if world > 1:
+            dist.all_gather_into_tensor(gs, s)
+            dist.all_gather_into_tensor(gi, i)
+            res[0] = merge_topk_batch(gs.view(world, Bq, k), gi.view(world, Bq, k), k)
+        else:
+            res[0] = (s, i)
+
+    for j in range(bwarm):
+        step(j, False)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    fallbacks[0] = 0
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for j in range(bwarm, bwarm + bsteps):
+        step(j, True)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    elapsed = t0.elapsed_time(t1)
+    scan_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    if world > 1:
+        t = torch.tensor([elapsed, scan_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed, scan_ms = float(t[0]), float(t[1])
+    ms_s, ms_i = res[0]
+
+    # exactness of the last timed batch: first queries against float64 brute force
+    from oracle import oracle
+
+    leaf = idx.leaf_vectors
+    bad, nchk = 0, 3
+    for b in range(nchk):
+        q = QB[bwarm + bsteps - 1, b].double()
+        ex = torch.empty(n_local, dtype=torch.float64, device=dev)
+        for a in range(0, n_local, 1 << 20):
+            ex[a:a + (1 << 20)] = leaf[a:a + (1 << 20)].double() @ q
+        if world == 1:
+            exact = torch.empty_like(ex)
+            exact[idx.original_ids.long() - start] = ex
+            exact = exact.cpu().numpy()
+        else:
+            top = torch.topk(ex, k)
+            g1 = torch.empty(world * k, dtype=torch.float64, device=dev)
+            g2 = torch.empty(world * k, dtype=torch.int32, device=dev)
+            dist.all_gather_into_tensor(g1, top.values)
+            dist.all_gather_into_tensor(g2, idx.original_ids[top.indices].contiguous())
+            exact = np.full(n_total, -np.inf)
+            exact[g2.cpu().numpy()] = g1.cpu().numpy()
+        try:
+            oracle.check_topk(exact, k, ms_s[b].cpu().numpy(), ms_i[b].cpu().numpy() - (start if world == 1 else 0))
+        except AssertionError:
+            bad += 1
+
+    # end to end through the public API with host buffers
+    if world == 1:
+        hq = np.ascontiguousarray(QB[0].cpu().numpy())
+        hs = np.zeros((Bq, k), np.float32)
+        hi = np.zeros((Bq, k), np.int32)
+        assert L.circuit_search_batch(handle, hq.ctypes.data, Bq, k, hs.ctypes.data, hi.ctypes.data) == 0
+        reps = 2
+        tt = time.perf_counter()
+        for _ in range(reps):
+            assert L.circuit_search_batch(handle, hq.ctypes.data, Bq, k, hs.ctypes.data, hi.ctypes.data) == 0
+        e2e_s = (time.perf_counter() - tt) / reps
+        api = "circuit_search_batch (C ABI, host buffers)"
+    else:
+        hq = QB[0].cpu().pin_memory()
+        hres_s = torch.empty(Bq, k, pin_memory=True)
+        hres_i = torch.empty(Bq, k, dtype=torch.int32, pin_memory=True)
+        dq = torch.empty(Bq, D, device=dev)
+        reps = 2
+        torch.cuda.synchronize()
+        dist.barrier()
+        tt = time.perf_counter()
+        for _ in range(reps):
+            dq.copy_(hq, non_blocking=True)
+            assert L.circuit_search_batch_async(handle, dq.data_ptr(), Bq, k, s.data_ptr(), i.data_ptr(),
+                                                stream.cuda_stream, None, None) == 0
+            dist.all_gather_into_tensor(gs, s)
+            dist.all_gather_into_tensor(gi, i)
+            a, b = merge_topk_batch(gs.view(world, Bq, k), gi.view(world, Bq, k), k)
+            hres_s.copy_(a, non_blocking=True)
+            hres_i.copy_(b, non_blocking=True)
+            torch.cuda.synchronize()
+        t = torch.tensor([(time.perf_counter() - tt) / reps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+        api = "circuit_search_batch_async + NCCL all-gather + circuit_merge_topk_batch"
+
+    burst, peak = tf32_gemm_peak(dev)  # TFLOP/s
+    flops = 2.0 * Bq * n_local * D
+    achieved = flops / (scan_ms * 1e-3) / 1e12
+    return {
+        "value": round(Bq * bsteps / (elapsed / 1000.0), 1), "unit": "queries/s", "batch": Bq, "k": k,
+        "steps": bsteps, "warmup": bwarm, "ms_per_batch": round(elapsed / bsteps, 3),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4),
+                     "peak_kind": "measured in this run: cuBLAS tf32 8192^3, back-to-back mean (sustained)",
+                     "peak_burst": round(burst, 1), "frac_of_burst": round(achieved / burst, 4),
+                     "kernel": "k_batch_scan (2-SM tcgen05 kind::tf32 filter GEMM, fused candidate epilogue)",
+                     "algorithmic_flops_per_launch": flops, "mean_launch_ms": round(scan_ms, 3)},
+        "overflow_fallbacks": fallbacks[0],
+        "check": {"checked_queries": nchk, "mismatches": bad},
+        "e2e": {"value": round(Bq / e2e_s, 1), "unit": "queries/s", "h2d_bytes_per_step": Bq * D * 4,
+                "d2h_bytes_per_step": Bq * k * 8, "api": api},
+        "gpu_launches_per_step": 2 + (1 if world > 1 else 0),
+    }
 
 
 def main():
@@ -360,6 +552,10 @@ def main():
         e2e = {"value": e2e_steps / float(e2e_s.item()), "unit": "queries/s", "h2d_bytes_per_step": D * 4,
                "d2h_bytes_per_step": k * 8, "api": "circuit_search_async + NCCL all-gather + circuit_merge_topk"}
 
+    batched = None
+    if args.batch > 0:
+        batched = run_batched(args, w, idx, dev, world, rank, n_total, n_local, start, k, D)
+
     peak, peak_kind = measured_peaks()
     mean_scan_ms = statistics.mean(scan_ms)
     alg_bytes = statistics.mean(main_rows) * D * 4
@@ -389,7 +585,7 @@ def main():
                                                                                       len(lat_us) * 99 // 100)], 2),
             "pruned_leaf_fraction": round(1.0 - statistics.mean(all_rows) / n_local, 5),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": (4 if world == 1 else 5) * steps, "clocks": clocks,
-            "build_s": round(build_s, 1), "check": check,
+            "build_s": round(build_s, 1), "check": check, "batched": batched,
         }
         print(json.dumps(line), flush=True)
     idx.close()

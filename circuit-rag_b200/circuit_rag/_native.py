@@ -39,6 +39,7 @@ EXPORTED_SYMBOLS = (
     "circuit_op_flat_exact_score",
     "circuit_op_hierarchical_search",
     "circuit_merge_topk",
+    "circuit_merge_topk_batch",
     "circuit_plan_shards",
     "circuit_flat_search_noalloc",
     "circuit_search_batch_async",
@@ -103,9 +104,10 @@ def _declare(lib):
         "circuit_op_flat_exact_score": (_I, [_P, _P, _I64, _I, _P, _P]),
         "circuit_op_hierarchical_search": (_I, [_P] * 21 + [_I, _I, _I64, _I, _F, _I, _F, _P]),
         "circuit_merge_topk": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+        "circuit_merge_topk_batch": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P]),
         "circuit_plan_shards": (_I, [_P, _I, _I, _P, _P]),
         "circuit_flat_search_noalloc": (_I, [_P, _I64, _I, _P, _I, _P, _P, _P]),
-        "circuit_search_batch_async": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+        "circuit_search_batch_async": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _P]),
         "circuit_batch_overflow": (_I, [_P, _P]),
         "circuit_search_batch": (_I, [_P, _P, _I, _I, _P, _P]),
     }

@@ -158,7 +158,7 @@ def circuit_search_batch(queries: torch.Tensor, index: CircuitIndex, k: int = 10
         if B == 0:
             return scores, ids
         rc = _native.lib().circuit_search_batch_async(handle, queries.data_ptr(), B, k, scores.data_ptr(),
-                                                      ids.data_ptr(), stream.cuda_stream)
+                                                      ids.data_ptr(), stream.cuda_stream, None, None)
         _native.check(rc, "circuit_search_batch")
         n_over = ctypes.c_int(0)
         _native.check(_native.lib().circuit_batch_overflow(handle, ctypes.byref(n_over)), "circuit_batch_overflow")

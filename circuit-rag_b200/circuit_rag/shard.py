@@ -108,6 +108,31 @@ def merge_topk(scores: torch.Tensor, ids: torch.Tensor, k: int) -> Tuple[torch.T
     return out_s, out_i
 
 
+def merge_topk_batch(scores: torch.Tensor, ids: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-query global top-k of gathered batch results on the device
+    (circuit_merge_topk_batch): scores / ids [world, B, k_in] -> [B, k]."""
+    world, B, k_in = scores.shape
+    scores = scores.to(torch.float32).contiguous()
+    ids = ids.to(torch.int32).contiguous()
+    out_s = torch.empty(B, k, dtype=torch.float32, device=scores.device)
+    out_i = torch.empty(B, k, dtype=torch.int32, device=scores.device)
+    rc = _native.lib().circuit_merge_topk_batch(scores.data_ptr(), ids.data_ptr(), B, world, k_in, int(k),
+                                                out_s.data_ptr(), out_i.data_ptr(),
+                                                torch.cuda.current_stream(scores.device).cuda_stream)
+    _native.check(rc, "merge_topk_batch")
+    return out_s, out_i
+
+
+def merge_topk_batch_host(scores: torch.Tensor, ids: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The batched merge on host tensors (used with the gloo backend)."""
+    world, B, k_in = scores.shape
+    out_s = torch.empty(B, k)
+    out_i = torch.empty(B, k, dtype=torch.int32)
+    for q in range(B):
+        out_s[q], out_i[q] = merge_topk_host(scores[:, q].reshape(-1), ids[:, q].reshape(-1), k)
+    return out_s, out_i
+
+
 def merge_topk_host(scores: torch.Tensor, ids: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
     """The same merge on host tensors (used with the gloo backend)."""
     s = scores.double().numpy()
@@ -153,6 +178,28 @@ class ShardedSearcher:
         self.dist.all_gather_into_tensor(gs, s.contiguous(), group=self.group)
         self.dist.all_gather_into_tensor(gi, i.contiguous(), group=self.group)
         return self._merge(gs, gi, k)
+
+    def search_batch(self, queries: torch.Tensor, k: int = 10, local_batch: Optional[Callable] = None,
+                     merge_batch: Optional[Callable] = None):
+        """Exact top-k of a batch [B, dim]: each rank runs the batched search on
+        its shard, one all-gather of [B, k] scores and ids, per-query merge."""
+        local = local_batch or self._native_local_batch
+        s, i = local(queries, k)
+        B = queries.shape[0]
+        gs = s.new_empty((self.world * B, k))
+        gi = i.new_empty((self.world * B, k))
+        self.dist.all_gather_into_tensor(gs, s.contiguous(), group=self.group)
+        self.dist.all_gather_into_tensor(gi, i.contiguous(), group=self.group)
+        return (merge_batch or merge_topk_batch)(gs.view(self.world, B, k), gi.view(self.world, B, k), k)
+
+    def _native_local_batch(self, queries: torch.Tensor, k: int):
+        from circuit_rag.search import circuit_search_batch
+
+        s, i = circuit_search_batch(queries, self.index, k=min(k, self.index.N))
+        if i.shape[1] < k:
+            s = torch.cat([s, s.new_full((s.shape[0], k - s.shape[1]), float("-inf"))], dim=1)
+            i = torch.cat([i, i.new_full((i.shape[0], k - i.shape[1]), -1)], dim=1)
+        return s, i
 
 
 def init_process_group(backend: str = "nccl", timeout_s: float = 120.0):

@@ -530,7 +530,8 @@ static cudaError_t launch_rescore_t(const float* Q, const IndexView& ix, const B
 }
 
 cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, const float* Q, int B, int k,
-                                float* out_scores, int* out_ids, cudaStream_t st) {
+                                float* out_scores, int* out_ids, cudaStream_t st, cudaEvent_t ev_scan_begin,
+                                cudaEvent_t ev_scan_end) {
   cudaError_t e;
   if ((e = cudaMemsetAsync(bw.theta, 0, sizeof(uint32_t) * B, st)) != cudaSuccess) return e;
   if ((e = cudaMemsetAsync(bw.cand_count, 0, sizeof(int) * B, st)) != cudaSuccess) return e;
@@ -560,9 +561,11 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   alignas(64) unsigned char qmap[128];
   if (!make_rows_tensor_map(Q, B, ix.D, qmap)) return cudaErrorInvalidValue;
   const int max_pairs = bw.sms / 2;
+  if (ev_scan_begin && (e = cudaEventRecord(ev_scan_begin, st)) != cudaSuccess) return e;
   e = (k <= 16) ? launch_batch_scan_t<16>(qmap, bw.tmap, P, max_pairs, st)
                 : launch_batch_scan_t<32>(qmap, bw.tmap, P, max_pairs, st);
   if (e != cudaSuccess) return e;
+  if (ev_scan_end && (e = cudaEventRecord(ev_scan_end, st)) != cudaSuccess) return e;
   const int vpl = (ix.D / 4 + 31) / 32;
   switch (vpl) {
     case 1: return launch_rescore_t<1>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);

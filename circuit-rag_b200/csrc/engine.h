@@ -118,7 +118,8 @@ bool make_leaf_tensor_map(const float* leaf, int N, int D, void* out_map);
 cudaError_t launch_max_row_norm(const float* leaf, int N, int D, unsigned int* out_key, int sms, cudaStream_t st);
 // queries [B, D] (device) -> out_scores / out_ids [B, k], original ids, (score desc, row asc).
 cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, const float* Q, int B, int k,
-                                float* out_scores, int* out_ids, cudaStream_t st);
+                                float* out_scores, int* out_ids, cudaStream_t st, cudaEvent_t ev_scan_begin,
+                                cudaEvent_t ev_scan_end);
 
 int scan_smem_bytes(int D);
 int sm_count(int device);

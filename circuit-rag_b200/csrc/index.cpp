@@ -523,7 +523,7 @@ int circuit_index_opaque::ensure_batch(int B) {
 }
 
 int circuit_index_opaque::search_batch_async(const float* dq, int B, int k, float* dscores, int* dids,
-                                             cudaStream_t st) {
+                                             cudaStream_t st, cudaEvent_t ev0, cudaEvent_t ev1) {
   if (B < 1) { set_error("num_queries must be >= 1"); return CIRCUIT_ERR_ARG; }
   if (k < 1 || k > cb::BATCH_MAX_K) {
     set_error("batched search supports 1 <= k <= " + std::to_string(cb::BATCH_MAX_K));
@@ -540,7 +540,7 @@ int circuit_index_opaque::search_batch_async(const float* dq, int B, int k, floa
   int rc = ensure_batch(B);
   if (rc != CIRCUIT_OK) return rc;
   if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice")) return CIRCUIT_ERR_CUDA;
-  cudaError_t e = cb::launch_batch_search(view, bw, dq, B, k, dscores, dids, st);
+  cudaError_t e = cb::launch_batch_search(view, bw, dq, B, k, dscores, dids, st, ev0, ev1);
   last_stream = st;
   if (e != cudaSuccess) { set_error(std::string("batch launch: ") + cudaGetErrorString(e)); return CIRCUIT_ERR_CUDA; }
   return CIRCUIT_OK;
@@ -550,9 +550,11 @@ int circuit_index_opaque::search_batch_async(const float* dq, int B, int k, floa
 extern "C" {
 
 int circuit_search_batch_async(circuit_index_t index, const float* dev_queries, int num_queries, int k,
-                               float* dev_out_scores, int* dev_out_ids, void* stream) {
+                               float* dev_out_scores, int* dev_out_ids, void* stream, void* ev_scan_begin,
+                               void* ev_scan_end) {
   if (!index) return CIRCUIT_ERR_NULL;
-  return index->search_batch_async(dev_queries, num_queries, k, dev_out_scores, dev_out_ids, (cudaStream_t)stream);
+  return index->search_batch_async(dev_queries, num_queries, k, dev_out_scores, dev_out_ids, (cudaStream_t)stream,
+                                   (cudaEvent_t)ev_scan_begin, (cudaEvent_t)ev_scan_end);
 }
 
 int circuit_batch_overflow(circuit_index_t index, int* out_count) {

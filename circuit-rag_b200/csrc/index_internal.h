@@ -64,6 +64,7 @@ struct circuit_index_opaque {
                       circuit_trace_t* trace);
   void fill_trace(const cb::SearchCtrl& c, circuit_trace_ex_t* t) const;
   int ensure_batch(int B);
-  int search_batch_async(const float* dq, int B, int k, float* dscores, int* dids, cudaStream_t st);
+  int search_batch_async(const float* dq, int B, int k, float* dscores, int* dids, cudaStream_t st,
+                         cudaEvent_t ev_scan_begin = nullptr, cudaEvent_t ev_scan_end = nullptr);
   static float key_to_float(uint32_t k);
 };

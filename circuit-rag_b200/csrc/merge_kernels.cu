@@ -40,9 +40,63 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge_topk(const float* __res
   }
 }
 
+// One CTA per query; candidate j of query q is at [(j / k_in) * qstride + q * k_in + j % k_in].
+__global__ void __launch_bounds__(MERGE_THREADS) k_merge_topk_batch(const float* __restrict__ scores,
+                                                                      const int* __restrict__ ids, int world, int k_in,
+                                                                      size_t qstride, int k, int selN,
+                                                                      float* __restrict__ out_scores,
+                                                                      int* __restrict__ out_ids) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int n = world * k_in;
+  unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem);
+  unsigned long long* sel = cand + n;
+  SelectScratch* scratch = reinterpret_cast<SelectScratch*>(sel + selN);
+  const int q = blockIdx.x;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const size_t at = (size_t)(j / k_in) * qstride + (size_t)q * k_in + (size_t)(j % k_in);
+    const int id = ids[at];
+    cand[j] = id >= 0 ? pack_cand(f2key(scores[at]), (uint32_t)id) : 0ull;
+  }
+  __syncthreads();
+  block_select_topk<false>(cand, n, k, sel, selN, scratch);
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const unsigned long long c = sel[i];
+    out_scores[(size_t)q * k + i] = c ? key2f(cand_key(c)) : -INFINITY;
+    out_ids[(size_t)q * k + i] = c ? (int)cand_row(c) : -1;
+  }
+}
+
 }  // namespace cb
 
 extern "C" {
+
+int circuit_merge_topk_batch(const float* scores, const int* ids, int num_queries, int world, int k_in, int k,
+                             float* out_scores, int* out_ids, void* stream) {
+  if (!scores || !ids || !out_scores || !out_ids) {
+    cb::set_error("merge_topk_batch: null pointer");
+    return CIRCUIT_ERR_ARG;
+  }
+  if (num_queries < 1 || world < 1 || k_in < 1 || (int64_t)world * k_in > cb::MERGE_MAX_N || k < 1 ||
+      k > cb::KMAX) {
+    cb::set_error("merge_topk_batch: need num_queries >= 1, 1 <= world * k_in <= 16384, 1 <= k <= 256");
+    return CIRCUIT_ERR_ARG;
+  }
+  int selN = 1;
+  while (selN < k) selN <<= 1;
+  const int n = world * k_in;
+  const size_t smem = sizeof(unsigned long long) * (size_t)(n + selN) + sizeof(cb::SelectScratch) + 16;
+  static size_t configured = 0;
+  if (smem > 48 * 1024 && smem > configured) {
+    if (!cb::cuda_ok(
+            cudaFuncSetAttribute(cb::k_merge_topk_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+            "merge batch smem"))
+      return CIRCUIT_ERR_CUDA;
+    configured = smem;
+  }
+  cb::k_merge_topk_batch<<<num_queries, cb::MERGE_THREADS, smem, (cudaStream_t)stream>>>(
+      scores, ids, world, k_in, (size_t)num_queries * k_in, k, selN, out_scores, out_ids);
+  return cb::cuda_ok(cudaGetLastError(), "merge_topk_batch launch") ? CIRCUIT_OK : CIRCUIT_ERR_CUDA;
+}
 
 int circuit_merge_topk(const float* scores, const int* ids, int n, int k, float* out_scores, int* out_ids,
                        void* stream) {

@@ -158,9 +158,11 @@ int circuit_trace_decode(circuit_index_t index, const void* snapshot, int path, 
  * circuit_batch_overflow counts them and circuit_search_batch answers them
  * with the single-query search.
  * Asynchronous on `stream`; the first call per handle allocates its batch
- * workspace and synchronises once. */
+ * workspace and synchronises once.  ev_scan_begin / ev_scan_end (cudaEvent_t,
+ * optional) are recorded around the tensor-core scan kernel. */
 int circuit_search_batch_async(circuit_index_t index, const float* dev_queries, int num_queries, int k,
-                               float* dev_out_scores, int* dev_out_ids, void* stream);
+                               float* dev_out_scores, int* dev_out_ids, void* stream, void* ev_scan_begin,
+                               void* ev_scan_end);
 /* Queries of the last batch whose candidate list overflowed (synchronises its stream). */
 int circuit_batch_overflow(circuit_index_t index, int* out_count);
 /* Blocking host-buffer variant of circuit_search_batch_async (host_scores / host_ids [num_queries, k]). */

@@ -26,6 +26,14 @@ extern "C" {
 int circuit_merge_topk(const float* scores, const int* ids, int n, int k, float* out_scores, int* out_ids,
                        void* stream);
 
+/* Batched form for circuit_search_batch results: scores / ids hold `world`
+ * blocks of [num_queries, k_in] (the rank-major layout of an all-gather of each
+ * rank's [num_queries, k_in] result); writes out_scores / out_ids
+ * [num_queries, k], each row ordered by (score desc, id asc).  One CTA per
+ * query.  1 <= world * k_in <= 16384, 1 <= k <= CIRCUIT_MAX_K. */
+int circuit_merge_topk_batch(const float* scores, const int* ids, int num_queries, int world, int k_in, int k,
+                             float* out_scores, int* out_ids, void* stream);
+
 /* Host-only: assign roots to `world` ranks by longest-processing-time on their
  * leaf rows (heaviest root to the lightest rank).  root_to_rank[num_roots] is
  * written; rank_rows[world] (optional) receives each rank's total rows. */

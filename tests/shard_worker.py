@@ -16,7 +16,7 @@ def search_worker(rank, world, port, root, index_path, queries_path, out_path, k
     import torch
     import torch.distributed as dist
 
-    from circuit_rag.shard import ShardedSearcher, load_shard, merge_topk_host
+    from circuit_rag.shard import ShardedSearcher, load_shard, merge_topk_batch_host, merge_topk_host
     from oracle import oracle
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
@@ -45,7 +45,13 @@ def search_worker(rank, world, port, root, index_path, queries_path, out_path, k
         for q in Q:
             s, i = srch.search(torch.from_numpy(q), k=k)
             res.append({"scores": s.tolist(), "ids": i.tolist()})
-        result.update(ok=True, results=res, shard_rows=int(len(X)), shard_ids=gid.tolist())
+        def local_batch(qs, kk):
+            pairs = [local(q, kk, 0) for q in qs]
+            return torch.stack([a for a, _ in pairs]), torch.stack([b for _, b in pairs])
+
+        bs, bi = srch.search_batch(torch.from_numpy(Q), k=k, local_batch=local_batch, merge_batch=merge_topk_batch_host)
+        result.update(ok=True, results=res, shard_rows=int(len(X)), shard_ids=gid.tolist(),
+                      batch_results={"scores": bs.tolist(), "ids": bi.tolist()})
     except SystemExit:
         raise
     except Exception as e:  # the survivor of a lost rank lands here

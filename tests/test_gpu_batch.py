@@ -100,7 +100,7 @@ def test_batch_overflow_falls_back_to_single_query():
     s = torch.empty(4, 10, device=DEV)
     i = torch.empty(4, 10, dtype=torch.int32, device=DEV)
     rc = _native.lib().circuit_search_batch_async(handle, Q.data_ptr(), 4, 10, s.data_ptr(), i.data_ptr(),
-                                                  torch.cuda.current_stream().cuda_stream)
+                                                  torch.cuda.current_stream().cuda_stream, None, None)
     assert rc == 0
     n_over = ctypes.c_int(-1)
     assert _native.lib().circuit_batch_overflow(handle, ctypes.byref(n_over)) == 0
@@ -136,10 +136,10 @@ def test_batch_rejects_unsupported():
     s = torch.empty(4, 33, device=DEV)
     i = torch.empty(4, 33, dtype=torch.int32, device=DEV)
     rc = _native.lib().circuit_search_batch_async(index.native_handle(), Q.data_ptr(), 4, 33, s.data_ptr(),
-                                                  i.data_ptr(), None)
+                                                  i.data_ptr(), None, None, None)
     assert rc == -7
     X2 = _unit_rows(300, 392, 33)
     index2 = build_circuit_index(X2, num_roots=2, children_per_root=2, rank=2, device=DEV)
     rc = _native.lib().circuit_search_batch_async(index2.native_handle(), X2.data_ptr(), 4, 10, s.data_ptr(),
-                                                  i.data_ptr(), None)
+                                                  i.data_ptr(), None, None, None)
     assert rc == -7

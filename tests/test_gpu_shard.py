@@ -6,8 +6,8 @@ import numpy as np
 import pytest
 import torch
 
-from circuit_rag import build_circuit_index, circuit_search
-from circuit_rag.shard import load_shard, merge_topk, merge_topk_host
+from circuit_rag import build_circuit_index, circuit_search, circuit_search_batch
+from circuit_rag.shard import load_shard, merge_topk, merge_topk_batch, merge_topk_batch_host, merge_topk_host
 from circuit_rag.synthetic import WORKLOADS
 from oracle import oracle
 
@@ -46,3 +46,39 @@ def test_shards_merge_to_brute_force(tmp_path, world):
                 I.append(torch.cat([i, i.new_full((k - len(i),), -1)]))
             ms, mi = merge_topk(torch.cat(S), torch.cat(I), k)
             oracle.check_topk((X.double() @ q.double()).cpu().numpy(), k, ms.cpu().numpy(), mi.cpu().numpy())
+
+
+@pytest.mark.parametrize("world,k_in,k", [(1, 10, 10), (3, 10, 10), (8, 32, 20)])
+def test_batched_merge_kernel_matches_host_merge(world, k_in, k):
+    g = torch.Generator().manual_seed(world * 100 + k)
+    B = 37
+    s = torch.randn(world, B, k_in, generator=g)
+    s[0, :, 3] = s[0, :, 2]  # exact ties across ids
+    i = torch.randint(0, 1 << 30, (world, B, k_in), generator=g, dtype=torch.int32)
+    i[:, :, -1] = -1  # empty slots
+    hs, hi = merge_topk_batch_host(s, i, k)
+    ds, di = merge_topk_batch(s.cuda(), i.cuda(), k)
+    assert torch.equal(di.cpu(), hi)
+    assert torch.equal(ds.cpu(), hs)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_batched_shards_merge_to_brute_force(tmp_path, world):
+    """Each shard answers the whole batch with circuit_search_batch; the
+    rank-major gathered results, merged per query, are the global top-k."""
+    w = WORKLOADS["spread-200k"]
+    X = w.corpus(0, 30000, device="cuda")
+    idx = build_circuit_index(X, num_roots=16, children_per_root=4, rank=8, device="cuda")
+    path = str(tmp_path / "b.circuit")
+    idx.save(path)
+    Q = w.query_batch(70, device="cuda")
+    S, I = [], []
+    for r in range(world):
+        sh = load_shard(path, r, world, device="cuda")
+        s, i = circuit_search_batch(Q, sh, 10)
+        S.append(s)
+        I.append(i)
+    ms, mi = merge_topk_batch(torch.stack(S), torch.stack(I), 10)
+    exact = (Q.double() @ X.double().T).cpu().numpy()
+    for b in range(Q.shape[0]):
+        oracle.check_topk(exact[b], 10, ms[b].cpu().numpy(), mi[b].cpu().numpy())

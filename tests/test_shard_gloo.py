@@ -105,6 +105,10 @@ def test_sharded_search_is_exact(index_file, tmp_path, world):
         for r in res:  # every rank returns the same global answer
             oracle.check_topk(exact, 10, r["results"][qi]["scores"], r["results"][qi]["ids"])
         assert res[0]["results"][qi]["ids"] == res[-1]["results"][qi]["ids"]
+        # the batched path (one all-gather of [B, k], per-query merge) gives the same answers
+        for r in res:
+            assert r["batch_results"]["ids"][qi] == r["results"][qi]["ids"]
+            oracle.check_topk(exact, 10, r["batch_results"]["scores"][qi], r["batch_results"]["ids"][qi])
 
 
 def test_lost_rank_becomes_an_error_not_a_hang(index_file, tmp_path):
