@@ -68,6 +68,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=4096, help="queries per batch of the batched search (0: skip it)")
     ap.add_argument("--batch-steps", type=int, default=3)
     ap.add_argument("--batch-warmup", type=int, default=2)
+    ap.add_argument("--tf32-seconds", type=float, default=2.0, help="length of the sustained cuBLAS tf32 loop")
     return ap.parse_args()
 
 
@@ -349,7 +350,7 @@ def run_batched(args, w, idx, dev, world, rank, n_total, n_local, start, k, D):
         e2e_s = float(t.item())
         api = "circuit_search_batch_async + NCCL all-gather + circuit_merge_topk_batch"
 
-    burst, peak = tf32_gemm_peak(dev)  # TFLOP/s
+    burst, peak = tf32_gemm_peak(dev, args.tf32_seconds)  # TFLOP/s
     flops = 2.0 * Bq * n_local * D
     achieved = flops / (scan_ms * 1e-3) / 1e12
     return {
