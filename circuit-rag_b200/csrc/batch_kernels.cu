@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   // full / acc_empty are used in the even CTA only; empty / acc_full in both
-  // (multicast commits).
+  // (the even CTA's MMA thread commits to its own and to the odd CTA's copy).
   __shared__ uint64_t full[BATCH_MAX_STAGES], empty[BATCH_MAX_STAGES], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -171,6 +171,8 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
   const uint32_t tmem = tmem_base;
   const uint32_t lead_full = tc::mapa_shared(smem_u32(&full[0]), 0);
   const uint32_t lead_acc_empty = tc::mapa_shared(smem_u32(&acc_empty[0]), 0);
+  const uint32_t empty0 = tc::mapa_shared(smem_u32(&empty[0]), 0), empty1 = tc::mapa_shared(smem_u32(&empty[0]), 1);
+  const uint32_t accf0 = tc::mapa_shared(smem_u32(&acc_full[0]), 0), accf1 = tc::mapa_shared(smem_u32(&acc_full[0]), 1);
 
   if (warp == 4) {
     // ---------------------------------------------------------- TMA producer (both CTAs)
@@ -224,9 +226,14 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
             for (int kk = 0; kk < 4; ++kk)
               tc::mma_tf32_ss_pair(acc, tc::sdesc_k_sw128(sa + (uint32_t)(kk * 32)),
                                    tc::sdesc_k_sw128(sa + (uint32_t)(A_BYTES + kk * 32)), idesc, (j | kk) ? 1u : 0u);
-            tc::commit_pair(&empty[s], 0x3);  // the stage refills once these MMAs have read it
+            // both CTAs' stage s refills once these MMAs have read it
+            tc::commit_pair(empty0 + 8u * (uint32_t)s);
+            tc::commit_pair(empty1 + 8u * (uint32_t)s);
           }
-          if (ok) tc::commit_pair(&acc_full[b], 0x3);
+          if (ok) {
+            tc::commit_pair(accf0 + 8u * (uint32_t)b);
+            tc::commit_pair(accf1 + 8u * (uint32_t)b);
+          }
         }
       }
     }

@@ -1,8 +1,9 @@
 // Shared device helpers for the circuit-b200 search kernels (sm_100a only).
 //
 // * mbarrier + 1-D bulk TMA (cp.async.bulk) wrappers used to stage leaf tiles,
-//   centroids and rank-r bases into shared memory.  No cluster multicast is used
-//   anywhere: every copy reads this GPU's own memory into its own CTA.
+//   centroids and rank-r bases into shared memory.  Every copy reads this
+//   GPU's own memory into the issuing CTA's shared memory (the batched scan's
+//   CTA-pair loads only route their completion to the even CTA's barrier).
 // * bounded waits: every spin on an mbarrier gives up after WAIT_LIMIT_NS of
 //   %globaltimer time, records an error bit in the per-query control block and
 //   returns false, so a stuck copy can never hang the GPU.

@@ -167,14 +167,11 @@ __device__ __forceinline__ void mma_tf32_ss_pair(uint32_t d_tmem, uint64_t a_des
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// Arrive on the mbarrier at this offset in every CTA of `cta_mask` once the
-// pair's previously issued tcgen05 ops completed.
-__device__ __forceinline__ void commit_pair(uint64_t* bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"(cta_mask)
-      : "memory");
+// Arrive on an mbarrier of either CTA of the pair (cluster address, from
+// mapa_shared) once the pair's previously issued tcgen05 ops completed.
+__device__ __forceinline__ void commit_pair(uint32_t bar_cluster_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr)
+               : "memory");
 }
 // 2-D tiled TMA load into this CTA's shared memory whose completion is counted
 // on an mbarrier of the pair's even CTA (cluster address).
