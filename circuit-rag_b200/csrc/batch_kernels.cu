@@ -573,11 +573,18 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
                 : launch_batch_scan_t<32>(qmap, bw.tmap, P, max_pairs, st);
   if (e != cudaSuccess) return e;
   if (ev_scan_end && (e = cudaEventRecord(ev_scan_end, st)) != cudaSuccess) return e;
-  const int vpl = (ix.D / 4 + 31) / 32;
-  switch (vpl) {
+  // float4 registers per lane for the query (the per-lane FMA order does not
+  // depend on this bucket, so scores match the single-query scan bit for bit)
+  const int v = (ix.D / 4 + 31) / 32;
+  switch (v <= 1 ? 1 : v <= 2 ? 2 : v <= 3 ? 3 : v <= 4 ? 4 : v <= 6 ? 6 : v <= 8 ? 8 : v <= 12 ? 12 : 16) {
     case 1: return launch_rescore_t<1>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
     case 2: return launch_rescore_t<2>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
-    default: return launch_rescore_t<3>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
+    case 3: return launch_rescore_t<3>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
+    case 4: return launch_rescore_t<4>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
+    case 6: return launch_rescore_t<6>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
+    case 8: return launch_rescore_t<8>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
+    case 12: return launch_rescore_t<12>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
+    default: return launch_rescore_t<16>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
   }
 }
 

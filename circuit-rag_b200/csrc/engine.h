@@ -94,7 +94,7 @@ cudaError_t launch_flat_scan(const float* leaf, int D, int N, const float* q, in
                              float* out_scores, int* out_ids, cudaStream_t stream);
 
 // ---- batched search (batch_kernels.cu) ----
-constexpr int BATCH_MAX_DIM = 384;   // 128 query rows of D fp32 columns + 2 x 64 accumulator columns in TMEM
+constexpr int BATCH_MAX_DIM = 2048;  // the rescoring keeps the query in registers (16 float4 per lane)
 constexpr int BATCH_MAX_K = 32;
 constexpr int BATCH_CAND_CAP = 16384;  // candidate rows appended per query
 

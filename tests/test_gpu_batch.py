@@ -57,6 +57,7 @@ def test_batch_many_ties_within_capacity():
     ("mixed-100m", 30_000, 384),
     ("clustered-50k", 20_011, 128),
     (None, 9_000, 100),
+    (None, 6_000, 1028),
 ])
 @pytest.mark.parametrize("k", [1, 10, 32])
 def test_batch_matches_single_query_and_oracle(name, n, dim, k):
@@ -138,8 +139,7 @@ def test_batch_rejects_unsupported():
     rc = _native.lib().circuit_search_batch_async(index.native_handle(), Q.data_ptr(), 4, 33, s.data_ptr(),
                                                   i.data_ptr(), None, None, None)
     assert rc == -7
-    X2 = _unit_rows(300, 392, 33)
-    index2 = build_circuit_index(X2, num_roots=2, children_per_root=2, rank=2, device=DEV)
-    rc = _native.lib().circuit_search_batch_async(index2.native_handle(), X2.data_ptr(), 4, 10, s.data_ptr(),
+    # a query pointer that is not 16-byte aligned is rejected before any launch
+    rc = _native.lib().circuit_search_batch_async(index.native_handle(), Q.data_ptr() + 4, 2, 10, s.data_ptr(),
                                                   i.data_ptr(), None, None, None)
-    assert rc == -7
+    assert rc == -2
