@@ -133,8 +133,9 @@ def circuit_search_batch(queries: torch.Tensor, index: CircuitIndex, k: int = 10
     results equal B calls of circuit_search: a tf32 tcgen05 pass over every
     leaf row keeps each query's rows within a rigorous error band of its running
     k-th best, and those rows are rescored exactly in fp32.  Returns (scores
-    [B, k] float32 descending, original ids [B, k] int32).  Needs dim <= 2048,
-    dim % 4 == 0 and 1 <= k <= 32.  A query whose candidate list overflows
+    [B, k] float32 descending, original ids [B, k] int32).  k <= 32 runs on the
+    tensor cores; 32 < k <= 256 is answered query by query by the single-query
+    path (same results).  A query whose candidate list overflows
     (more than 8192 rows inside the band, e.g. thousands of near-identical
     rows) is answered by circuit_search."""
     if queries.ndim != 2 or queries.shape[1] != index.dim:
@@ -143,8 +144,8 @@ def circuit_search_batch(queries: torch.Tensor, index: CircuitIndex, k: int = 10
         raise RuntimeError("circuit-b200 searches run on a CUDA device (no CPU path); load or build the index "
                            "with device='cuda'")
     k = min(int(k), index.N)
-    if k < 1 or k > _native.CIRCUIT_BATCH_MAX_K:
-        raise ValueError(f"batched k must be in [1, {_native.CIRCUIT_BATCH_MAX_K}]")
+    if k < 1 or k > _native.CIRCUIT_MAX_K:
+        raise ValueError(f"k must be in [1, {_native.CIRCUIT_MAX_K}]")
     B = queries.shape[0]
     dev = index.leaf_vectors.device
     queries = queries.to(device=dev, dtype=torch.float32).contiguous()
@@ -161,7 +162,9 @@ def circuit_search_batch(queries: torch.Tensor, index: CircuitIndex, k: int = 10
                                                       ids.data_ptr(), stream.cuda_stream, None, None)
         _native.check(rc, "circuit_search_batch")
         n_over = ctypes.c_int(0)
-        _native.check(_native.lib().circuit_batch_overflow(handle, ctypes.byref(n_over)), "circuit_batch_overflow")
+        if k <= _native.CIRCUIT_BATCH_MAX_K:
+            _native.check(_native.lib().circuit_batch_overflow(handle, ctypes.byref(n_over)),
+                          "circuit_batch_overflow")
         if n_over.value:
             for q in torch.nonzero(ids[:, 0] == -2).flatten().tolist():
                 s1, i1, _ = circuit_search(queries[q], index, k)

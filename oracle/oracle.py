@@ -134,6 +134,15 @@ def torch_flat_search(X, q, k):
     return torch.topk(X @ q, k)
 
 
+def torch_batch_flat_search(X, Q, k):
+    """Batched form of the same brute force, ``topk(Q @ X.T, k, dim=1)`` (the
+    reference's exactness test computes its truth this way per query,
+    tests/test_exact.py:26).  Used for the timed CPU baseline of batches."""
+    import torch
+
+    return torch.topk(Q @ X.T, k, dim=1)
+
+
 # ------------------------------------------------------------------ reference pipeline pieces
 def seed_threshold(ix, q: np.ndarray, k: int, f64: bool = False) -> Tuple[float, int]:
     """reference search.py:26-41 -> (T, best_root)."""

@@ -131,15 +131,27 @@ def test_batch_rejects_unsupported():
     index = build_circuit_index(X, num_roots=2, children_per_root=2, rank=2, device=DEV)
     Q = _unit_rows(4, 64, 32)
     with pytest.raises(ValueError):
-        circuit_search_batch(Q, index, 33)
+        circuit_search_batch(Q, index, 257)
     with pytest.raises(ValueError):
         circuit_search_batch(Q[:, :32], index, 10)
-    s = torch.empty(4, 33, device=DEV)
-    i = torch.empty(4, 33, dtype=torch.int32, device=DEV)
-    rc = _native.lib().circuit_search_batch_async(index.native_handle(), Q.data_ptr(), 4, 33, s.data_ptr(),
+    s = torch.empty(4, 257, device=DEV)
+    i = torch.empty(4, 257, dtype=torch.int32, device=DEV)
+    rc = _native.lib().circuit_search_batch_async(index.native_handle(), Q.data_ptr(), 4, 257, s.data_ptr(),
                                                   i.data_ptr(), None, None, None)
     assert rc == -7
     # a query pointer that is not 16-byte aligned is rejected before any launch
     rc = _native.lib().circuit_search_batch_async(index.native_handle(), Q.data_ptr() + 4, 2, 10, s.data_ptr(),
                                                   i.data_ptr(), None, None, None)
     assert rc == -2
+
+
+def test_batch_large_k_matches_single_query():
+    """k = 100 (the zipf-10m configuration's k) is beyond the tensor-core path's
+    per-thread top-k; the batched call answers query by query, same results."""
+    w = WORKLOADS["zipf-10m"]
+    X = w.corpus(0, 40_000, device=DEV)
+    index = build_circuit_index(X, num_roots=32, children_per_root=8, rank=16, device=DEV)
+    Q = w.query_batch(24, device=DEV)
+    scores, ids = circuit_search_batch(Q, index, 100)
+    assert scores.shape == (24, 100)
+    _check_batch(X, Q, index, 100, scores, ids)
