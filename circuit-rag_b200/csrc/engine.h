@@ -84,6 +84,15 @@ cudaError_t launch_prepare_roots(const IndexView& ix, double* root_cn, double* r
 cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float* q, int k, int hierarchical,
                           float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
                           cudaEvent_t ev_scan0, cudaEvent_t ev_scan1);
+// The hierarchical search in two phases, so that shards can exchange their seed
+// thresholds in between: seed = reset + root scan + seed scan (writes the seed
+// k-th best score to T_export, -inf if the seed root has fewer than k rows);
+// finish = bounds + main scan with threshold max(own seed, *T_ext).
+cudaError_t launch_search_seed(const IndexView& ix, const Workspace& ws, const float* q, int k, float* T_export,
+                               cudaStream_t stream);
+cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const float* q, int k, const float* T_ext,
+                                 float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
+                                 cudaEvent_t ev_scan0, cudaEvent_t ev_scan1);
 
 // Flat exact top-k of leaf[0..N) . q with caller-provided scratch: ctrl (its
 // first CTRL_RESET_BYTES zeroed by the caller), range = {0, 0, N, -1},

@@ -670,6 +670,48 @@ int circuit_search_device(circuit_index_t index, const float* dev_query, int k, 
   return index->search_blocking(dev_query, false, k, dev_out_scores, dev_out_ids, trace);
 }
 
+int circuit_search_seed_async(circuit_index_t index, const float* dev_query, int k, float* dev_threshold_out,
+                              void* stream) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  if (k < 1 || k > cb::KMAX) { set_error("k must be in [1, " + std::to_string(cb::KMAX) + "]"); return CIRCUIT_ERR_ARG; }
+  if (!dev_query || !dev_threshold_out || ((uintptr_t)dev_query & 15)) {
+    set_error("null or misaligned pointer");
+    return CIRCUIT_ERR_ARG;
+  }
+  if (!cuda_ok(cudaSetDevice(index->device), "cudaSetDevice")) return CIRCUIT_ERR_CUDA;
+  cudaStream_t st = (cudaStream_t)stream;
+  index->have_host_ctrl = false;
+  cudaError_t e = cb::launch_search_seed(index->view, index->ws, dev_query, k, dev_threshold_out, st);
+  index->last_stream = st;
+  index->last_path = 1;
+  index->last_k = k;
+  if (e != cudaSuccess) { set_error(std::string("seed launch: ") + cudaGetErrorString(e)); return CIRCUIT_ERR_CUDA; }
+  return CIRCUIT_OK;
+}
+
+int circuit_search_finish_async(circuit_index_t index, const float* dev_query, int k, const float* dev_threshold_in,
+                                float* dev_out_scores, int* dev_out_ids, int64_t* dev_out_rows, void* stream,
+                                void* ev_scan_begin, void* ev_scan_end) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  if (k < 1 || k > cb::KMAX) { set_error("k must be in [1, " + std::to_string(cb::KMAX) + "]"); return CIRCUIT_ERR_ARG; }
+  if (!dev_query || !dev_out_scores || ((uintptr_t)dev_query & 15)) {
+    set_error("null or misaligned pointer");
+    return CIRCUIT_ERR_ARG;
+  }
+  if (k != index->last_k || index->last_path != 1) {
+    set_error("circuit_search_finish_async must follow circuit_search_seed_async with the same k");
+    return CIRCUIT_ERR_ARG;
+  }
+  if (!cuda_ok(cudaSetDevice(index->device), "cudaSetDevice")) return CIRCUIT_ERR_CUDA;
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = cb::launch_search_finish(index->view, index->ws, dev_query, k, dev_threshold_in, dev_out_scores,
+                                           dev_out_ids, (long long*)dev_out_rows, st, (cudaEvent_t)ev_scan_begin,
+                                           (cudaEvent_t)ev_scan_end);
+  index->last_stream = st;
+  if (e != cudaSuccess) { set_error(std::string("finish launch: ") + cudaGetErrorString(e)); return CIRCUIT_ERR_CUDA; }
+  return CIRCUIT_OK;
+}
+
 int circuit_search_async(circuit_index_t index, const float* dev_query, int k, int64_t min_hierarchy_n,
                          float* dev_out_scores, int* dev_out_ids, int64_t* dev_out_rows, void* stream,
                          void* ev_scan_begin, void* ev_scan_end) {

@@ -57,6 +57,7 @@ struct ScanParams {
   int merge_seed;                             // final: also merge ctrl seed list
   unsigned long long* seed_list;              // [k]
   uint32_t* seed_T_key;
+  float* T_export;                            // seed mode: the seed threshold as a float (optional)
   float* out_scores;
   int* out_ids;
   long long* out_rows;
@@ -357,6 +358,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       const uint32_t T = (cnt_sel == k) ? cand_key(sel[k - 1]) : 0u;
       *P.seed_T_key = T;
       if (T > *P.theta_key) *P.theta_key = T;
+      if (P.T_export) *P.T_export = T ? key2f(T) : -INFINITY;
     }
   } else {
     for (int i = tid; i < k; i += blockDim.x) {
@@ -466,9 +468,12 @@ __host__ __device__ inline BoundsLayout bounds_layout(int D, int rank, int chunk
   return L;
 }
 
+// T_ext (optional): a threshold from outside this index (the max of all shards'
+// seed thresholds); the bounds and the main scan use max(own seed, T_ext).
 __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, const float* __restrict__ q,
                                                                SearchCtrl* ctrl, const float* __restrict__ root_dots,
-                                                               int4* __restrict__ main_ranges, int chunk_rows) {
+                                                               int4* __restrict__ main_ranges, int chunk_rows,
+                                                               const float* __restrict__ T_ext) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int D = ix.D, r = ix.rank;
@@ -490,7 +495,16 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
   }
   __syncthreads();
 
-  const uint32_t Tkey = ctrl->seed_T_key;
+  uint32_t Tkey = ctrl->seed_T_key;
+  if (T_ext) {
+    const float te = *T_ext;
+    if (te > -INFINITY) {
+      const uint32_t ek = f2key(te);
+      if (ek > Tkey) Tkey = ek;
+      // the main scan starts from the raised threshold (it runs after this kernel)
+      if (blockIdx.x == 0 && threadIdx.x == 0) atomicMax(&ctrl->theta_key, ek);
+    }
+  }
   const double T = Tkey ? (double)key2f(Tkey) : -INFINITY;
   const int best = ctrl->best_root;
   const double gD = gamma_n(D);
@@ -787,12 +801,8 @@ cudaError_t launch_prepare_roots(const IndexView& ix, double* root_cn, double* r
   return cudaGetLastError();
 }
 
-cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float* q, int k, int hierarchical,
-                          float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
-                          cudaEvent_t ev_scan0, cudaEvent_t ev_scan1) {
-  cudaError_t e = cudaMemsetAsync(ws.ctrl, 0, CTRL_RESET_BYTES, stream);
-  if (e != cudaSuccess) return e;
-  const int vpl = vpl_bucket(ix.D4);
+static ScanParams scan_params(const IndexView& ix, const Workspace& ws, const float* q, int k, float* out_scores,
+                              int* out_ids, long long* out_rows) {
   ScanParams P{};
   P.leaf = ix.leaf;
   P.q = q;
@@ -802,53 +812,74 @@ cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float*
   P.D4 = ix.D4;
   P.row_bytes = ix.D * 4;
   P.k = k;
-  P.stages = stages_for(vpl, P.row_bytes);
+  P.stages = stages_for(vpl_bucket(ix.D4), P.row_bytes);
   P.seed_list = ws.ctrl->seed_list;
   P.seed_T_key = &ws.ctrl->seed_T_key;
   P.out_scores = out_scores;
   P.out_ids = out_ids;
   P.out_rows = out_rows;
   P.original_ids = ix.original_ids;
+  return P;
+}
 
-  if (hierarchical) {
-    k_root_scan<<<(ix.R + ROOT_SCAN_WARPS - 1) / ROOT_SCAN_WARPS, ROOT_SCAN_WARPS * 32, 0, stream>>>(
-        ix, q, ws.ctrl, ws.root_dots, ws.seed_ranges, k);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    ScanParams S = P;
-    S.ranges = ws.seed_ranges;
-    S.packed_counts = &ws.ctrl->seed_packed;
-    S.done = &ws.ctrl->seed_done;
-    S.final_mode = 0;
-    S.merge_seed = 0;
-    if ((e = launch_scan(S, ws.scan_grid, stream)) != cudaSuccess) return e;
+cudaError_t launch_search_seed(const IndexView& ix, const Workspace& ws, const float* q, int k, float* T_export,
+                               cudaStream_t stream) {
+  cudaError_t e = cudaMemsetAsync(ws.ctrl, 0, CTRL_RESET_BYTES, stream);
+  if (e != cudaSuccess) return e;
+  k_root_scan<<<(ix.R + ROOT_SCAN_WARPS - 1) / ROOT_SCAN_WARPS, ROOT_SCAN_WARPS * 32, 0, stream>>>(
+      ix, q, ws.ctrl, ws.root_dots, ws.seed_ranges, k);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  ScanParams S = scan_params(ix, ws, q, k, nullptr, nullptr, nullptr);
+  S.ranges = ws.seed_ranges;
+  S.packed_counts = &ws.ctrl->seed_packed;
+  S.done = &ws.ctrl->seed_done;
+  S.final_mode = 0;
+  S.merge_seed = 0;
+  S.T_export = T_export;
+  return launch_scan(S, ws.scan_grid, stream);
+}
 
-    const int chunk_rows = bounds_chunk_rows(ix.D, ix.rank);
-    const BoundsLayout BL = bounds_layout(ix.D, ix.rank, chunk_rows);
-    static int bounds_configured = 0;
-    if ((int)BL.total > bounds_configured) {
-      if ((e = cudaFuncSetAttribute(k_bounds, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BL.total)) !=
-          cudaSuccess)
-        return e;
-      bounds_configured = (int)BL.total;
-    }
-    int grid_b = (ix.R + BOUNDS_WARPS - 1) / BOUNDS_WARPS;
-    if (grid_b > 2 * ws.scan_grid) grid_b = 2 * ws.scan_grid;
-    k_bounds<<<grid_b, BOUNDS_WARPS * 32, BL.total, stream>>>(ix, q, ws.ctrl, ws.root_dots, ws.main_ranges,
-                                                               chunk_rows);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-
-    ScanParams M = P;
-    M.ranges = ws.main_ranges;
-    M.packed_counts = &ws.ctrl->main_packed;
-    M.done = &ws.ctrl->main_done;
-    M.final_mode = 1;
-    M.merge_seed = 1;
-    if (ev_scan0) cudaEventRecord(ev_scan0, stream);
-    e = launch_scan(M, ws.scan_grid, stream);
-    if (ev_scan1) cudaEventRecord(ev_scan1, stream);
-    return e;
+cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const float* q, int k, const float* T_ext,
+                                 float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
+                                 cudaEvent_t ev_scan0, cudaEvent_t ev_scan1) {
+  cudaError_t e;
+  const int chunk_rows = bounds_chunk_rows(ix.D, ix.rank);
+  const BoundsLayout BL = bounds_layout(ix.D, ix.rank, chunk_rows);
+  static int bounds_configured = 0;
+  if ((int)BL.total > bounds_configured) {
+    if ((e = cudaFuncSetAttribute(k_bounds, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BL.total)) !=
+        cudaSuccess)
+      return e;
+    bounds_configured = (int)BL.total;
   }
-  ScanParams F = P;
+  int grid_b = (ix.R + BOUNDS_WARPS - 1) / BOUNDS_WARPS;
+  if (grid_b > 2 * ws.scan_grid) grid_b = 2 * ws.scan_grid;
+  k_bounds<<<grid_b, BOUNDS_WARPS * 32, BL.total, stream>>>(ix, q, ws.ctrl, ws.root_dots, ws.main_ranges, chunk_rows,
+                                                             T_ext);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  ScanParams M = scan_params(ix, ws, q, k, out_scores, out_ids, out_rows);
+  M.ranges = ws.main_ranges;
+  M.packed_counts = &ws.ctrl->main_packed;
+  M.done = &ws.ctrl->main_done;
+  M.final_mode = 1;
+  M.merge_seed = 1;
+  if (ev_scan0) cudaEventRecord(ev_scan0, stream);
+  e = launch_scan(M, ws.scan_grid, stream);
+  if (ev_scan1) cudaEventRecord(ev_scan1, stream);
+  return e;
+}
+
+cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float* q, int k, int hierarchical,
+                          float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
+                          cudaEvent_t ev_scan0, cudaEvent_t ev_scan1) {
+  if (hierarchical) {
+    cudaError_t e = launch_search_seed(ix, ws, q, k, nullptr, stream);
+    if (e != cudaSuccess) return e;
+    return launch_search_finish(ix, ws, q, k, nullptr, out_scores, out_ids, out_rows, stream, ev_scan0, ev_scan1);
+  }
+  cudaError_t e = cudaMemsetAsync(ws.ctrl, 0, CTRL_RESET_BYTES, stream);
+  if (e != cudaSuccess) return e;
+  ScanParams F = scan_params(ix, ws, q, k, out_scores, out_ids, out_rows);
   F.ranges = ws.flat_range;
   F.packed_counts = ws.flat_packed;
   F.done = &ws.ctrl->main_done;

@@ -145,6 +145,24 @@ int circuit_last_trace(circuit_index_t index, circuit_trace_ex_t* out);
 int circuit_trace_snapshot_async(circuit_index_t index, void* dst, void* stream);
 int circuit_trace_decode(circuit_index_t index, const void* snapshot, int path, circuit_trace_ex_t* out);
 
+/* The hierarchical search in two phases, for a corpus sharded over several
+ * GPUs (no reference counterpart).  circuit_search_seed_async resets the
+ * handle's search state, scans the roots and the best root's rows, and writes
+ * this shard's seed threshold (k-th best score of k of its rows, -inf if the
+ * best root holds fewer than k rows) to dev_threshold_out[0] (float, device).
+ * The caller may replace it by the maximum over all shards (e.g. an NCCL
+ * all-reduce MAX): each shard's value is the k-th best of k real rows, so the
+ * maximum never exceeds the global k-th best score.  circuit_search_finish_async
+ * then prunes with max(own seed, dev_threshold_in[0]) (dev_threshold_in may be
+ * NULL) and writes this shard's top-k (empty slots -inf / -1 when fewer than k
+ * rows reach the threshold).  Both run on `stream`, in this order, with the
+ * same query and k and no other search on the handle in between. */
+int circuit_search_seed_async(circuit_index_t index, const float* dev_query, int k, float* dev_threshold_out,
+                              void* stream);
+int circuit_search_finish_async(circuit_index_t index, const float* dev_query, int k, const float* dev_threshold_in,
+                                float* dev_out_scores, int* dev_out_ids, int64_t* dev_out_rows, void* stream,
+                                void* ev_scan_begin, void* ev_scan_end);
+
 /* Batched exact top-k on the tensor cores (no reference counterpart: the
  * reference searches one query at a time).  dev_queries [num_queries, dim]
  * (device, 16-byte aligned) -> dev_out_scores / dev_out_ids [num_queries, k]
