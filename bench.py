@@ -12,7 +12,10 @@ each GPU builds and searches its own shard index; the N local top-k lists are
 merged after an NCCL all-gather (k scores + k ids per GPU per query).
 
 A step is one query: root scan -> seed scan -> bounds -> main leaf scan (fused
-top-k) on every GPU, then the all-gather merge.  `value` is queries/s of the
+top-k) on every GPU, then the all-gather merge.  At N > 1 the shards' seed
+thresholds are all-reduced (MAX) between the seed scan and the bounds, so every
+shard prunes with the best threshold any shard found (--no-threshold-exchange
+turns this off).  `value` is queries/s of the
 whole job (device time, CUDA events, max over ranks); `e2e` is the same metric
 through the public C ABI (circuit_search with host buffers: H2D query, search,
 D2H results per query) at N = 1, or the torch-level equivalent with an NCCL
@@ -69,6 +72,8 @@ def parse():
     ap.add_argument("--batch-steps", type=int, default=3)
     ap.add_argument("--batch-warmup", type=int, default=2)
     ap.add_argument("--tf32-seconds", type=float, default=2.0, help="length of the sustained cuBLAS tf32 loop")
+    ap.add_argument("--no-threshold-exchange", action="store_true",
+                    help="N > 1: prune each shard with its own seed threshold only")
     return ap.parse_args()
 
 
@@ -440,6 +445,22 @@ def main():
         for e in pair:
             e.record(stream)
 
+    exchange = world > 1 and not args.no_threshold_exchange
+    T_buf = torch.empty(1, device=dev)
+
+    def local_search(q, e0=None, e1=None):
+        """This shard's top-k of q; with the exchange, the shards' seed
+        thresholds are all-reduced (MAX) between the seed and finish phases."""
+        if not exchange:
+            _launch(handle, q, k, 0, scores, ids, None, stream, e0, e1)
+            return
+        assert L.circuit_search_seed_async(handle, q.data_ptr(), k, T_buf.data_ptr(), stream.cuda_stream) == 0
+        dist.all_reduce(T_buf, op=dist.ReduceOp.MAX)
+        assert L.circuit_search_finish_async(handle, q.data_ptr(), k, T_buf.data_ptr(), scores.data_ptr(),
+                                             ids.data_ptr(), None, stream.cuda_stream,
+                                             e0.cuda_event if e0 is not None else None,
+                                             e1.cuda_event if e1 is not None else None) == 0
+
     def one(i, timed):
         q = Q[i]
         if timed:
@@ -447,7 +468,7 @@ def main():
             e0, e1 = s_ev[i - warm]
         else:
             e0 = e1 = None
-        _launch(handle, q, k, 0, scores, ids, None, stream, e0, e1)
+        local_search(q, e0, e1)
         if world > 1:
             dist.all_gather_into_tensor(g_scores, scores)
             dist.all_gather_into_tensor(g_ids, ids)
@@ -487,7 +508,7 @@ def main():
     snap = torch.empty(_native.TRACE_SNAPSHOT_BYTES, dtype=torch.uint8, device=dev)
     main_rows, all_rows = [], []
     for i in range(warm, warm + steps):
-        _launch(handle, Q[i], k, 0, scores, ids, None, stream)
+        local_search(Q[i])
         L.circuit_trace_snapshot_async(handle, snap.data_ptr(), stream.cuda_stream)
         host = snap.cpu()
         raw = host.numpy().view(np.uint64)
@@ -566,7 +587,7 @@ def main():
         t0 = time.perf_counter()
         for j in range(e2e_steps):
             dq.copy_(hq[j], non_blocking=True)
-            _launch(handle, dq, k, 0, scores, ids, None, stream)
+            local_search(dq)
             dist.all_gather_into_tensor(g_scores, scores)
             dist.all_gather_into_tensor(g_ids, ids)
             ms, mi = merge_topk(g_scores, g_ids, k)
@@ -577,7 +598,9 @@ def main():
         e2e_s = torch.tensor([time.perf_counter() - t0], device=dev)
         dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
         e2e = {"value": e2e_steps / float(e2e_s.item()), "unit": "queries/s", "h2d_bytes_per_step": D * 4,
-               "d2h_bytes_per_step": k * 8, "api": "circuit_search_async + NCCL all-gather + circuit_merge_topk"}
+               "d2h_bytes_per_step": k * 8,
+               "api": ("circuit_search_seed_async + NCCL all-reduce(MAX) + circuit_search_finish_async"
+                       if exchange else "circuit_search_async") + " + NCCL all-gather + circuit_merge_topk"}
 
     batched = None
     if args.batch > 0:
@@ -613,7 +636,7 @@ def main():
                                                                                       len(lat_us) * 99 // 100)], 2),
             "pruned_leaf_fraction": round(1.0 - statistics.mean(all_rows) / n_local, 5),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": (4 if world == 1 else 5) * steps, "clocks": clocks,
-            "build_s": round(build_s, 1), "check": check, "batched": batched,
+            "build_s": round(build_s, 1), "check": check, "threshold_exchange": exchange, "batched": batched,
         }
         print(json.dumps(line), flush=True)
     idx.close()

@@ -96,6 +96,11 @@ def load_shard(filepath: str, rank: int, world: int, device: str = "cuda") -> Ci
                         dim=D, rank=r, device=device, **new)
 
 
+def _aligned(q: torch.Tensor) -> torch.Tensor:
+    q = q.to(torch.float32).contiguous()
+    return q if q.data_ptr() % 16 == 0 else q.clone()
+
+
 def merge_topk(scores: torch.Tensor, ids: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
     """Global top-k of gathered candidates on the device (circuit_merge_topk)."""
     scores = scores.to(torch.float32).contiguous()
@@ -171,13 +176,41 @@ class ShardedSearcher:
             i = torch.cat([i, i.new_full((k - len(i),), -1)])
         return s, i
 
-    def search(self, query: torch.Tensor, k: int = 10, min_hierarchy_n: int = 10000):
-        s, i = self._local(query, k, min_hierarchy_n)
+    def search(self, query: torch.Tensor, k: int = 10, min_hierarchy_n: int = 10000,
+               exchange_threshold: bool = False, local_seed: Optional[Callable] = None,
+               local_finish: Optional[Callable] = None):
+        """Global exact top-k of one query.  With exchange_threshold, every rank
+        first computes its shard's seed threshold, one all-reduce (MAX) makes
+        the largest of them every rank's pruning threshold (it never exceeds
+        the global k-th best score), then each rank finishes its search."""
+        if exchange_threshold:
+            T = (local_seed or self._native_seed)(query, k)
+            self.dist.all_reduce(T, op=self.dist.ReduceOp.MAX, group=self.group)
+            s, i = (local_finish or self._native_finish)(query, k, T)
+        else:
+            s, i = self._local(query, k, min_hierarchy_n)
         gs = s.new_empty(self.world * k)
         gi = i.new_empty(self.world * k)
         self.dist.all_gather_into_tensor(gs, s.contiguous(), group=self.group)
         self.dist.all_gather_into_tensor(gi, i.contiguous(), group=self.group)
         return self._merge(gs, gi, k)
+
+    def _native_seed(self, query: torch.Tensor, k: int) -> torch.Tensor:
+        T = torch.empty(1, dtype=torch.float32, device=query.device)
+        rc = _native.lib().circuit_search_seed_async(self.index.native_handle(), _aligned(query).data_ptr(), int(k),
+                                                     T.data_ptr(), torch.cuda.current_stream(query.device).cuda_stream)
+        _native.check(rc, "circuit_search_seed_async")
+        return T
+
+    def _native_finish(self, query: torch.Tensor, k: int, T: torch.Tensor):
+        s = torch.empty(k, dtype=torch.float32, device=query.device)
+        i = torch.empty(k, dtype=torch.int32, device=query.device)
+        rc = _native.lib().circuit_search_finish_async(self.index.native_handle(), _aligned(query).data_ptr(), int(k),
+                                                       T.data_ptr(), s.data_ptr(), i.data_ptr(), None,
+                                                       torch.cuda.current_stream(query.device).cuda_stream, None,
+                                                       None)
+        _native.check(rc, "circuit_search_finish_async")
+        return s, i
 
     def search_batch(self, queries: torch.Tensor, k: int = 10, local_batch: Optional[Callable] = None,
                      merge_batch: Optional[Callable] = None):

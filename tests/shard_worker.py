@@ -50,8 +50,30 @@ def search_worker(rank, world, port, root, index_path, queries_path, out_path, k
             return torch.stack([a for a, _ in pairs]), torch.stack([b for _, b in pairs])
 
         bs, bi = srch.search_batch(torch.from_numpy(Q), k=k, local_batch=local_batch, merge_batch=merge_topk_batch_host)
+
+        # threshold exchange: seed = k-th best of this shard's first rows (any k
+        # real rows qualify); finish = this shard's rows at or above the
+        # exchanged threshold, padded with empty slots
+        def seed(q, kk):
+            n0 = min(len(X), max(kk, 40))
+            s0 = np.sort(X[:n0].astype(np.float64) @ q.numpy().astype(np.float64))[::-1]
+            return torch.tensor([s0[kk - 1] if n0 >= kk else float("-inf")], dtype=torch.float32)
+
+        def finish(q, kk, T):
+            s, rows = oracle.brute_topk(X, q.numpy(), min(kk, len(X)))
+            keep = s >= float(T[0]) - 1e-6
+            out_s = torch.full((kk,), float("-inf"))
+            out_i = torch.full((kk,), -1, dtype=torch.int32)
+            out_s[:int(keep.sum())] = torch.from_numpy(s[keep]).float()
+            out_i[:int(keep.sum())] = torch.from_numpy(gid[rows[keep]]).int()
+            return out_s, out_i
+
+        ex = []
+        for q in Q:
+            s, i = srch.search(torch.from_numpy(q), k=k, exchange_threshold=True, local_seed=seed, local_finish=finish)
+            ex.append({"scores": s.tolist(), "ids": i.tolist()})
         result.update(ok=True, results=res, shard_rows=int(len(X)), shard_ids=gid.tolist(),
-                      batch_results={"scores": bs.tolist(), "ids": bi.tolist()})
+                      batch_results={"scores": bs.tolist(), "ids": bi.tolist()}, exchange_results=ex)
     except SystemExit:
         raise
     except Exception as e:  # the survivor of a lost rank lands here

@@ -82,3 +82,57 @@ def test_batched_shards_merge_to_brute_force(tmp_path, world):
     exact = (Q.double() @ X.double().T).cpu().numpy()
     for b in range(Q.shape[0]):
         oracle.check_topk(exact[b], 10, ms[b].cpu().numpy(), mi[b].cpu().numpy())
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_threshold_exchange_is_exact_and_prunes_no_less(tmp_path, world):
+    """Seed phase on every shard, the max of the shards' seed thresholds, finish
+    phase with it: the merged result is the exact global top-k, and no shard
+    scans more rows than it does with its own seed alone."""
+    import ctypes
+
+    from circuit_rag import _native
+
+    w = WORKLOADS["clustered-50k"]
+    X = w.corpus(0, 40000, device="cuda")
+    idx = build_circuit_index(X, num_roots=32, children_per_root=8, rank=8, device="cuda")
+    path = str(tmp_path / "c.circuit")
+    idx.save(path)
+    shards = [load_shard(path, r, world, device="cuda") for r in range(world)]
+    L = _native.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    Q = w.query_batch(12, device="cuda")
+    k = 10
+    rows_plain, rows_ex = 0, 0
+    tx = _native.TraceEx()
+    for q in Q:
+        exact = (X.double() @ q.double()).cpu().numpy()
+        # plain: every shard prunes with its own seed
+        for sh in shards:
+            s = torch.empty(k, device="cuda")
+            i = torch.empty(k, dtype=torch.int32, device="cuda")
+            assert L.circuit_search_async(sh.native_handle(), q.data_ptr(), k, 0, s.data_ptr(), i.data_ptr(), None, st,
+                                          None, None) == 0
+            assert L.circuit_last_trace(sh.native_handle(), ctypes.byref(tx)) == 0 and tx.device_error == 0
+            rows_plain += tx.vectors_scored
+        # exchange: seeds -> max -> finish
+        Ts = []
+        for sh in shards:
+            T = torch.empty(1, device="cuda")
+            assert L.circuit_search_seed_async(sh.native_handle(), q.data_ptr(), k, T.data_ptr(), st) == 0
+            Ts.append(T)
+        Tmax = torch.stack(Ts).max().reshape(1).contiguous()
+        assert float(Tmax) <= float(np.sort(exact)[-k]) + 1e-6  # never above the global k-th best
+        S, I = [], []
+        for sh, T in zip(shards, Ts):
+            s = torch.empty(k, device="cuda")
+            i = torch.empty(k, dtype=torch.int32, device="cuda")
+            assert L.circuit_search_finish_async(sh.native_handle(), q.data_ptr(), k, Tmax.data_ptr(), s.data_ptr(),
+                                                 i.data_ptr(), None, st, None, None) == 0
+            assert L.circuit_last_trace(sh.native_handle(), ctypes.byref(tx)) == 0 and tx.device_error == 0
+            rows_ex += tx.vectors_scored
+            S.append(s)
+            I.append(i)
+        ms, mi = merge_topk(torch.cat(S), torch.cat(I), k)
+        oracle.check_topk(exact, k, ms.cpu().numpy(), mi.cpu().numpy())
+    assert rows_ex <= rows_plain

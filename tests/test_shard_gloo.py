@@ -108,6 +108,8 @@ def test_sharded_search_is_exact(index_file, tmp_path, world):
         # the batched path (one all-gather of [B, k], per-query merge) gives the same answers
         for r in res:
             assert r["batch_results"]["ids"][qi] == r["results"][qi]["ids"]
+            # all-reduce(MAX) of the shards' seed thresholds, then the finish phase
+            assert r["exchange_results"][qi]["ids"] == r["results"][qi]["ids"]
             oracle.check_topk(exact, 10, r["batch_results"]["scores"][qi], r["batch_results"]["ids"][qi])
 
 
