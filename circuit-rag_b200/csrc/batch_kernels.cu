@@ -176,22 +176,25 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
 
   if (warp == 4) {
     // ---------------------------------------------------------- TMA producer (both CTAs)
+    // The stage index and its phase advance incrementally (no division in the loop).
     if (lane == 0) {
-      int c = 0;
+      int s = 0, c = 0;
+      uint32_t ph = 0;
       bool ok = true;
       for (int u = pair; u < P.units && ok; u += npairs) {
         const int qp = u % P.QP, slice = u / P.QP;
         const int qrow = qp * (2 * BQ) + (int)rank * BQ;
         const int r0 = slice * SLICE_ROWS, r1 = min(P.N, r0 + SLICE_ROWS);
         for (int row0 = r0; row0 < r1 && ok; row0 += BN) {
+          const int xrow = row0 + (int)rank * HALF_N;
           for (int j = 0; j < P.kb; ++j, ++c) {
-            const int s = c % S, f = c / S;
-            if (f > 0 && !mbar_wait(&empty[s], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) { ok = false; break; }
+            if (c >= S && !mbar_wait(&empty[s], ph ^ 1u, P.err, ERR_TIMEOUT_EMPTY)) { ok = false; break; }
             if (leader) mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * STAGE_BYTES));
             unsigned char* dst = smem + (size_t)s * STAGE_BYTES;
             const uint32_t bar = lead_full + 8u * (uint32_t)s;
             tc::tma_load_2d_pair(dst, &qmap, 32 * j, qrow, bar);
-            tc::tma_load_2d_pair(dst + A_BYTES, &xmap, 32 * j, row0 + (int)rank * HALF_N, bar);
+            tc::tma_load_2d_pair(dst + A_BYTES, &xmap, 32 * j, xrow, bar);
+            if (++s == S) { s = 0; ph ^= 1u; }
           }
         }
       }
@@ -201,39 +204,53 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
     }
   } else if (warp == 5) {
     // ---------------------------------------------------------- MMA issuer (even CTA)
-    if (leader && lane == 0) {
+    // The whole warp runs the loop and one elected lane issues: a lean issue
+    // loop matters, since one 2-SM MMA (M = N = 256, K = 8) takes only ~70 ns.
+    // Descriptors are formed once and advanced by adding (byte offset >> 4) to
+    // their start-address field (shared-memory addresses stay below 256 KB,
+    // so the 14-bit field never carries).
+    if (leader) {
       const uint32_t idesc = tc::idesc_tf32(2 * BQ, BN);
       const uint32_t sbase = smem_u32(smem);
-      int c = 0, it = 0;
+      const uint64_t dA0 = tc::sdesc_k_sw128(sbase), dB0 = tc::sdesc_k_sw128(sbase + A_BYTES);
+      int s = 0, it = 0;
+      uint32_t ph = 0;
       bool ok = true;
       for (int u = pair; u < P.units && ok; u += npairs) {
         const int slice = u / P.QP;
         const int r0 = slice * SLICE_ROWS, r1 = min(P.N, r0 + SLICE_ROWS);
         for (int row0 = r0; row0 < r1 && ok; row0 += BN, ++it) {
           const int b = it & 1, fb = it >> 1;
-          if (fb > 0 && !tc::mbar_wait_cluster(&acc_empty[b], (fb - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) {
+          // wait results are made warp-uniform: elect.sync needs every lane
+          if (fb > 0 &&
+              !__all_sync(FULL_MASK, tc::mbar_wait_cluster(&acc_empty[b], (fb - 1) & 1, P.err, ERR_TIMEOUT_EMPTY))) {
             ok = false;
             break;
           }
           tc::fence_after();
           const uint32_t acc = tmem + (uint32_t)(b * BN);
-          for (int j = 0; j < P.kb; ++j, ++c) {
-            const int s = c % S, f = c / S;
-            if (!mbar_wait(&full[s], f & 1, P.err, ERR_TIMEOUT_FULL)) { ok = false; break; }
+          for (int j = 0; j < P.kb; ++j) {
+            if (!__all_sync(FULL_MASK, mbar_wait(&full[s], ph, P.err, ERR_TIMEOUT_FULL))) { ok = false; break; }
             tc::fence_after();
-            const uint32_t sa = sbase + (uint32_t)(s * STAGE_BYTES);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              tc::mma_tf32_ss_pair(acc, tc::sdesc_k_sw128(sa + (uint32_t)(kk * 32)),
-                                   tc::sdesc_k_sw128(sa + (uint32_t)(A_BYTES + kk * 32)), idesc, (j | kk) ? 1u : 0u);
-            // both CTAs' stage s refills once these MMAs have read it
-            tc::commit_pair(empty0 + 8u * (uint32_t)s);
-            tc::commit_pair(empty1 + 8u * (uint32_t)s);
+            if (tc::elect_one()) {
+              const uint64_t off = (uint64_t)(((uint32_t)s * (uint32_t)STAGE_BYTES) >> 4);
+              const uint64_t a = dA0 + off, bq = dB0 + off;
+              tc::mma_tf32_ss_pair(acc, a, bq, idesc, j != 0 ? 1u : 0u);
+              tc::mma_tf32_ss_pair(acc, a + 2, bq + 2, idesc, 1u);
+              tc::mma_tf32_ss_pair(acc, a + 4, bq + 4, idesc, 1u);
+              tc::mma_tf32_ss_pair(acc, a + 6, bq + 6, idesc, 1u);
+              // both CTAs' stage s refills once these MMAs have read it
+              tc::commit_pair(empty0 + 8u * (uint32_t)s);
+              tc::commit_pair(empty1 + 8u * (uint32_t)s);
+            }
+            __syncwarp();
+            if (++s == S) { s = 0; ph ^= 1u; }
           }
-          if (ok) {
+          if (ok && tc::elect_one()) {
             tc::commit_pair(accf0 + 8u * (uint32_t)b);
             tc::commit_pair(accf1 + 8u * (uint32_t)b);
           }
+          __syncwarp();
         }
       }
     }

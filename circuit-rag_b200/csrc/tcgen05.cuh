@@ -91,6 +91,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst_smem, const CUtensorMap* m
       : "memory");
 }
 
+// One lane of a converged warp (the whole warp executes this).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile("{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.u32 %0, 1, 0, P;\n\t}" : "=r"(pred));
+  return pred != 0;
+}
+
 // ---- CTA pair (cluster of 2) forms: one MMA over both SMs' TMEM / shared memory
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
