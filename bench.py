@@ -395,7 +395,7 @@ def run_batched(args, w, idx, dev, world, rank, n_total, n_local, start, k, D):
         "check": {"checked_queries": nchk, "mismatches": bad},
         "e2e": {"value": round(Bq / e2e_s, 1), "unit": "queries/s", "h2d_bytes_per_step": Bq * D * 4,
                 "d2h_bytes_per_step": Bq * k * 8, "api": api},
-        "gpu_launches_per_step": 2 + (1 if world > 1 else 0),
+        "gpu_launches_per_step": 3 + (1 if world > 1 else 0),
         "cpu_baseline": (cpu_batched_baseline(w, n_total, min(args.cpu_seconds, 10.0), k)
                          if rank == 0 and world == 1 else None),
     }

@@ -69,6 +69,7 @@ struct BatchScanParams {
   int stages;            // shared-memory ring depth (<= BATCH_MAX_STAGES)
   int QP, units;         // query pair-tiles (256 queries), work units
   float band_scale;      // band = band_scale * ||q||
+  const float* qband;    // [B] band of each query (k_query_bands)
   uint32_t* theta;       // [B] order-preserving keys of the running k-th best
   int* cand_count;       // [B]
   unsigned long long* cand;  // [B * cap]: tf32 score key << 32 | leaf row
@@ -263,12 +264,7 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
       const int qp = u % P.QP, slice = u / P.QP;
       const int q = qp * (2 * BQ) + (int)rank * BQ + 32 * warp + lane;
       const bool qv = q < P.B;
-      float qn2 = 0.f;
-      if (qv) {
-        const float* qrow = P.Q + (size_t)q * P.D;
-        for (int c = 0; c < P.D; ++c) qn2 = fmaf(__ldg(qrow + c), __ldg(qrow + c), qn2);
-      }
-      const float band = P.band_scale * sqrtf(qn2) * 1.0001f;
+      const float band = qv ? __ldg(P.qband + q) : 0.f;
       float top[KB];
 #pragma unroll
       for (int i = 0; i < KB; ++i) top[i] = -INFINITY;
@@ -353,7 +349,8 @@ constexpr int RESCORE_SMEM_ROWS = 8192;
 template <int VPL>
 __global__ void __launch_bounds__(256) k_batch_rescore(const float* __restrict__ Q, const float* __restrict__ leaf,
                                                        const int* __restrict__ original_ids, int D, int k, int cap,
-                                                       float band_scale, const uint32_t* __restrict__ theta,
+                                                       const float* __restrict__ qband,
+                                                       const uint32_t* __restrict__ theta,
                                                        const int* __restrict__ cand_count,
                                                        const unsigned long long* __restrict__ cand_in,
                                                        float* __restrict__ out_s, int* __restrict__ out_i,
@@ -363,28 +360,23 @@ __global__ void __launch_bounds__(256) k_batch_rescore(const float* __restrict__
   unsigned long long* sel = cand + RESCORE_SMEM_ROWS;
   SelectScratch* scratch = reinterpret_cast<SelectScratch*>(sel + 32);
   __shared__ int s_n;
-  __shared__ float s_qn2[8];
   const int q = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int total = cand_count[q];
   const int D4 = D >> 2;
   const float4* q4 = reinterpret_cast<const float4*>(Q + (size_t)q * D);
   float4 qv[VPL];
-  float qn2 = 0.f;
 #pragma unroll
   for (int v = 0; v < VPL; ++v) {
     const int c = lane + 32 * v;
     qv[v] = c < D4 ? __ldg(q4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-    qn2 = fmaf(qv[v].x, qv[v].x, fmaf(qv[v].y, qv[v].y, fmaf(qv[v].z, qv[v].z, fmaf(qv[v].w, qv[v].w, qn2))));
   }
-  qn2 = warp_sum(qn2);
   if (threadIdx.x == 0) s_n = 0;
-  if (lane == 0) s_qn2[warp] = qn2;
   __syncthreads();
   bool over = total > cap;
   if (!over) {
     const uint32_t tk = theta[q];
-    const float lim = tk ? key2f(tk) - band_scale * sqrtf(s_qn2[0]) * 1.0001f : -INFINITY;
+    const float lim = tk ? key2f(tk) - qband[q] : -INFINITY;
     for (int i = threadIdx.x; i < total; i += blockDim.x) {
       const unsigned long long e = cand_in[(size_t)q * cap + i];
       if (key2f((uint32_t)(e >> 32)) >= lim) {
@@ -433,6 +425,18 @@ __global__ void __launch_bounds__(256) k_batch_rescore(const float* __restrict__
     out_s[(size_t)q * k + i] = c ? key2f(cand_key(c)) : -INFINITY;
     out_i[(size_t)q * k + i] = c ? original_ids[cand_row(c)] : -1;
   }
+}
+
+// Error band of each query, 2 eps = band_scale ||q|| (padded): one warp per query.
+__global__ void k_query_bands(const float* __restrict__ Q, int B, int D, float band_scale, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int q = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  if (q >= B) return;
+  const float* row = Q + (size_t)q * D;
+  float s = 0.f;
+  for (int d = lane; d < D; d += 32) s = fmaf(row[d], row[d], s);
+  s = warp_sum(s);
+  if (lane == 0) out[q] = band_scale * sqrtf(s) * 1.0001f;
 }
 
 // Max row norm (upper bound) of the leaf matrix: one warp per row, grid-stride.
@@ -540,7 +544,7 @@ static cudaError_t launch_batch_scan_t(const void* qmap, const void* xmap, const
 
 template <int VPL>
 static cudaError_t launch_rescore_t(const float* Q, const IndexView& ix, const BatchWorkspace& bw, int B, int k,
-                                    float band_scale, float* out_s, int* out_i, cudaStream_t st) {
+                                    float* out_s, int* out_i, cudaStream_t st) {
   const size_t smem = (size_t)RESCORE_SMEM_ROWS * 8 + 32 * 8 + sizeof(SelectScratch) + 16;
   static size_t configured = 0;
   if (smem > configured) {
@@ -548,7 +552,7 @@ static cudaError_t launch_rescore_t(const float* Q, const IndexView& ix, const B
     if (e != cudaSuccess) return e;
     configured = smem;
   }
-  k_batch_rescore<VPL><<<B, 256, smem, st>>>(Q, ix.leaf, ix.original_ids, ix.D, k, bw.cap, band_scale, bw.theta,
+  k_batch_rescore<VPL><<<B, 256, smem, st>>>(Q, ix.leaf, ix.original_ids, ix.D, k, bw.cap, bw.qband, bw.theta,
                                              bw.cand_count, bw.cand, out_s, out_i, bw.overflow);
   return cudaGetLastError();
 }
@@ -577,6 +581,9 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   const double gD = ix.D * u / (1.0 - ix.D * u);
   const double eps_rel = 1.953125e-3 + 9.5367431640625e-07 + 2.0 * ix.D * 1.1920928955078125e-07 + gD;
   P.band_scale = (float)(2.0 * eps_rel * 1.01 * bw.xmax);
+  P.qband = bw.qband;
+  k_query_bands<<<(B + 7) / 8, 256, 0, st>>>(Q, B, ix.D, P.band_scale, bw.qband);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
   P.theta = bw.theta;
   P.cand_count = bw.cand_count;
   P.cand = bw.cand;
@@ -594,14 +601,14 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   // depend on this bucket, so scores match the single-query scan bit for bit)
   const int v = (ix.D / 4 + 31) / 32;
   switch (v <= 1 ? 1 : v <= 2 ? 2 : v <= 3 ? 3 : v <= 4 ? 4 : v <= 6 ? 6 : v <= 8 ? 8 : v <= 12 ? 12 : 16) {
-    case 1: return launch_rescore_t<1>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
-    case 2: return launch_rescore_t<2>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
-    case 3: return launch_rescore_t<3>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
-    case 4: return launch_rescore_t<4>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
-    case 6: return launch_rescore_t<6>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
-    case 8: return launch_rescore_t<8>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
-    case 12: return launch_rescore_t<12>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
-    default: return launch_rescore_t<16>(Q, ix, bw, B, k, P.band_scale, out_scores, out_ids, st);
+    case 1: return launch_rescore_t<1>(Q, ix, bw, B, k, out_scores, out_ids, st);
+    case 2: return launch_rescore_t<2>(Q, ix, bw, B, k, out_scores, out_ids, st);
+    case 3: return launch_rescore_t<3>(Q, ix, bw, B, k, out_scores, out_ids, st);
+    case 4: return launch_rescore_t<4>(Q, ix, bw, B, k, out_scores, out_ids, st);
+    case 6: return launch_rescore_t<6>(Q, ix, bw, B, k, out_scores, out_ids, st);
+    case 8: return launch_rescore_t<8>(Q, ix, bw, B, k, out_scores, out_ids, st);
+    case 12: return launch_rescore_t<12>(Q, ix, bw, B, k, out_scores, out_ids, st);
+    default: return launch_rescore_t<16>(Q, ix, bw, B, k, out_scores, out_ids, st);
   }
 }
 

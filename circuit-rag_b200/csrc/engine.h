@@ -114,6 +114,7 @@ struct BatchWorkspace {
   int* overflow = nullptr;        // queries whose candidate list overflowed
   int* err = nullptr;
   float* queries = nullptr;       // [capacity * D] staging for host queries
+  float* qband = nullptr;         // [capacity] per-query error band (2 eps, padded)
   float* out_scores = nullptr;    // [capacity * BATCH_MAX_K]
   int* out_ids = nullptr;
   int cap = BATCH_CAND_CAP;

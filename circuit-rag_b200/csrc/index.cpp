@@ -510,9 +510,10 @@ int circuit_index_opaque::ensure_batch(int B) {
     bw.cand = (unsigned long long*)grab(sizeof(unsigned long long) * (size_t)cap_B * bw.cap, "cudaMalloc(cand)");
     bw.overflow = (int*)grab(sizeof(int), "cudaMalloc(overflow)");
     bw.queries = (float*)grab(sizeof(float) * (size_t)cap_B * D, "cudaMalloc(batch queries)");
+    bw.qband = (float*)grab(sizeof(float) * (size_t)cap_B, "cudaMalloc(batch bands)");
     bw.out_scores = (float*)grab(sizeof(float) * (size_t)cap_B * cb::BATCH_MAX_K, "cudaMalloc(batch scores)");
     bw.out_ids = (int*)grab(sizeof(int) * (size_t)cap_B * cb::BATCH_MAX_K, "cudaMalloc(batch ids)");
-    if (!bw.theta || !bw.cand_count || !bw.cand || !bw.overflow || !bw.queries || !bw.out_scores ||
+    if (!bw.theta || !bw.cand_count || !bw.cand || !bw.overflow || !bw.queries || !bw.qband || !bw.out_scores ||
         !bw.out_ids) {
       bw.capacity = 0;
       return CIRCUIT_ERR_CUDA;
