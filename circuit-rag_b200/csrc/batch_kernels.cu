@@ -145,8 +145,9 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   // full / acc_empty are used in the even CTA only; empty / acc_full in both
   // (the even CTA's MMA thread commits to its own and to the odd CTA's copy).
-  __shared__ uint64_t full[BATCH_MAX_STAGES], empty[BATCH_MAX_STAGES], acc_full[2], acc_empty[2];
+  __shared__ uint64_t full[BATCH_MAX_STAGES], empty[BATCH_MAX_STAGES], acc_full[2], acc_empty[2], drain;
   __shared__ uint32_t tmem_base;
+  __shared__ int s_err;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = tc::cluster_ctarank();
   const bool leader = rank == 0;
@@ -163,6 +164,7 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 8);  // one lane of each epilogue warp of both CTAs
     }
+    mbar_init(&drain, 1);
     tc::fence_mbar_init_cluster();
   }
   if (warp == 5) tc::tmem_alloc_pair(&tmem_base, 512);
@@ -330,10 +332,24 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
       }
     }
   }
-  // Every MMA has completed (each epilogue waited for its last accumulator) and
-  // no CTA touches its peer after this point.
+  // Normally every MMA has completed here (each epilogue waited for its last
+  // accumulator).  On the error path a wait gave up: the even CTA waits
+  // (bounded) for the MMAs it issued, and both CTAs give in-flight TMA copies a
+  // bounded grace period, before TMEM is freed and shared memory released.
   tc::fence_before();
   tc::cluster_sync();
+  if (threadIdx.x == 0) s_err = ld_volatile_u32(reinterpret_cast<const uint32_t*>(P.err)) != 0u;
+  __syncthreads();
+  if (s_err) {
+    if (warp == 5 && leader) {
+      if (tc::elect_one()) tc::commit_pair(tc::mapa_shared(smem_u32(&drain), 0));
+      __syncwarp();
+      mbar_wait(&drain, 0, nullptr, 0);
+    }
+    if (threadIdx.x == 0) grace_period();
+  }
+  tc::fence_before();
+  tc::cluster_sync();  // no CTA touches its peer after this point
   tc::fence_after();
   if (warp == 5) tc::tmem_dealloc_pair(tmem, 512);
 }

@@ -96,6 +96,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     }
   }
 }
+// Error path only: a bounded wait gave up while bulk copies (or MMAs) may still
+// be in flight into this CTA's shared memory.  They complete within
+// microseconds unless the memory system is stuck, so the CTA waits a fixed,
+// bounded grace period before it reuses that memory or exits.
+constexpr unsigned long long GRACE_NS = 1000000ull;  // 1 ms
+__device__ __forceinline__ void grace_period() {
+  const unsigned long long t0 = globaltimer();
+  while (globaltimer() - t0 < GRACE_NS) __nanosleep(1000);
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes % 16 == 0,
 // both addresses 16-byte aligned: callers check this on the host).
 __device__ __forceinline__ void tma_load_1d(void* dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -66,9 +66,37 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge_topk_batch(const float*
   }
 }
 
+// One thread waits on an mbarrier that nothing arrives on: the bounded wait
+// gives up after WAIT_LIMIT_NS and records ERR_TIMEOUT_FULL.
+__global__ void k_selftest_wait(int* err) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_wait(&bar, 0, err, ERR_TIMEOUT_FULL);
+  }
+}
+
 }  // namespace cb
 
 extern "C" {
+
+int circuit_selftest_wait_timeout(int device_id, int* out_error_bits) {
+  if (!out_error_bits) { cb::set_error("null out_error_bits"); return CIRCUIT_ERR_ARG; }
+  if (!cb::cuda_ok(cudaSetDevice(device_id), "cudaSetDevice")) return CIRCUIT_ERR_CUDA;
+  int* d = nullptr;
+  if (!cb::cuda_ok(cudaMalloc(&d, sizeof(int)), "cudaMalloc")) return CIRCUIT_ERR_CUDA;
+  int rc = CIRCUIT_OK;
+  if (!cb::cuda_ok(cudaMemset(d, 0, sizeof(int)), "memset")) rc = CIRCUIT_ERR_CUDA;
+  if (rc == CIRCUIT_OK) {
+    cb::k_selftest_wait<<<1, 32>>>(d);
+    if (!cb::cuda_ok(cudaGetLastError(), "selftest launch") || !cb::cuda_ok(cudaDeviceSynchronize(), "selftest sync") ||
+        !cb::cuda_ok(cudaMemcpy(out_error_bits, d, sizeof(int), cudaMemcpyDeviceToHost), "selftest D2H"))
+      rc = CIRCUIT_ERR_CUDA;
+  }
+  cudaFree(d);
+  return rc;
+}
 
 int circuit_merge_topk_batch(const float* scores, const int* ids, int num_queries, int world, int k_in, int k,
                              float* out_scores, int* out_ids, void* stream) {

@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
   unsigned long long* topk_all = reinterpret_cast<unsigned long long*>(smem + L.topk_off);
   unsigned long long* sel = reinterpret_cast<unsigned long long*>(smem + L.sel_off);
   SelectScratch* scratch = reinterpret_cast<SelectScratch*>(smem + L.scratch_off);
-  __shared__ int s_is_last;
+  __shared__ int s_is_last, s_err;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int STAGES = P.stages;
@@ -315,6 +315,14 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     if (cnt > 0) merge();
   }
   __syncthreads();
+  // error path: a wait gave up and bulk copies may still land in the stage ring,
+  // which the grid merge below reuses
+  if (tid == 0) s_err = ld_volatile_u32(reinterpret_cast<const uint32_t*>(P.err)) != 0u;
+  __syncthreads();
+  if (s_err) {
+    if (tid == 0) grace_period();
+    __syncthreads();
+  }
 
   // ---------------------------------------------------------- CTA merge
   const int selN = KCAP;  // KCAP is a power of two >= k
@@ -676,6 +684,7 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
   if (lane == 0) {
     if (surv_roots) atomicAdd(&ctrl->n_surv_roots, surv_roots);
     if (surv_children) atomicAdd(&ctrl->n_surv_children, surv_children);
+    if (abort_all) grace_period();  // basis copies may still be in flight into this warp's buffers
   }
 }
 

@@ -103,6 +103,12 @@ void circuit_destroy_index(circuit_index_t index);
 /* Description of the last error on this thread ("" if none). */
 const char* circuit_last_error(void);
 int circuit_abi_version(void);
+/* Diagnostic: runs, on `device_id`, one kernel whose mbarrier wait is never
+ * satisfied, through the same bounded wait every search kernel uses (2 s of
+ * %globaltimer).  The wait gives up, the kernel records its error bit and
+ * returns; *out_error_bits receives the bits (1 = a "full" wait timed out).
+ * Blocking; the context stays usable.  No reference counterpart. */
+int circuit_selftest_wait_timeout(int device_id, int* out_error_bits);
 
 /* Wrap index arrays that already live on `device_id` (borrowed: the caller keeps
  * them alive and unmodified until circuit_destroy_index).  Shapes as in the

@@ -208,3 +208,18 @@ def test_cuda_graph_replay_matches():
         v1, i1 = idx.search_graph(q, k=10)
         s, i, _ = circuit_search(q, idx, k=10, min_hierarchy_n=10001)
         assert torch.equal(i1, i) and torch.equal(v1, s)
+
+
+def test_bounded_wait_gives_up_and_context_stays_usable():
+    """A device wait that nothing satisfies ends after its 2 s limit with an error
+    bit the host reads (no trap, no hang); the next search runs normally."""
+    L = _native.lib()
+    bits = ctypes.c_int(-1)
+    assert L.circuit_selftest_wait_timeout(0, ctypes.byref(bits)) == 0
+    assert bits.value == 1
+    w = WORKLOADS["clustered-50k"]
+    X = w.corpus(0, 5000, device=DEV)
+    idx = build_circuit_index(X, num_roots=8, children_per_root=4, rank=4, device=DEV)
+    q = w.query_batch(1, device=DEV)[0]
+    s, i, _ = circuit_search(q, idx, k=10)
+    _check(X, q, 10, s, i)
