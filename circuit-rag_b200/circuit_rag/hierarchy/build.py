@@ -134,6 +134,97 @@ class CircuitIndex:
             ws[name] = torch.full(shape, fill, dtype=spec[1], device=self.leaf_vectors.device)
         return ws[name]
 
+    # ------------------------------------------------------------------ incremental growth
+    def append(self, X_new, ids_new=None) -> None:
+        """Add rows without rebuilding the hierarchy.
+
+        Each new row joins the root with the largest inner product with its
+        centre (the builder's assignment rule); the root's radius is widened
+        if needed, and every touched root gets one new child whose box and
+        residual radius are computed from the new rows against the root's
+        stored float32 basis, in float64 with outward rounding (the builder's
+        certificate rules, so pruning stays exact).  Rows and children are
+        then laid out root-major again, so every root's rows stay contiguous.
+        ``ids_new`` defaults to N, N + 1, ...  Costs one gather of the leaf rows;
+        the native handle, workspaces and captured graphs are rebuilt on the
+        next search."""
+        Xn = torch.as_tensor(np.ascontiguousarray(X_new, dtype=np.float32) if isinstance(X_new, np.ndarray)
+                             else X_new).to(device=self.leaf_vectors.device, dtype=torch.float32).contiguous()
+        if Xn.ndim != 2 or Xn.shape[1] != self.dim:
+            raise ValueError("X_new must have shape [n, index.dim]")
+        n_new = Xn.shape[0]
+        if n_new == 0:
+            return
+        dev = self.leaf_vectors.device
+        if ids_new is None:
+            ids_new = torch.arange(self.N, self.N + n_new, dtype=torch.int32, device=dev)
+        ids_new = torch.as_tensor(ids_new).to(device=dev, dtype=torch.int32).reshape(-1)
+        if ids_new.numel() != n_new:
+            raise ValueError("ids_new must have one id per new row")
+        labels = _assign(Xn, self.root_centers)
+        touched = torch.unique(labels).tolist()
+        C0, r = self.num_total_children, self.rank
+        new_l, new_u, new_rho, new_parent, new_rows = [], [], [], [], []
+        radii = self.root_radii.clone()
+        for p in touched:
+            sel = torch.nonzero(labels == p).flatten()
+            d = Xn[sel].double() - self.root_centers[p].double()
+            rad = d.norm(dim=1).max() + _EPS
+            radii[p] = torch.maximum(radii[p], _round_up_f32(rad.reshape(1))[0])
+            Q64 = self.bases[p].double()
+            z = d @ Q64
+            new_l.append(_round_down_f32(z.min(dim=0).values - _EPS))
+            new_u.append(_round_up_f32(z.max(dim=0).values + _EPS))
+            res = d - z @ Q64.T
+            new_rho.append(_round_up_f32((res.norm(dim=1).max() + _EPS).reshape(1))[0])
+            new_parent.append(p)
+            new_rows.append(sel)
+        # children of both kinds, root-major: each root's old children (in leaf
+        # order), then its new child; empty children keep their records
+        parent = torch.cat([self.child_parent_ids.long(), torch.tensor(new_parent, device=dev)])
+        sizes = torch.cat([self.leaf_sizes.long(), torch.tensor([len(x) for x in new_rows], device=dev)])
+        offs = torch.cat([self.leaf_offsets.long(), torch.full((len(new_rows),), self.N, device=dev)])
+        is_new = torch.cat([torch.zeros(C0, dtype=torch.long, device=dev),
+                            torch.ones(len(new_rows), dtype=torch.long, device=dev)])
+        key = (parent * 2 + is_new) * (self.N + n_new + 1) + offs
+        order = torch.argsort(key, stable=True)
+        # gather map over the source [old leaf rows ; new rows]
+        new_src = torch.cat([x + self.N for x in new_rows]) if new_rows else torch.empty(0, dtype=torch.long,
+                                                                                        device=dev)
+        starts = torch.cat([self.leaf_offsets.long(), torch.cumsum(torch.tensor([0] + [len(x) for x in new_rows][:-1],
+                                                                                 device=dev), 0) + self.N])
+        pieces = []
+        for g in order.tolist():
+            m = int(sizes[g])
+            if m == 0:
+                continue
+            if g < C0:
+                pieces.append(torch.arange(int(starts[g]), int(starts[g]) + m, device=dev))
+            else:
+                b = int(starts[g]) - self.N
+                pieces.append(new_src[b:b + m])
+        gather = torch.cat(pieces)
+        src_rows = torch.cat([self.leaf_vectors, Xn])
+        src_ids = torch.cat([self.original_ids, ids_new])
+        sizes_o = sizes[order]
+        offs_o = torch.cumsum(sizes_o, 0) - sizes_o
+        l_all = torch.cat([self.child_intervals_l] + ([torch.stack(new_l)] if new_l else []))[order]
+        u_all = torch.cat([self.child_intervals_u] + ([torch.stack(new_u)] if new_u else []))[order]
+        rho_all = torch.cat([self.child_radii] + ([torch.stack(new_rho)] if new_rho else []))[order]
+        self.close()
+        self.__dict__["_ws"] = {}
+        self.root_radii = radii.contiguous()
+        self.child_intervals_l = l_all.contiguous()
+        self.child_intervals_u = u_all.contiguous()
+        self.child_radii = rho_all.contiguous()
+        self.child_parent_ids = parent[order].to(torch.int32).contiguous()
+        self.leaf_offsets = offs_o.to(torch.int32).contiguous()
+        self.leaf_sizes = sizes_o.to(torch.int32).contiguous()
+        self.leaf_vectors = src_rows[gather].contiguous()
+        self.original_ids = src_ids[gather].contiguous()
+        self.num_total_children = self.child_radii.shape[0]
+        self.N = self.leaf_vectors.shape[0]
+
     # ------------------------------------------------------------------ CUDA graphs
     def warmup_cuda_graph(self, k: int = 10):
         """Capture one search (pruning on) into a CUDA graph on static buffers

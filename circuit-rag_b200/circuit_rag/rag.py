@@ -1,4 +1,5 @@
-"""Text-in / text-out wrapper (reference circuit_rag/rag.py:11-65).
+"""Text-in / text-out wrapper (reference circuit_rag/rag.py:11-65), with
+incremental document adds instead of a full rebuild per call.
 
 The embedding model is out of scope for the search path and sentence-
 transformers is an optional dependency: CircuitRAG imports it only when it is
@@ -37,21 +38,44 @@ class CircuitRAG:
         self.metadatas: List[Dict[str, Any]] = []
         self._vectors: Optional[np.ndarray] = None
         self.index = None
+        self._built_n = 0
+        self.appended_rows = 0
+
+    # appended rows beyond this fraction of the last full build trigger a rebuild
+    REBUILD_FRACTION = 0.5
 
     def add_documents(self, texts: List[str], metadatas: Optional[List[Dict[str, Any]]] = None) -> List[int]:
-        """Embed and add documents, then rebuild the index (as the reference does)."""
-        if metadatas is None:
-            metadatas = [{} for _ in texts]
+        """Embed and add documents; returns their ids (reference rag.py:33-45).
+
+        The reference rebuilds the whole index on every call.  Here new
+        documents are appended to the existing hierarchy (CircuitIndex.append:
+        nearest root, new child, certificates recomputed) until the appended
+        rows exceed REBUILD_FRACTION of the rows of the last full build; then
+        the index is rebuilt with the reference's size rule (rag.py:47-55)."""
+        metadatas = metadatas or [{} for _ in texts]
+        if len(metadatas) != len(texts):
+            raise ValueError("metadatas must be the same length as texts")
         vecs = np.asarray(self._embed(list(texts)), dtype=np.float32)
         first = len(self.texts)
-        self.texts.extend(texts)
-        self.metadatas.extend(metadatas)
-        self._vectors = vecs if self._vectors is None else np.concatenate([self._vectors, vecs])
+        self.texts += list(texts)
+        self.metadatas += list(metadatas)
+        self._vectors = vecs if self._vectors is None else np.vstack([self._vectors, vecs])
         n = len(self._vectors)
-        roots = max(1, min(64, n // 16))
-        self.index = build_circuit_index(self._vectors, num_roots=roots, children_per_root=max(1, min(16, n // roots)),
-                                         rank=min(8, self._vectors.shape[1]), device=self.device)
+        if self.index is not None and (n - self._built_n) <= self.REBUILD_FRACTION * self._built_n:
+            self.index.append(vecs, np.arange(first, n, dtype=np.int32))
+            self.appended_rows = n - self._built_n
+        else:
+            self._rebuild()
         return list(range(first, n))
+
+    def _rebuild(self):
+        n = len(self._vectors)
+        roots = int(max(1, min(64, n // 256)))
+        children = int(max(1, min(16, n // (roots * 16))))
+        self.index = build_circuit_index(self._vectors, num_roots=roots, children_per_root=children,
+                                         rank=min(8, self._vectors.shape[1]), device=self.device)
+        self._built_n = n
+        self.appended_rows = 0
 
     def search(self, query: str, k: int = 5) -> List[SearchResult]:
         if self.index is None:

@@ -57,3 +57,50 @@ def test_search_requires_cuda_and_validates_shape():
         circuit_search(torch.zeros(7), idx)
     with pytest.raises(RuntimeError, match="CUDA"):
         circuit_search(torch.zeros(8), idx)
+
+
+def test_append_keeps_certificates_and_layout():
+    """CircuitIndex.append: new rows (some far from every centre) join their
+    nearest root under new children; every certificate still holds exactly and
+    the layout stays root-major and child-contiguous."""
+    w = WORKLOADS["clustered-50k"]
+    X1 = w.corpus(0, 3000).numpy()
+    idx = build_circuit_index(X1, num_roots=8, children_per_root=4, rank=6, device="cpu")
+    rng = np.random.default_rng(7)
+    X2 = w.corpus(3000, 3400).numpy()
+    X3 = (rng.normal(size=(60, X1.shape[1])) * 3.0).astype(np.float32)  # outside every root's old radius
+    idx.append(X2)
+    idx.append(X3)
+    X = np.concatenate([X1, X2, X3])
+    assert idx.N == len(X)
+    assert idx.num_total_children > 8 * 4
+    _check_invariants(idx, X)
+
+
+def test_append_validates_shapes():
+    X = np.random.default_rng(0).normal(size=(300, 8)).astype(np.float32)
+    idx = build_circuit_index(X, num_roots=4, children_per_root=2, rank=2, device="cpu")
+    with pytest.raises(ValueError):
+        idx.append(np.zeros((3, 7), np.float32))
+    with pytest.raises(ValueError):
+        idx.append(np.zeros((3, 8), np.float32), ids_new=[1, 2])
+
+
+def test_rag_appends_then_rebuilds():
+    from circuit_rag import CircuitRAG
+
+    dim = 16
+
+    def embed(texts):
+        out = np.stack([np.random.default_rng(abs(hash(t)) % (2 ** 32)).normal(size=dim) for t in texts])
+        return (out / np.linalg.norm(out, axis=1, keepdims=True)).astype(np.float32)
+
+    rag = CircuitRAG(device="cpu", embed_fn=embed)
+    ids = rag.add_documents([f"doc {i}" for i in range(600)])
+    assert ids == list(range(600)) and rag.index.N == 600 and rag.appended_rows == 0
+    rag.add_documents([f"more {i}" for i in range(200)], [{"i": i} for i in range(200)])
+    assert rag.index.N == 800 and rag.appended_rows == 200  # appended, not rebuilt
+    rag.add_documents([f"late {i}" for i in range(200)])
+    assert rag.index.N == 1000 and rag.appended_rows == 0   # beyond half of the last build: rebuilt
+    with pytest.raises(ValueError):
+        rag.add_documents(["a", "b"], [{}])

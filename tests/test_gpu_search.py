@@ -223,3 +223,26 @@ def test_bounded_wait_gives_up_and_context_stays_usable():
     q = w.query_batch(1, device=DEV)[0]
     s, i, _ = circuit_search(q, idx, k=10)
     _check(X, q, 10, s, i)
+
+
+def test_search_after_append_is_exact():
+    """An index grown with CircuitIndex.append (rows far outside the old roots
+    included) searches exactly, single and batched."""
+    from circuit_rag import circuit_search_batch
+
+    w = WORKLOADS["clustered-50k"]
+    X1 = w.corpus(0, 20000, device=DEV)
+    idx = build_circuit_index(X1, num_roots=16, children_per_root=8, rank=8, device=DEV)
+    g = torch.Generator(device="cpu").manual_seed(3)
+    X2 = w.corpus(20000, 26000, device=DEV)
+    X3 = (torch.randn(500, X1.shape[1], generator=g) * 2.0).to(DEV)
+    idx.append(X2)
+    idx.append(X3)
+    X = torch.cat([X1, X2, X3])
+    Q = torch.cat([w.query_batch(6, device=DEV), X3[:4] * 1.01])
+    for q in Q:
+        s, i, tr = circuit_search(q, idx, k=10)
+        _check(X, q, 10, s, i)
+    bs, bi = circuit_search_batch(Q, idx, k=10)
+    for b in range(Q.shape[0]):
+        _check(X, Q[b], 10, bs[b], bi[b])
