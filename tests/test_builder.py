@@ -104,3 +104,24 @@ def test_rag_appends_then_rebuilds():
     assert rag.index.N == 1000 and rag.appended_rows == 0   # beyond half of the last build: rebuilt
     with pytest.raises(ValueError):
         rag.add_documents(["a", "b"], [{}])
+
+
+def test_appended_index_saves_and_shards(tmp_path):
+    from circuit_rag.shard import load_shard
+
+    w = WORKLOADS["clustered-50k"]
+    X1 = w.corpus(0, 2000).numpy()
+    idx = build_circuit_index(X1, num_roots=6, children_per_root=3, rank=4, device="cpu")
+    X2 = w.corpus(2000, 2300).numpy()
+    idx.append(X2)
+    X = np.concatenate([X1, X2])
+    path = str(tmp_path / "a.circuit")
+    idx.save(path)
+    ids = []
+    for r in range(2):
+        sh = load_shard(path, r, 2, device="cpu")
+        assert torch.equal(sh.leaf_vectors, torch.from_numpy(X)[sh.original_ids.long()])
+        offs = sh.leaf_offsets[sh.leaf_sizes > 0]
+        assert torch.all(offs[1:] > offs[:-1])
+        ids += sh.original_ids.tolist()
+    assert sorted(ids) == list(range(len(X)))
