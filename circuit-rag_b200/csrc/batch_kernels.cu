@@ -57,7 +57,9 @@ constexpr int HALF_N = BN / 2;
 constexpr int EPI_COLS = 64;             // accumulator columns per epilogue pass
 constexpr int BATCH_THREADS = 192;       // warps 0-3 epilogue, 4 TMA, 5 MMA
 constexpr int BATCH_MAX_STAGES = 8;
-constexpr int SLICE_ROWS = 8192;         // rows per work unit
+constexpr int SLICE_ROWS = 8192;         // rows per work unit of the main pass
+constexpr int SEED_ROWS = 32768;         // rows of the threshold pass (one unit per query tile)
+constexpr int BATCH_SEED_MIN_N = 65536;  // smaller corpora skip the threshold pass
 constexpr int A_BYTES = BQ * 128;        // 128 query rows x 32 floats
 constexpr int B_BYTES = HALF_N * 128;    // 128 leaf rows x 32 floats
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -75,6 +77,9 @@ struct BatchScanParams {
   unsigned long long* cand;  // [B * cap]: tf32 score key << 32 | leaf row
   int cap;
   int* err;
+  int seed_only;         // threshold pass: raise theta, append no candidates
+  uint32_t* slots;       // [B * k] per-query slots of the rotated top-k publication
+  int slice_rows;        // rows per work unit
 };
 
 // One epilogue pass over 64 accumulator columns (leaf rows row_base + i) of this
@@ -119,6 +124,7 @@ __device__ __forceinline__ void epi_pass(const uint32_t (&sc0)[32], const uint32
     }
   }
   theta = fmaxf(theta, theta_local);
+  if (P.seed_only) return;
   const float lim2 = theta - band;
   for (uint64_t m = mask; m; m &= m - 1ull) {
     const int i = __ffsll((long long)m) - 1;
@@ -187,7 +193,7 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
       for (int u = pair; u < P.units && ok; u += npairs) {
         const int qp = u % P.QP, slice = u / P.QP;
         const int qrow = qp * (2 * BQ) + (int)rank * BQ;
-        const int r0 = slice * SLICE_ROWS, r1 = min(P.N, r0 + SLICE_ROWS);
+        const int r0 = slice * P.slice_rows, r1 = min(P.N, r0 + P.slice_rows);
         for (int row0 = r0; row0 < r1 && ok; row0 += BN) {
           const int xrow = row0 + (int)rank * HALF_N;
           for (int j = 0; j < P.kb; ++j, ++c) {
@@ -221,7 +227,7 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
       bool ok = true;
       for (int u = pair; u < P.units && ok; u += npairs) {
         const int slice = u / P.QP;
-        const int r0 = slice * SLICE_ROWS, r1 = min(P.N, r0 + SLICE_ROWS);
+        const int r0 = slice * P.slice_rows, r1 = min(P.N, r0 + P.slice_rows);
         for (int row0 = r0; row0 < r1 && ok; row0 += BN, ++it) {
           const int b = it & 1, fb = it >> 1;
           // wait results are made warp-uniform: elect.sync needs every lane
@@ -275,7 +281,7 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
       uint32_t g_pending = g_key;
       float theta = g_key ? key2f(g_key) : -INFINITY;
       uint32_t published = 0;
-      const int r0 = slice * SLICE_ROWS, r1 = min(P.N, r0 + SLICE_ROWS);
+      const int r0 = slice * P.slice_rows, r1 = min(P.N, r0 + P.slice_rows);
       int tiles = 0;
       for (int row0 = r0; row0 < r1; row0 += BN, ++it, ++tiles) {
         const int b = it & 1, fb = it >> 1;
@@ -329,6 +335,27 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
       if (qv && theta_local > -INFINITY) {
         const uint32_t key = f2key(theta_local);
         if (key > published) atomicMax(P.theta + q, key);
+        published = key > published ? key : published;
+      }
+      if (qv && !P.seed_only) {
+        // Rotated publication: this unit's i-th best goes into slot (i + u) mod k
+        // by atomicMax.  Every slot then holds the score of one real row, and
+        // two slots never hold the same row (main-pass units scan disjoint
+        // rows; each (unit, rank) pair writes one slot), so the smallest slot
+        // is the k-th best of k distinct rows: a valid threshold, and one that
+        // climbs towards the global k-th best as units finish, unlike any
+        // single unit's k-th best.  (The threshold pass, whose sampled rows are
+        // scanned again here, stays out of the slots.)
+        uint32_t* sl = P.slots + (size_t)q * P.k;
+        int j = u % P.k;
+#pragma unroll 1
+        for (int i = 0; i < P.k && top[i] > -INFINITY; ++i) {
+          atomicMax(sl + j, f2key(top[i]));
+          if (++j == P.k) j = 0;
+        }
+        uint32_t mn = 0xffffffffu;
+        for (int i = 0; i < P.k; ++i) mn = min(mn, ld_volatile_u32(sl + i));
+        if (mn != 0u && mn > published) atomicMax(P.theta + q, mn);  // 0: a slot not yet filled
       }
     }
   }
@@ -374,7 +401,7 @@ __global__ void __launch_bounds__(256) k_batch_rescore(const float* __restrict__
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem);
   unsigned long long* sel = cand + RESCORE_SMEM_ROWS;
-  SelectScratch* scratch = reinterpret_cast<SelectScratch*>(sel + 32);
+  SelectScratch* scratch = reinterpret_cast<SelectScratch*>(sel + BATCH_MAX_K);
   __shared__ int s_n;
   const int q = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -389,9 +416,19 @@ __global__ void __launch_bounds__(256) k_batch_rescore(const float* __restrict__
   }
   if (threadIdx.x == 0) s_n = 0;
   __syncthreads();
+  int selN = 1;
+  while (selN < k) selN <<= 1;
   bool over = total > cap;
   if (!over) {
-    const uint32_t tk = theta[q];
+    // threshold: the larger of the scan's final one and the k-th best tf32
+    // score among the candidates themselves (k real rows either way), minus
+    // the band
+    uint32_t tk = theta[q];
+    if (total >= k) {
+      block_select_topk<true>(cand_in + (size_t)q * cap, total, k, sel, selN, scratch);
+      const uint32_t ck = (uint32_t)(sel[k - 1] >> 32);
+      tk = ck > tk ? ck : tk;
+    }
     const float lim = tk ? key2f(tk) - qband[q] : -INFINITY;
     for (int i = threadIdx.x; i < total; i += blockDim.x) {
       const unsigned long long e = cand_in[(size_t)q * cap + i];
@@ -433,8 +470,6 @@ __global__ void __launch_bounds__(256) k_batch_rescore(const float* __restrict__
     if (lane == 0) cand[i] = pack_cand(f2key(acc), (uint32_t)row);
   }
   __syncthreads();
-  int selN = 1;
-  while (selN < k) selN <<= 1;
   block_select_topk<false>(cand, n, k, sel, selN, scratch);
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
     const unsigned long long c = sel[i];
@@ -483,12 +518,13 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// [rows, D] fp32 row-major -> boxes of 128 rows x 32 columns, 128-byte swizzle.
-static bool make_rows_tensor_map(const float* base, int rows, int D, void* out_map) {
+// [rows, D] fp32 -> boxes of 128 rows x 32 columns, 128-byte swizzle; row r of
+// the map is row r * row_step of the buffer.
+static bool make_rows_tensor_map(const float* base, int rows, int D, void* out_map, int row_step = 1) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)D * 4};
+  cuuint64_t strides[1] = {(cuuint64_t)D * 4 * (cuuint64_t)row_step};
   cuuint32_t box[2] = {32, 128};
   cuuint32_t estr[2] = {1, 1};
   return enc(reinterpret_cast<CUtensorMap*>(out_map), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base),
@@ -498,6 +534,19 @@ static bool make_rows_tensor_map(const float* base, int rows, int D, void* out_m
 
 bool make_leaf_tensor_map(const float* leaf, int N, int D, void* out_map) {
   return make_rows_tensor_map(leaf, N, D, out_map);
+}
+
+// rows r * step, step = max(16, N / 32768), r < sample_rows_for(N) <= 32768:
+// all inside the corpus
+static int sample_step(int N) { return N / SEED_ROWS > 16 ? N / SEED_ROWS : 16; }
+int sample_rows_for(int N) {
+  if (N < BATCH_SEED_MIN_N) return 0;
+  const int n = (N - 1) / sample_step(N) + 1;
+  return n < SEED_ROWS ? n : SEED_ROWS;
+}
+
+bool make_sample_tensor_map(const float* leaf, int N, int D, void* out_map) {
+  return make_rows_tensor_map(leaf, sample_rows_for(N), D, out_map, sample_step(N));
 }
 
 cudaError_t launch_max_row_norm(const float* leaf, int N, int D, unsigned int* out_key, int sms, cudaStream_t st) {
@@ -561,7 +610,7 @@ static cudaError_t launch_batch_scan_t(const void* qmap, const void* xmap, const
 template <int VPL>
 static cudaError_t launch_rescore_t(const float* Q, const IndexView& ix, const BatchWorkspace& bw, int B, int k,
                                     float* out_s, int* out_i, cudaStream_t st) {
-  const size_t smem = (size_t)RESCORE_SMEM_ROWS * 8 + 32 * 8 + sizeof(SelectScratch) + 16;
+  const size_t smem = (size_t)RESCORE_SMEM_ROWS * 8 + BATCH_MAX_K * 8 + sizeof(SelectScratch) + 16;
   static size_t configured = 0;
   if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(k_batch_rescore<VPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -580,6 +629,7 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   if ((e = cudaMemsetAsync(bw.theta, 0, sizeof(uint32_t) * B, st)) != cudaSuccess) return e;
   if ((e = cudaMemsetAsync(bw.cand_count, 0, sizeof(int) * B, st)) != cudaSuccess) return e;
   if ((e = cudaMemsetAsync(bw.overflow, 0, sizeof(int), st)) != cudaSuccess) return e;
+  if ((e = cudaMemsetAsync(bw.slots, 0, sizeof(uint32_t) * (size_t)B * k, st)) != cudaSuccess) return e;
   BatchScanParams P{};
   P.Q = Q;
   P.B = B;
@@ -601,17 +651,38 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   k_query_bands<<<(B + 7) / 8, 256, 0, st>>>(Q, B, ix.D, P.band_scale, bw.qband);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   P.theta = bw.theta;
+  P.slots = bw.slots;
   P.cand_count = bw.cand_count;
   P.cand = bw.cand;
   P.cap = bw.cap;
   P.err = bw.err;
+  P.seed_only = 0;
+  P.slice_rows = SLICE_ROWS;
   alignas(64) unsigned char qmap[128];
   if (!make_rows_tensor_map(Q, B, ix.D, qmap)) return cudaErrorInvalidValue;
   const int max_pairs = bw.sms / 2;
+  // the per-thread top-k array is sized for k (16 / 32 / 64 / 128 entries); it
+  // is touched only on the epilogue's rare path
+  auto scan = [&](const void* xmap, const BatchScanParams& PP) -> cudaError_t {
+    if (k <= 16) return launch_batch_scan_t<16>(qmap, xmap, PP, max_pairs, st);
+    if (k <= 32) return launch_batch_scan_t<32>(qmap, xmap, PP, max_pairs, st);
+    if (k <= 64) return launch_batch_scan_t<64>(qmap, xmap, PP, max_pairs, st);
+    return launch_batch_scan_t<128>(qmap, xmap, PP, max_pairs, st);
+  };
   if (ev_scan_begin && (e = cudaEventRecord(ev_scan_begin, st)) != cudaSuccess) return e;
-  e = (k <= 16) ? launch_batch_scan_t<16>(qmap, bw.tmap, P, max_pairs, st)
-                : launch_batch_scan_t<32>(qmap, bw.tmap, P, max_pairs, st);
-  if (e != cudaSuccess) return e;
+  if (bw.sample_rows > 0) {
+    // threshold pass over up to 32,768 rows spread evenly through the corpus,
+    // one unit per query tile: every query starts the main pass from the k-th
+    // best of these rows instead of -inf (any k rows give a valid threshold),
+    // which removes most cold-start candidates and rare-path epilogue work
+    BatchScanParams S = P;
+    S.N = bw.sample_rows;
+    S.units = P.QP;
+    S.seed_only = 1;
+    S.slice_rows = SEED_ROWS;  // one unit per query tile: its k best over all sampled rows
+    if ((e = scan(bw.smap, S)) != cudaSuccess) return e;
+  }
+  if ((e = scan(bw.tmap, P)) != cudaSuccess) return e;
   if (ev_scan_end && (e = cudaEventRecord(ev_scan_end, st)) != cudaSuccess) return e;
   // float4 registers per lane for the query (the per-lane FMA order does not
   // depend on this bucket, so scores match the single-query scan bit for bit)

@@ -104,27 +104,32 @@ cudaError_t launch_flat_scan(const float* leaf, int D, int N, const float* q, in
 
 // ---- batched search (batch_kernels.cu) ----
 constexpr int BATCH_MAX_DIM = 2048;  // the rescoring keeps the query in registers (16 float4 per lane)
-constexpr int BATCH_MAX_K = 32;
+constexpr int BATCH_MAX_K = 128;  // per-thread top-k of the scan epilogue (16 / 32 / 64 / 128)
 constexpr int BATCH_CAND_CAP = 16384;  // candidate rows appended per query
 
 struct BatchWorkspace {
   uint32_t* theta = nullptr;      // [capacity] running k-th best keys
+  uint32_t* slots = nullptr;      // [capacity * BATCH_MAX_K] rotated top-k publication
   int* cand_count = nullptr;      // [capacity]
   unsigned long long* cand = nullptr;  // [capacity * cap] tf32 key << 32 | row
   int* overflow = nullptr;        // queries whose candidate list overflowed
   int* err = nullptr;
   float* queries = nullptr;       // [capacity * D] staging for host queries
   float* qband = nullptr;         // [capacity] per-query error band (2 eps, padded)
-  float* out_scores = nullptr;    // [capacity * BATCH_MAX_K]
+  float* out_scores = nullptr;    // [capacity * KMAX] host-call staging
   int* out_ids = nullptr;
   int cap = BATCH_CAND_CAP;
   int capacity = 0;
   float xmax = 0.f;               // upper bound of max ||x|| over the leaf rows
   int sms = 0;
-  alignas(64) unsigned char tmap[128];  // CUtensorMap of leaf_vectors, boxes of 64 rows x 32 columns
+  alignas(64) unsigned char tmap[128];  // CUtensorMap of leaf_vectors, boxes of 128 rows x 32 columns
+  alignas(64) unsigned char smap[128];  // the same over evenly spaced rows (threshold pass)
+  int sample_rows = 0;                  // rows of smap (0: no threshold pass)
 };
 
 bool make_leaf_tensor_map(const float* leaf, int N, int D, void* out_map);
+int sample_rows_for(int N);
+bool make_sample_tensor_map(const float* leaf, int N, int D, void* out_map);
 cudaError_t launch_max_row_norm(const float* leaf, int N, int D, unsigned int* out_key, int sms, cudaStream_t st);
 // queries [B, D] (device) -> out_scores / out_ids [B, k], original ids, (score desc, row asc).
 cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, const float* Q, int B, int k,

@@ -491,6 +491,11 @@ int circuit_index_opaque::ensure_batch(int B) {
       set_error("cuTensorMapEncodeTiled failed for leaf_vectors");
       return CIRCUIT_ERR_CUDA;
     }
+    bw.sample_rows = cb::sample_rows_for(N);
+    if (bw.sample_rows > 0 && !cb::make_sample_tensor_map(view.leaf, N, D, bw.smap)) {
+      set_error("cuTensorMapEncodeTiled failed for the sampled leaf rows");
+      return CIRCUIT_ERR_CUDA;
+    }
     batch_ready = true;
   }
   if (B > bw.capacity) {
@@ -506,14 +511,16 @@ int circuit_index_opaque::ensure_batch(int B) {
       return p;
     };
     bw.theta = (uint32_t*)grab(sizeof(uint32_t) * cap_B, "cudaMalloc(theta)");
+    bw.slots = (uint32_t*)grab(sizeof(uint32_t) * (size_t)cap_B * cb::BATCH_MAX_K, "cudaMalloc(slots)");
     bw.cand_count = (int*)grab(sizeof(int) * cap_B, "cudaMalloc(cand_count)");
     bw.cand = (unsigned long long*)grab(sizeof(unsigned long long) * (size_t)cap_B * bw.cap, "cudaMalloc(cand)");
     bw.overflow = (int*)grab(sizeof(int), "cudaMalloc(overflow)");
     bw.queries = (float*)grab(sizeof(float) * (size_t)cap_B * D, "cudaMalloc(batch queries)");
     bw.qband = (float*)grab(sizeof(float) * (size_t)cap_B, "cudaMalloc(batch bands)");
-    bw.out_scores = (float*)grab(sizeof(float) * (size_t)cap_B * cb::BATCH_MAX_K, "cudaMalloc(batch scores)");
-    bw.out_ids = (int*)grab(sizeof(int) * (size_t)cap_B * cb::BATCH_MAX_K, "cudaMalloc(batch ids)");
-    if (!bw.theta || !bw.cand_count || !bw.cand || !bw.overflow || !bw.queries || !bw.qband || !bw.out_scores ||
+    // staging for the host-buffer call: any k up to KMAX (k > BATCH_MAX_K is answered per query)
+    bw.out_scores = (float*)grab(sizeof(float) * (size_t)cap_B * cb::KMAX, "cudaMalloc(batch scores)");
+    bw.out_ids = (int*)grab(sizeof(int) * (size_t)cap_B * cb::KMAX, "cudaMalloc(batch ids)");
+    if (!bw.theta || !bw.slots || !bw.cand_count || !bw.cand || !bw.overflow || !bw.queries || !bw.qband || !bw.out_scores ||
         !bw.out_ids) {
       bw.capacity = 0;
       return CIRCUIT_ERR_CUDA;

@@ -145,9 +145,25 @@ def test_batch_rejects_unsupported():
     assert rc == -2
 
 
+@pytest.mark.parametrize("k", [64, 100, 128, 200])
+def test_batch_large_k_host_buffers(k):
+    """Host-buffer batched call at large k: 64 / 100 / 128 on the tensor cores,
+    200 query by query; results identical to the single-query search."""
+    w = WORKLOADS["zipf-10m"]
+    X = w.corpus(0, 30_000, device=DEV)
+    index = build_circuit_index(X, num_roots=32, children_per_root=8, rank=16, device=DEV)
+    Qh = w.query_batch(20).contiguous()
+    s = np.zeros((20, k), np.float32)
+    i = np.zeros((20, k), np.int32)
+    torch.cuda.synchronize()
+    rc = _native.lib().circuit_search_batch(index.native_handle(), Qh.data_ptr(), 20, k, s.ctypes.data, i.ctypes.data)
+    assert rc == 0, _native.last_error()
+    _check_batch(X, Qh.to(DEV), index, k, torch.from_numpy(s).to(DEV), torch.from_numpy(i).to(DEV))
+
+
 def test_batch_large_k_matches_single_query():
-    """k = 100 (the zipf-10m configuration's k) is beyond the tensor-core path's
-    per-thread top-k; the batched call answers query by query, same results."""
+    """k = 100 (the zipf-10m configuration's k) on the tensor-core path (per-thread
+    top-k of 128 entries), same results as the single-query search."""
     w = WORKLOADS["zipf-10m"]
     X = w.corpus(0, 40_000, device=DEV)
     index = build_circuit_index(X, num_roots=32, children_per_root=8, rank=16, device=DEV)
