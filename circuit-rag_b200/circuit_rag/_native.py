@@ -12,7 +12,7 @@ LIB_PATH = os.path.join(_HERE, "libcircuit.so")
 
 CIRCUIT_OK = 0
 CIRCUIT_MAX_K = 256
-CIRCUIT_BATCH_MAX_K = 128
+CIRCUIT_BATCH_MAX_K = 256
 CIRCUIT_BATCH_MAX_DIM = 2048
 CIRCUIT_MAX_RANK = 64
 CIRCUIT_MAX_DIM = 2048

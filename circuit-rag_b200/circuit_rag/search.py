@@ -133,9 +133,8 @@ def circuit_search_batch(queries: torch.Tensor, index: CircuitIndex, k: int = 10
     results equal B calls of circuit_search: a tf32 tcgen05 pass over every
     leaf row keeps each query's rows within a rigorous error band of its running
     k-th best, and those rows are rescored exactly in fp32.  Returns (scores
-    [B, k] float32 descending, original ids [B, k] int32).  k <= 128 runs on the
-    tensor cores; 128 < k <= 256 is answered query by query by the single-query
-    path (same results).  A query whose candidate list overflows
+    [B, k] float32 descending, original ids [B, k] int32), 1 <= k <= 256.
+    A query whose candidate list overflows
     (more than 8192 rows inside the band, e.g. thousands of near-identical
     rows) is answered by circuit_search."""
     if queries.ndim != 2 or queries.shape[1] != index.dim:

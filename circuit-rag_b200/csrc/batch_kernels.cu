@@ -78,14 +78,16 @@ struct BatchScanParams {
   int cap;
   int* err;
   int seed_only;         // threshold pass: raise theta, append no candidates
-  uint32_t* slots;       // [B * k] per-query slots of the rotated top-k publication
+  uint32_t* slots;       // [B * k] per-query threshold slots (slot_min)
+  int row_step;          // leaf row = scan row * row_step (threshold pass: sampled rows)
   int slice_rows;        // rows per work unit
 };
 
-// One epilogue pass over 64 accumulator columns (leaf rows row_base + i) of this
-// thread's query.  Returns nothing; updates the running state in place.
+// Top-k variant (k <= 32): one epilogue pass over 64 accumulator columns (leaf
+// rows row_base + i) of this thread's query; the thread's k best tf32 scores are
+// kept sorted in `top`, so its threshold rises with every insertion.
 template <int KB>
-__device__ __forceinline__ void epi_pass(const uint32_t (&sc0)[32], const uint32_t (&sc1)[32], int row_base, int nrow,
+__device__ __forceinline__ void epi_pass_topk(const uint32_t (&sc0)[32], const uint32_t (&sc1)[32], int row_base, int nrow,
                                          float band, float& theta, float& theta_local, float (&top)[KB], int q,
                                          float* stash, const BatchScanParams& P) {
   const float lim = theta - band;
@@ -137,11 +139,65 @@ __device__ __forceinline__ void epi_pass(const uint32_t (&sc0)[32], const uint32
   }
 }
 
+// Per-query threshold from k slots.  Leaf row r publishes its tf32 score into
+// slot r mod k by atomicMax.  The slots cover disjoint sets of rows, so each
+// holds the score of one real row and no row is in two slots: the smallest
+// slot is the k-th best of k distinct rows, a valid threshold (0 = a slot not
+// yet filled).  A row always maps to the same slot, so rows seen twice (the
+// threshold pass samples rows that the main pass scans again) cannot count
+// twice.  No per-thread top-k list is needed, for any k.
+__device__ __forceinline__ uint32_t slot_min(const uint32_t* sl, int k) {
+  uint32_t mn = 0xffffffffu;
+  for (int i = 0; i < k; ++i) mn = min(mn, ld_volatile_u32(sl + i));
+  return mn;
+}
+
+// One epilogue pass over 64 accumulator columns (rows row_base + i of the scan's
+// row space) of this thread's query: rows within `band` of the threshold are
+// appended as candidates (main pass), rows above it raise their slot.  Returns
+// whether a slot was raised.
+__device__ __forceinline__ bool epi_pass(const uint32_t (&sc0)[32], const uint32_t (&sc1)[32], int row_base, int nrow,
+                                         float band, float theta, int q, float* stash, const BatchScanParams& P) {
+  const float lim = theta - band;
+  uint64_t mask = 0ull;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    mask |= (uint64_t)(__uint_as_float(sc0[i]) >= lim) << i;
+    mask |= (uint64_t)(__uint_as_float(sc1[i]) >= lim) << (32 + i);
+  }
+  if (nrow < EPI_COLS) mask &= nrow > 0 ? (1ull << nrow) - 1ull : 0ull;
+  if (!mask) return false;
+  // rare: stage the scores ([column][thread], conflict-free) and walk the rows
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    stash[i * BQ + threadIdx.x] = __uint_as_float(sc0[i]);
+    stash[(32 + i) * BQ + threadIdx.x] = __uint_as_float(sc1[i]);
+  }
+  uint32_t* sl = P.slots + (size_t)q * P.k;
+  bool raised = false;
+  for (uint64_t m = mask; m; m &= m - 1ull) {
+    const int i = __ffsll((long long)m) - 1;
+    const float sv = stash[i * BQ + threadIdx.x];
+    const uint32_t key = f2key(sv);
+    if (sv > theta) {  // a row below every slot cannot raise one
+      const uint32_t leaf_row = (uint32_t)(row_base + i) * (uint32_t)P.row_step;
+      atomicMax(sl + leaf_row % (uint32_t)P.k, key);
+      raised = true;
+    }
+    if (!P.seed_only) {
+      const int slot = atomicAdd(P.cand_count + q, 1);
+      if (slot < P.cap) P.cand[(size_t)q * P.cap + slot] = ((unsigned long long)key << 32) | (uint32_t)(row_base + i);
+    }
+  }
+  return raised;
+}
+
 // Launched as clusters of 2 CTAs.  CTA rank r of the pair loads queries
 // [256 qp + 128 r, +128) and leaf rows [row0 + 128 r, +128) of every tile; the
 // pair's accumulator holds, in CTA r's TMEM lanes, its 128 queries against all
 // 256 rows of the tile (columns 0-127: rows loaded by the even CTA, 128-255:
 // by the odd CTA).
+// KB > 0: per-thread top-KB epilogue (k <= KB); KB == 0: slot thresholds (any k).
 template <int KB>
 __global__ void __launch_bounds__(BATCH_THREADS, 1)
     k_batch_scan(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap xmap,
@@ -272,6 +328,7 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
       const int qp = u % P.QP, slice = u / P.QP;
       const int q = qp * (2 * BQ) + (int)rank * BQ + 32 * warp + lane;
       const bool qv = q < P.B;
+      if constexpr (KB > 0) {
       const float band = qv ? __ldg(P.qband + q) : 0.f;
       float top[KB];
 #pragma unroll
@@ -320,8 +377,8 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
             for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
           if (mx[0] >= theta - band) {
             const int rb = row0 + half * 128;
-            epi_pass<KB>(sa, sb, rb, r1 - rb, band, theta, theta_local, top, q, stash, P);
-            epi_pass<KB>(sc, sd, rb + 64, r1 - rb - 64, band, theta, theta_local, top, q, stash, P);
+            epi_pass_topk<KB>(sa, sb, rb, r1 - rb, band, theta, theta_local, top, q, stash, P);
+            epi_pass_topk<KB>(sc, sd, rb + 64, r1 - rb - 64, band, theta, theta_local, top, q, stash, P);
           }
         }
         if (qv && (tiles & 1) == 1 && theta_local > -INFINITY) {
@@ -356,6 +413,66 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
         uint32_t mn = 0xffffffffu;
         for (int i = 0; i < P.k; ++i) mn = min(mn, ld_volatile_u32(sl + i));
         if (mn != 0u && mn > published) atomicMax(P.theta + q, mn);  // 0: a slot not yet filled
+      }
+      } else {
+      const float band = qv ? __ldg(P.qband + q) : 0.f;
+      const uint32_t* sl = P.slots + (size_t)q * P.k;
+      uint32_t g_key = qv ? ld_volatile_u32(P.theta + q) : 0u;
+      uint32_t g_pending = g_key;
+      float theta = g_key ? key2f(g_key) : -INFINITY;
+      const int r0 = slice * P.slice_rows, r1 = min(P.N, r0 + P.slice_rows);
+      for (int row0 = r0; row0 < r1; row0 += BN, ++it) {
+        const int b = it & 1, fb = it >> 1;
+        if (!mbar_wait(&acc_full[b], fb & 1, P.err, ERR_TIMEOUT_FULL)) { ok = false; break; }
+        tc::fence_after();
+        if (qv) {
+          // the query's published threshold, read one tile ahead (its latency
+          // overlaps this tile)
+          if (g_pending) theta = fmaxf(theta, key2f(g_pending));
+          g_pending = ld_volatile_u32(P.theta + q);
+        }
+        // two halves of 128 columns: all four loads of a half issued before one
+        // wait; the common case is one max per score and one compare per half
+        bool raised = false;
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          uint32_t sa[32], sb[32], sc[32], sd[32];
+          const uint32_t col = tmem + lane_base + (uint32_t)(b * BN + half * 128);
+          tc::ld_32x32b_x32(col, sa);
+          tc::ld_32x32b_x32(col + 32, sb);
+          tc::ld_32x32b_x32(col + 64, sc);
+          tc::ld_32x32b_x32(col + 96, sd);
+          tc::wait_ld();
+          if (half == 1) {
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive_remote(lead_acc_empty + 8u * (uint32_t)b);
+          }
+          if (!qv) continue;
+          float mx[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            mx[i] = fmaxf(fmaxf(__uint_as_float(sa[i]), __uint_as_float(sb[i])),
+                          fmaxf(__uint_as_float(sc[i]), __uint_as_float(sd[i])));
+#pragma unroll
+          for (int w = 16; w > 0; w >>= 1)
+#pragma unroll
+            for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
+          if (mx[0] >= theta - band) {
+            const int rb = row0 + half * 128;
+            raised |= epi_pass(sa, sb, rb, r1 - rb, band, theta, q, stash, P);
+            raised |= epi_pass(sc, sd, rb + 64, r1 - rb - 64, band, theta, q, stash, P);
+          }
+        }
+        if (raised) {
+          // this thread raised a slot: recompute the slot minimum and publish it
+          const uint32_t mn = slot_min(sl, P.k);
+          if (mn != 0u && mn != 0xffffffffu) {
+            theta = fmaxf(theta, key2f(mn));
+            if (mn > g_pending) atomicMax(P.theta + q, mn);
+          }
+        }
+      }
       }
     }
   }
@@ -569,7 +686,7 @@ static int batch_scan_smem(int stages) {
 }
 
 template <int KB>
-static cudaError_t launch_batch_scan_t(const void* qmap, const void* xmap, const BatchScanParams& P, int max_pairs,
+static cudaError_t launch_batch_scan(const void* qmap, const void* xmap, const BatchScanParams& P, int max_pairs,
                                        cudaStream_t st) {
   const int smem = batch_scan_smem(P.stages);
   static int configured = 0;
@@ -658,28 +775,29 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   P.err = bw.err;
   P.seed_only = 0;
   P.slice_rows = SLICE_ROWS;
+  P.row_step = 1;
   alignas(64) unsigned char qmap[128];
   if (!make_rows_tensor_map(Q, B, ix.D, qmap)) return cudaErrorInvalidValue;
   const int max_pairs = bw.sms / 2;
-  // the per-thread top-k array is sized for k (16 / 32 / 64 / 128 entries); it
-  // is touched only on the epilogue's rare path
+  // k <= 32: per-thread top-k in registers (its threshold rises on every
+  // insertion); larger k: slot thresholds, no per-thread list
   auto scan = [&](const void* xmap, const BatchScanParams& PP) -> cudaError_t {
-    if (k <= 16) return launch_batch_scan_t<16>(qmap, xmap, PP, max_pairs, st);
-    if (k <= 32) return launch_batch_scan_t<32>(qmap, xmap, PP, max_pairs, st);
-    if (k <= 64) return launch_batch_scan_t<64>(qmap, xmap, PP, max_pairs, st);
-    return launch_batch_scan_t<128>(qmap, xmap, PP, max_pairs, st);
+    if (k <= 16) return launch_batch_scan<16>(qmap, xmap, PP, max_pairs, st);
+    if (k <= 32) return launch_batch_scan<32>(qmap, xmap, PP, max_pairs, st);
+    return launch_batch_scan<0>(qmap, xmap, PP, max_pairs, st);
   };
   if (ev_scan_begin && (e = cudaEventRecord(ev_scan_begin, st)) != cudaSuccess) return e;
   if (bw.sample_rows > 0) {
     // threshold pass over up to 32,768 rows spread evenly through the corpus,
-    // one unit per query tile: every query starts the main pass from the k-th
-    // best of these rows instead of -inf (any k rows give a valid threshold),
+    // one unit per query tile: it fills every query's slots, so the main pass
+    // starts from the k-th best of k distinct sampled rows instead of -inf,
     // which removes most cold-start candidates and rare-path epilogue work
     BatchScanParams S = P;
     S.N = bw.sample_rows;
     S.units = P.QP;
     S.seed_only = 1;
-    S.slice_rows = SEED_ROWS;  // one unit per query tile: its k best over all sampled rows
+    S.slice_rows = SEED_ROWS;  // one unit per query tile
+    S.row_step = sample_step(ix.N);
     if ((e = scan(bw.smap, S)) != cudaSuccess) return e;
   }
   if ((e = scan(bw.tmap, P)) != cudaSuccess) return e;

@@ -104,12 +104,12 @@ cudaError_t launch_flat_scan(const float* leaf, int D, int N, const float* q, in
 
 // ---- batched search (batch_kernels.cu) ----
 constexpr int BATCH_MAX_DIM = 2048;  // the rescoring keeps the query in registers (16 float4 per lane)
-constexpr int BATCH_MAX_K = 128;  // per-thread top-k of the scan epilogue (16 / 32 / 64 / 128)
+constexpr int BATCH_MAX_K = KMAX;  // any k of the single-query search
 constexpr int BATCH_CAND_CAP = 16384;  // candidate rows appended per query
 
 struct BatchWorkspace {
   uint32_t* theta = nullptr;      // [capacity] running k-th best keys
-  uint32_t* slots = nullptr;      // [capacity * BATCH_MAX_K] rotated top-k publication
+  uint32_t* slots = nullptr;      // [capacity * BATCH_MAX_K] per-query threshold slots
   int* cand_count = nullptr;      // [capacity]
   unsigned long long* cand = nullptr;  // [capacity * cap] tf32 key << 32 | row
   int* overflow = nullptr;        // queries whose candidate list overflowed

@@ -517,7 +517,7 @@ int circuit_index_opaque::ensure_batch(int B) {
     bw.overflow = (int*)grab(sizeof(int), "cudaMalloc(overflow)");
     bw.queries = (float*)grab(sizeof(float) * (size_t)cap_B * D, "cudaMalloc(batch queries)");
     bw.qband = (float*)grab(sizeof(float) * (size_t)cap_B, "cudaMalloc(batch bands)");
-    // staging for the host-buffer call: any k up to KMAX (k > BATCH_MAX_K is answered per query)
+    // staging for the host-buffer call: any k up to KMAX
     bw.out_scores = (float*)grab(sizeof(float) * (size_t)cap_B * cb::KMAX, "cudaMalloc(batch scores)");
     bw.out_ids = (int*)grab(sizeof(int) * (size_t)cap_B * cb::KMAX, "cudaMalloc(batch ids)");
     if (!bw.theta || !bw.slots || !bw.cand_count || !bw.cand || !bw.overflow || !bw.queries || !bw.qband || !bw.out_scores ||
@@ -536,21 +536,6 @@ int circuit_index_opaque::search_batch_async(const float* dq, int B, int k, floa
   if (k < 1 || k > cb::KMAX) {
     set_error("batched search supports 1 <= k <= " + std::to_string(cb::KMAX));
     return CIRCUIT_ERR_UNSUPPORTED;
-  }
-  if (k > cb::BATCH_MAX_K) {
-    // beyond the tensor-core path's per-thread top-k: the single-query search,
-    // query after query on the same stream (same results, same workspace)
-    if (!dq || !dscores || !dids || ((uintptr_t)dq & 15) || (D * 4) % 16) {
-      set_error("null or misaligned batch pointer");
-      return CIRCUIT_ERR_ARG;
-    }
-    have_host_ctrl = false;
-    for (int q = 0; q < B; ++q) {
-      const int rc = search_async(dq + (size_t)q * D, k, 0, dscores + (size_t)q * k, dids + (size_t)q * k, nullptr, st,
-                                  nullptr, nullptr);
-      if (rc != CIRCUIT_OK) return rc;
-    }
-    return CIRCUIT_OK;
   }
   if (D > cb::BATCH_MAX_DIM || D % 4 != 0) {
     set_error("batched search supports dim <= " + std::to_string(cb::BATCH_MAX_DIM) + " with dim % 4 == 0");
@@ -615,7 +600,7 @@ int circuit_search_batch(circuit_index_t index, const float* host_queries, int n
       !cuda_ok(cudaStreamSynchronize(st), "batch sync"))
     return CIRCUIT_ERR_CUDA;
   // a query whose candidate list overflowed is answered by the single-query search
-  for (int q = 0; q < num_queries && k <= cb::BATCH_MAX_K; ++q) {
+  for (int q = 0; q < num_queries; ++q) {
     if (host_ids[(size_t)q * k] != -2) continue;
     rc = index->search_blocking(host_queries + (size_t)q * index->D, true, k, host_scores + (size_t)q * k,
                                 host_ids + (size_t)q * k, nullptr);

@@ -175,9 +175,8 @@ int circuit_search_finish_async(circuit_index_t index, const float* dev_query, i
  * (original ids, scores descending).  One tf32 tcgen05 pass over all leaf rows
  * selects candidates within a rigorous error band of each query's running
  * k-th best; the candidates are rescored exactly in fp32, so results equal
- * the single-query search's.  Limits: dim <= 2048 with dim % 4 == 0; k <= 128
- * runs on the tensor cores, 128 < k <= 256 is answered query by query by the
- * single-query search on the same stream (CIRCUIT_ERR_UNSUPPORTED beyond).
+ * the single-query search's.  Limits: dim <= 2048 with dim % 4 == 0,
+ * 1 <= k <= 256 (CIRCUIT_ERR_UNSUPPORTED otherwise).
  * A query with more than 16384 rows
  * appended, or more than 8192 rows inside the band of its final threshold
  * (thousands of near-identical rows), gets id -2 in its first slot;

@@ -147,8 +147,8 @@ def test_batch_rejects_unsupported():
 
 @pytest.mark.parametrize("k", [64, 100, 128, 200])
 def test_batch_large_k_host_buffers(k):
-    """Host-buffer batched call at large k: 64 / 100 / 128 on the tensor cores,
-    200 query by query; results identical to the single-query search."""
+    """Host-buffer batched call at large k (all on the tensor cores); results
+    identical to the single-query search."""
     w = WORKLOADS["zipf-10m"]
     X = w.corpus(0, 30_000, device=DEV)
     index = build_circuit_index(X, num_roots=32, children_per_root=8, rank=16, device=DEV)
@@ -162,8 +162,8 @@ def test_batch_large_k_host_buffers(k):
 
 
 def test_batch_large_k_matches_single_query():
-    """k = 100 (the zipf-10m configuration's k) on the tensor-core path (per-thread
-    top-k of 128 entries), same results as the single-query search."""
+    """k = 100 (the zipf-10m configuration's k): same results as the single-query
+    search."""
     w = WORKLOADS["zipf-10m"]
     X = w.corpus(0, 40_000, device=DEV)
     index = build_circuit_index(X, num_roots=32, children_per_root=8, rank=16, device=DEV)
