@@ -171,3 +171,16 @@ def test_batch_large_k_matches_single_query():
     scores, ids = circuit_search_batch(Q, index, 100)
     assert scores.shape == (24, 100)
     _check_batch(X, Q, index, 100, scores, ids)
+
+
+@pytest.mark.parametrize("k", [10, 50, 100])
+def test_batch_threshold_pass_and_slots(k):
+    """120K rows: the threshold pass over sampled rows runs (corpora of 65,536
+    rows and more), k = 10 takes the per-thread top-k epilogue, k = 50 / 100 the
+    slot thresholds; results equal the single-query search's."""
+    w = WORKLOADS["mixed-100m"]
+    X = w.corpus(0, 120_000, device=DEV)
+    index = build_circuit_index(X, num_roots=32, children_per_root=8, rank=8, device=DEV)
+    Q = w.query_batch(300, device=DEV)
+    scores, ids = circuit_search_batch(Q, index, k)
+    _check_batch(X, Q[:60], index, k, scores[:60], ids[:60])
