@@ -64,6 +64,8 @@ constexpr int A_BYTES = BQ * 128;        // 128 query rows x 32 floats
 constexpr int B_BYTES = HALF_N * 128;    // 128 leaf rows x 32 floats
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 
+constexpr int UNIT_RING = 4;             // unit ids published ahead of their consumers
+
 struct BatchScanParams {
   const float* Q;        // [B, D]
   int B, D, N, k;
@@ -80,6 +82,7 @@ struct BatchScanParams {
   int seed_only;         // threshold pass: raise theta, append no candidates
   uint32_t* slots;       // [B * k] per-query threshold slots (slot_min)
   int row_step;          // leaf row = scan row * row_step (threshold pass: sampled rows)
+  int* unit_counter;     // next work unit (dynamic scheduling; zeroed before the launch)
   int slice_rows;        // rows per work unit
 };
 
@@ -197,6 +200,26 @@ __device__ __forceinline__ bool epi_pass(const uint32_t (&sc0)[32], const uint32
 // pair's accumulator holds, in CTA r's TMEM lanes, its 128 queries against all
 // 256 rows of the tile (columns 0-127: rows loaded by the even CTA, 128-255:
 // by the odd CTA).
+// Dynamic work units.  The even CTA's producer takes the next unit from a global
+// counter and publishes its id into a 4-deep ring in both CTAs' shared memory
+// (full barriers, one arrival each); the odd CTA's producer, the MMA warp and
+// the 8 epilogue warps take ids in order and release each slot on the even
+// CTA's empty barrier (10 arrivals).  Units in flight across the GPU are then
+// about 74 consecutive ids -- a few consecutive row slices -- so the rows of a
+// slice are read from HBM about once and from L2 by its 16 query tiles, which
+// static round-robin dealing lost as pairs drifted apart.  Id -1 ends the loops.
+__device__ __forceinline__ int take_unit(uint64_t* unit_full, const int* ring, uint32_t lead_unit_empty, int& ui,
+                                         bool warp_release, int* err) {
+  const int r = ui & (UNIT_RING - 1);
+  const uint32_t ph = (uint32_t)(ui / UNIT_RING) & 1u;
+  ++ui;
+  const bool got = tc::mbar_wait_cluster(&unit_full[r], ph, err, ERR_TIMEOUT_FULL);
+  const int u = got ? *reinterpret_cast<const volatile int*>(ring + r) : -1;
+  if (warp_release) __syncwarp();
+  if (!warp_release || (threadIdx.x & 31) == 0) tc::mbar_arrive_cluster(lead_unit_empty + 8u * (uint32_t)r);
+  return u;
+}
+
 // KB > 0: per-thread top-KB epilogue (k <= KB); KB == 0: slot thresholds (any k).
 template <int KB>
 __global__ void __launch_bounds__(BATCH_THREADS, 1)
@@ -208,12 +231,13 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
   // full / acc_empty are used in the even CTA only; empty / acc_full in both
   // (the even CTA's MMA thread commits to its own and to the odd CTA's copy).
   __shared__ uint64_t full[BATCH_MAX_STAGES], empty[BATCH_MAX_STAGES], acc_full[2], acc_empty[2], drain;
+  __shared__ uint64_t unit_full[UNIT_RING], unit_empty[UNIT_RING];
+  __shared__ int unit_ring[UNIT_RING];
   __shared__ uint32_t tmem_base;
   __shared__ int s_err;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = tc::cluster_ctarank();
   const bool leader = rank == 0;
-  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int S = P.stages;
   float* stash = reinterpret_cast<float*>(smem + (size_t)S * STAGE_BYTES);  // [64][BQ] scores
 
@@ -227,6 +251,10 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
       mbar_init(&acc_empty[b], 8);  // one lane of each epilogue warp of both CTAs
     }
     mbar_init(&drain, 1);
+    for (int r = 0; r < UNIT_RING; ++r) {
+      mbar_init(&unit_full[r], 1);
+      mbar_init(&unit_empty[r], 10);  // odd producer + MMA warp + 8 epilogue warps
+    }
     tc::fence_mbar_init_cluster();
   }
   if (warp == 5) tc::tmem_alloc_pair(&tmem_base, 512);
@@ -238,15 +266,35 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
   const uint32_t lead_acc_empty = tc::mapa_shared(smem_u32(&acc_empty[0]), 0);
   const uint32_t empty0 = tc::mapa_shared(smem_u32(&empty[0]), 0), empty1 = tc::mapa_shared(smem_u32(&empty[0]), 1);
   const uint32_t accf0 = tc::mapa_shared(smem_u32(&acc_full[0]), 0), accf1 = tc::mapa_shared(smem_u32(&acc_full[0]), 1);
+  const uint32_t lead_unit_empty = tc::mapa_shared(smem_u32(&unit_empty[0]), 0);
 
   if (warp == 4) {
     // ---------------------------------------------------------- TMA producer (both CTAs)
     // The stage index and its phase advance incrementally (no division in the loop).
     if (lane == 0) {
-      int s = 0, c = 0;
+      int s = 0, c = 0, ui = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int u = pair; u < P.units && ok; u += npairs) {
+      const uint32_t peer_ring = tc::mapa_shared(smem_u32(&unit_ring[0]), 1);
+      const uint32_t peer_unit_full = tc::mapa_shared(smem_u32(&unit_full[0]), 1);
+      while (ok) {
+        int u;
+        if (leader) {
+          // publish the next unit into both CTAs' rings (-1: none left)
+          const int r = ui & (UNIT_RING - 1), round = ui / UNIT_RING;
+          ++ui;
+          const bool free_slot =
+              round == 0 || tc::mbar_wait_cluster(&unit_empty[r], (uint32_t)(round - 1) & 1u, P.err, ERR_TIMEOUT_EMPTY);
+          const int n = free_slot ? atomicAdd(P.unit_counter, 1) : P.units;
+          u = n < P.units ? n : -1;
+          *reinterpret_cast<volatile int*>(&unit_ring[r]) = u;
+          tc::st_cluster_s32(peer_ring + 4u * (uint32_t)r, u);
+          mbar_arrive(&unit_full[r]);
+          tc::mbar_arrive_cluster(peer_unit_full + 8u * (uint32_t)r);
+        } else {
+          u = take_unit(unit_full, unit_ring, lead_unit_empty, ui, false, P.err);
+        }
+        if (u < 0) break;
         const int qp = u % P.QP, slice = u / P.QP;
         const int qrow = qp * (2 * BQ) + (int)rank * BQ;
         const int r0 = slice * P.slice_rows, r1 = min(P.N, r0 + P.slice_rows);
@@ -278,10 +326,12 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
       const uint32_t idesc = tc::idesc_tf32(2 * BQ, BN);
       const uint32_t sbase = smem_u32(smem);
       const uint64_t dA0 = tc::sdesc_k_sw128(sbase), dB0 = tc::sdesc_k_sw128(sbase + A_BYTES);
-      int s = 0, it = 0;
+      int s = 0, it = 0, ui = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int u = pair; u < P.units && ok; u += npairs) {
+      while (ok) {
+        const int u = __shfl_sync(FULL_MASK, take_unit(unit_full, unit_ring, lead_unit_empty, ui, true, P.err), 0);
+        if (u < 0) break;
         const int slice = u / P.QP;
         const int r0 = slice * P.slice_rows, r1 = min(P.N, r0 + P.slice_rows);
         for (int row0 = r0; row0 < r1 && ok; row0 += BN, ++it) {
@@ -322,9 +372,11 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
   } else {
     // ---------------------------------------------------------- epilogue (one query per thread)
     const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-    int it = 0;
+    int it = 0, ui = 0;
     bool ok = true;
-    for (int u = pair; u < P.units && ok; u += npairs) {
+    while (ok) {
+      const int u = __shfl_sync(FULL_MASK, take_unit(unit_full, unit_ring, lead_unit_empty, ui, true, P.err), 0);
+      if (u < 0) break;
       const int qp = u % P.QP, slice = u / P.QP;
       const int q = qp * (2 * BQ) + (int)rank * BQ + 32 * warp + lane;
       const bool qv = q < P.B;
@@ -747,6 +799,7 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   if ((e = cudaMemsetAsync(bw.cand_count, 0, sizeof(int) * B, st)) != cudaSuccess) return e;
   if ((e = cudaMemsetAsync(bw.overflow, 0, sizeof(int), st)) != cudaSuccess) return e;
   if ((e = cudaMemsetAsync(bw.slots, 0, sizeof(uint32_t) * (size_t)B * k, st)) != cudaSuccess) return e;
+  if ((e = cudaMemsetAsync(bw.unit_counter, 0, 2 * sizeof(int), st)) != cudaSuccess) return e;
   BatchScanParams P{};
   P.Q = Q;
   P.B = B;
@@ -776,6 +829,7 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   P.seed_only = 0;
   P.slice_rows = SLICE_ROWS;
   P.row_step = 1;
+  P.unit_counter = bw.unit_counter;
   alignas(64) unsigned char qmap[128];
   if (!make_rows_tensor_map(Q, B, ix.D, qmap)) return cudaErrorInvalidValue;
   const int max_pairs = bw.sms / 2;
@@ -798,6 +852,7 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
     S.seed_only = 1;
     S.slice_rows = SEED_ROWS;  // one unit per query tile
     S.row_step = sample_step(ix.N);
+    S.unit_counter = bw.unit_counter + 1;
     if ((e = scan(bw.smap, S)) != cudaSuccess) return e;
   }
   if ((e = scan(bw.tmap, P)) != cudaSuccess) return e;

@@ -110,6 +110,7 @@ constexpr int BATCH_CAND_CAP = 16384;  // candidate rows appended per query
 struct BatchWorkspace {
   uint32_t* theta = nullptr;      // [capacity] running k-th best keys
   uint32_t* slots = nullptr;      // [capacity * BATCH_MAX_K] per-query threshold slots
+  int* unit_counter = nullptr;    // [2] work-unit counters (main pass, threshold pass)
   int* cand_count = nullptr;      // [capacity]
   unsigned long long* cand = nullptr;  // [capacity * cap] tf32 key << 32 | row
   int* overflow = nullptr;        // queries whose candidate list overflowed

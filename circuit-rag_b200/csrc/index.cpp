@@ -515,12 +515,13 @@ int circuit_index_opaque::ensure_batch(int B) {
     bw.cand_count = (int*)grab(sizeof(int) * cap_B, "cudaMalloc(cand_count)");
     bw.cand = (unsigned long long*)grab(sizeof(unsigned long long) * (size_t)cap_B * bw.cap, "cudaMalloc(cand)");
     bw.overflow = (int*)grab(sizeof(int), "cudaMalloc(overflow)");
+    bw.unit_counter = (int*)grab(2 * sizeof(int), "cudaMalloc(unit counters)");
     bw.queries = (float*)grab(sizeof(float) * (size_t)cap_B * D, "cudaMalloc(batch queries)");
     bw.qband = (float*)grab(sizeof(float) * (size_t)cap_B, "cudaMalloc(batch bands)");
     // staging for the host-buffer call: any k up to KMAX
     bw.out_scores = (float*)grab(sizeof(float) * (size_t)cap_B * cb::KMAX, "cudaMalloc(batch scores)");
     bw.out_ids = (int*)grab(sizeof(int) * (size_t)cap_B * cb::KMAX, "cudaMalloc(batch ids)");
-    if (!bw.theta || !bw.slots || !bw.cand_count || !bw.cand || !bw.overflow || !bw.queries || !bw.qband || !bw.out_scores ||
+    if (!bw.theta || !bw.slots || !bw.unit_counter || !bw.cand_count || !bw.cand || !bw.overflow || !bw.queries || !bw.qband || !bw.out_scores ||
         !bw.out_ids) {
       bw.capacity = 0;
       return CIRCUIT_ERR_CUDA;
