@@ -1,13 +1,17 @@
 // Batched exact top-k search on the B200 tensor cores.
 //
+// k_query_bands  warp per query: the error band 2 eps (below) of each query.
 // k_batch_scan  persistent CTA pairs (clusters of 2, one CTA per SM) computing
 //               the score matrix Q X^T tile by tile with 2-SM tcgen05 MMAs
 //               (cta_group::2, kind::tf32, M = 256 queries, N = 256 leaf rows,
 //               K = 8) and filtering it in the epilogue; no score matrix is
 //               ever written.  A work unit is (query tile of 256 queries, slice
-//               of 8,192 leaf rows); units are dealt round-robin in slice-major
-//               order so the pairs in flight read the same slices and the leaf
-//               rows come from HBM once, then from L2.
+//               of 8,192 leaf rows); units are taken in slice-major order from
+//               a global counter (dynamic scheduling), so the units in flight
+//               share a few consecutive slices and every leaf row comes from
+//               HBM about once, then from L2.  Launched twice per batch: a
+//               threshold pass over up to 32,768 evenly spaced rows (one unit
+//               per query tile, no candidates), then the main pass.
 //               - a TMA warp per CTA streams 32-column K-chunks of its 128
 //                 queries and of its 128 leaf rows of the tile (fp32, 128-byte
 //                 swizzle) through a 6-stage shared-memory ring; completion is
@@ -15,22 +19,24 @@
 //               - the even CTA's MMA warp issues the pair's MMAs (both operands
 //                 from shared memory) into one of two 256-column TMEM
 //                 accumulators and commits to the barriers of both CTAs, so the
-//                 epilogue of tile t overlaps the MMAs of tile t + 1;
+//                 epilogue of tile t overlaps the MMAs of tile t + 1; its issue
+//                 loop is kept lean (one MMA instruction takes only ~70 ns);
 //               - each epilogue thread owns one query: it reads its 256 scores
-//                 in four 64-column passes with tcgen05.ld, keeps its k best
-//                 tf32 scores in registers, and appends every row whose tf32
-//                 score is within `band` of the running k-th best (max of its
-//                 own and the query's global atomicMax threshold) to the
-//                 query's candidate list, with its tf32 score.
-//               Dependent MMAs into one accumulator are latency-bound, so a
-//               1-SM design that keeps the queries resident in TMEM (384 of 512
-//               columns at D = 384) is capped near half the tensor peak by the
-//               128 accumulator columns left; streaming both operands frees all
-//               512 columns for two N = 256 accumulators.
-// k_batch_rescore  one CTA per query: drops the candidates below the final
-//               threshold minus the band, scores the rest exactly in fp32 (the
-//               same arithmetic as the single-query scan, so both paths return
-//               identical scores), radix select, original ids.
+//                 with tcgen05.ld, and appends every row whose tf32 score is
+//                 within `band` of the query's running threshold to the
+//                 query's candidate list, with its tf32 score.  The threshold
+//                 is always the tf32 score of the k-th best of k distinct rows:
+//                 for k <= 32 a per-thread top-k in registers plus rotated
+//                 per-query slots, for larger k slots keyed by row (see
+//                 slot_min).
+//               Both operands are streamed: with the queries resident in TMEM
+//               (384 of 512 columns at D = 384) only N = 64 accumulators fit,
+//               4x the MMA instructions per flop of N = 256.
+// k_batch_rescore  one CTA per query: threshold = max(final scan threshold, the
+//               k-th best tf32 score among its own candidates); drops the
+//               candidates below it minus the band, scores the rest exactly in
+//               fp32 (the same arithmetic as the single-query scan, so both
+//               paths return identical scores), radix select, original ids.
 //
 // Exactness: with eps >= |tf32 score - fp32 score| for every row (bound:
 // (2^-9 + 2^-20 + 2D 2^-23 + gamma_D) ||q|| max||x||, tf32 truncation of both
