@@ -23,7 +23,8 @@
  *     when CUDA calls fail); circuit_last_error() describes the last one.
  *
  * Threading: one in-flight search per index handle (the handle owns one
- * device workspace), as in the reference.  Use one handle per thread/stream.
+ * device workspace for single queries and one for batches, each used by one
+ * call at a time), as in the reference.  Use one handle per thread/stream.
  */
 #ifndef CIRCUIT_H
 #define CIRCUIT_H
