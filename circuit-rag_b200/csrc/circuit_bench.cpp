@@ -1,8 +1,10 @@
 // circuit_bench: native latency / throughput bench over a .circuit file.
 // Same command line as the reference (reference native/bin/circuit_bench.cpp:11-153):
-//     circuit_bench [path.circuit] [k] [num_queries]
+//     circuit_bench [path.circuit] [k] [num_queries] [batch]
 // Host-to-host queries (pinned host buffers, H2D + search + D2H per query) and
-// in-VRAM queries, p50/p90/p99/mean latency and QPS, then one JSON line.
+// in-VRAM queries, p50/p90/p99/mean latency and QPS, then one JSON line.  With
+// a fourth argument B > 0 it also times batches of B queries through
+// circuit_search_batch (host buffers; no reference counterpart).
 // Differences: dim is read from the index (the reference hard-codes 384), k and
 // the query count are optional arguments, errors are reported.
 #include <cuda_runtime.h>
@@ -33,8 +35,9 @@ int main(int argc, char** argv) {
   const char* path = argc > 1 ? argv[1] : "data/scifact_index.circuit";
   const int k = argc > 2 ? std::atoi(argv[2]) : 10;
   const int nq = argc > 3 ? std::atoi(argv[3]) : 500;
-  if (k < 1 || nq < 1) {
-    std::fprintf(stderr, "usage: circuit_bench [path.circuit] [k] [num_queries]\n");
+  const int nb = argc > 4 ? std::atoi(argv[4]) : 0;
+  if (k < 1 || nq < 1 || nb < 0) {
+    std::fprintf(stderr, "usage: circuit_bench [path.circuit] [k] [num_queries] [batch]\n");
     return 2;
   }
   auto t0 = std::chrono::steady_clock::now();
@@ -101,12 +104,30 @@ int main(int argc, char** argv) {
   b1 = std::chrono::steady_clock::now();
   summarize("in-VRAM", lat, std::chrono::duration<double, std::milli>(b1 - b0).count(), &p50_d, &qps_d);
 
+  double batch_qps = 0.0, batch_ms = 0.0;
+  if (nb > 0) {
+    std::vector<float> hq((size_t)nb * dim), hs((size_t)nb * k);
+    std::vector<int> hi((size_t)nb * k);
+    for (auto& v : hq) v = dist(rng);
+    if (circuit_search_batch(index, hq.data(), nb, k, hs.data(), hi.data()) != 0) {  // warm-up (workspace)
+      std::fprintf(stderr, "batched search failed: %s\n", circuit_last_error());
+      return 1;
+    }
+    const int reps = 3;
+    auto c0 = std::chrono::steady_clock::now();
+    for (int r = 0; r < reps; ++r) circuit_search_batch(index, hq.data(), nb, k, hs.data(), hi.data());
+    auto c1 = std::chrono::steady_clock::now();
+    batch_ms = std::chrono::duration<double, std::milli>(c1 - c0).count() / reps;
+    batch_qps = nb / batch_ms * 1000.0;
+    std::printf("%-14s %9.2f ms per batch of %d | %10.1f q/s\n", "batched", batch_ms, nb, batch_qps);
+  }
+
   std::printf("\nsample top-%d (last host query):\n", k);
   for (int i = 0; i < std::min(k, 10); ++i) std::printf("  rank %2d | id %9d | score %.6f\n", i + 1, h_ids[i], h_scores[i]);
   std::printf("{\"bench\": \"circuit_bench\", \"N\": %lld, \"dim\": %d, \"k\": %d, \"queries\": %d, "
               "\"host_p50_us\": %.3f, \"host_qps\": %.1f, \"vram_p50_us\": %.3f, \"vram_qps\": %.1f, "
-              "\"mean_vectors_scored\": %.1f}\n",
-              (long long)info[4], dim, k, nq, p50_h, qps_h, p50_d, qps_d, (double)scored / nq);
+              "\"mean_vectors_scored\": %.1f, \"batch\": %d, \"batch_ms\": %.3f, \"batch_qps\": %.1f}\n",
+              (long long)info[4], dim, k, nq, p50_h, qps_h, p50_d, qps_d, (double)scored / nq, nb, batch_ms, batch_qps);
   circuit_destroy_index(index);
   cudaFree(d_query);
   cudaFree(d_scores);

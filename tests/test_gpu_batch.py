@@ -58,6 +58,7 @@ def test_batch_many_ties_within_capacity():
     ("clustered-50k", 20_011, 128),
     (None, 9_000, 100),
     (None, 6_000, 1028),
+    (None, 3_000, 2048),
 ])
 @pytest.mark.parametrize("k", [1, 10, 32])
 def test_batch_matches_single_query_and_oracle(name, n, dim, k):

@@ -246,3 +246,23 @@ def test_search_after_append_is_exact():
     bs, bi = circuit_search_batch(Q, idx, k=10)
     for b in range(Q.shape[0]):
         _check(X, Q[b], 10, bs[b], bi[b])
+
+
+def test_circuit_bench_binary_runs(tmp_path):
+    """The native bench (reference command line plus an optional batch size)
+    loads a .circuit file, runs host, in-VRAM and batched queries, prints JSON."""
+    import json
+    import subprocess
+
+    binary = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "circuit-rag_b200", "csrc",
+                          "_build", "circuit_bench")
+    if not os.path.exists(binary):
+        pytest.skip("circuit_bench not built")
+    w = WORKLOADS["spread-5k"]
+    idx = build_circuit_index(w.corpus(0, 5183, device=DEV), num_roots=16, children_per_root=4, rank=8, device=DEV)
+    path = str(tmp_path / "b.circuit")
+    idx.save(path)
+    out = subprocess.run([binary, path, "10", "50", "256"], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr
+    line = json.loads([x for x in out.stdout.splitlines() if x.startswith("{")][-1])
+    assert line["N"] == 5183 and line["batch"] == 256 and line["batch_qps"] > 0 and line["host_qps"] > 0
