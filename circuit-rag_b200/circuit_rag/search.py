@@ -135,8 +135,9 @@ def circuit_search_batch(queries: torch.Tensor, index: CircuitIndex, k: int = 10
     k-th best, and those rows are rescored exactly in fp32.  Returns (scores
     [B, k] float32 descending, original ids [B, k] int32), 1 <= k <= 256.
     A query whose candidate list overflows
-    (more than 8192 rows inside the band, e.g. thousands of near-identical
-    rows) is answered by circuit_search."""
+    (more rows inside the error band than the batch's candidate pool holds:
+    16,384 per query for 4,096 queries, up to 65,536 for smaller batches) is
+    answered by circuit_search."""
     if queries.ndim != 2 or queries.shape[1] != index.dim:
         raise ValueError("queries must have shape [B, index.dim]")
     if not index.is_cuda:

@@ -557,12 +557,14 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
 }
 
 // One CTA per query.  The candidate list was appended against running
-// thresholds; the query's final threshold (k-th best tf32 score of k rows) is
-// tighter, so candidates whose tf32 score is below it minus the band are
-// dropped first.  The survivors are scored exactly in fp32 (the single-query
-// scan's arithmetic: per-lane float4 FMAs, xor-tree reduction 16..1), then
-// selected.
-constexpr int RESCORE_SMEM_ROWS = 8192;
+// thresholds; the query's final threshold (the larger of the scan's and the
+// k-th best tf32 score among the candidates themselves -- k real rows either
+// way) is tighter, so candidates whose tf32 score is below it minus the band are
+// dropped.  The rest are scored exactly in fp32 (the single-query scan's
+// arithmetic: per-lane float4 FMAs, xor-tree reduction 16..1) in rounds of up
+// to 8,192 candidates, each round merged with the running exact top-k, so any
+// number of candidates fits.
+constexpr int RESCORE_CHUNK = 8192;
 
 template <int VPL>
 __global__ void __launch_bounds__(256) k_batch_rescore(const float* __restrict__ Q, const float* __restrict__ leaf,
@@ -574,13 +576,23 @@ __global__ void __launch_bounds__(256) k_batch_rescore(const float* __restrict__
                                                        float* __restrict__ out_s, int* __restrict__ out_i,
                                                        int* __restrict__ overflow) {
   extern __shared__ __align__(16) unsigned char smem[];
-  unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem);
-  unsigned long long* sel = cand + RESCORE_SMEM_ROWS;
-  SelectScratch* scratch = reinterpret_cast<SelectScratch*>(sel + BATCH_MAX_K);
+  unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem);  // [RESCORE_CHUNK + BATCH_MAX_K]
+  unsigned long long* sel = cand + RESCORE_CHUNK + BATCH_MAX_K;            // [BATCH_MAX_K]
+  unsigned long long* run = sel + BATCH_MAX_K;                             // [BATCH_MAX_K] running top-k
+  SelectScratch* scratch = reinterpret_cast<SelectScratch*>(run + BATCH_MAX_K);
   __shared__ int s_n;
   const int q = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int total = cand_count[q];
+  if (total > cap) {  // the appended list overflowed: this query must be answered another way
+    if (threadIdx.x == 0) atomicAdd(overflow, 1);
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+      out_s[(size_t)q * k + i] = -INFINITY;
+      out_i[(size_t)q * k + i] = -2;
+    }
+    return;
+  }
+  const unsigned long long* in = cand_in + (size_t)q * cap;
   const int D4 = D >> 2;
   const float4* q4 = reinterpret_cast<const float4*>(Q + (size_t)q * D);
   float4 qv[VPL];
@@ -589,65 +601,54 @@ __global__ void __launch_bounds__(256) k_batch_rescore(const float* __restrict__
     const int c = lane + 32 * v;
     qv[v] = c < D4 ? __ldg(q4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  if (threadIdx.x == 0) s_n = 0;
-  __syncthreads();
   int selN = 1;
   while (selN < k) selN <<= 1;
-  bool over = total > cap;
-  if (!over) {
-    // threshold: the larger of the scan's final one and the k-th best tf32
-    // score among the candidates themselves (k real rows either way), minus
-    // the band
-    uint32_t tk = theta[q];
-    if (total >= k) {
-      block_select_topk<true>(cand_in + (size_t)q * cap, total, k, sel, selN, scratch);
-      const uint32_t ck = (uint32_t)(sel[k - 1] >> 32);
-      tk = ck > tk ? ck : tk;
-    }
-    const float lim = tk ? key2f(tk) - qband[q] : -INFINITY;
-    for (int i = threadIdx.x; i < total; i += blockDim.x) {
-      const unsigned long long e = cand_in[(size_t)q * cap + i];
-      if (key2f((uint32_t)(e >> 32)) >= lim) {
-        const int slot = atomicAdd(&s_n, 1);
-        if (slot < RESCORE_SMEM_ROWS) cand[slot] = e & 0xFFFFFFFFull;
-      }
+  uint32_t tk = theta[q];
+  if (total >= k) {
+    block_select_topk<true>(in, total, k, sel, selN, scratch);
+    const uint32_t ck = (uint32_t)(sel[k - 1] >> 32);
+    tk = ck > tk ? ck : tk;
+  }
+  const float lim = tk ? key2f(tk) - qband[q] : -INFINITY;
+  int run_n = 0;
+  for (int base = 0; base < total; base += RESCORE_CHUNK) {
+    if (threadIdx.x == 0) s_n = 0;
+    __syncthreads();
+    const int end = min(total, base + RESCORE_CHUNK);
+    for (int i = base + threadIdx.x; i < end; i += blockDim.x) {
+      const unsigned long long e = in[i];
+      if (key2f((uint32_t)(e >> 32)) >= lim) cand[atomicAdd(&s_n, 1)] = e & 0xFFFFFFFFull;
     }
     __syncthreads();
-    over = s_n > RESCORE_SMEM_ROWS;
-  }
-  if (over) {  // this query must be answered another way
-    if (threadIdx.x == 0) atomicAdd(overflow, 1);
-    for (int i = threadIdx.x; i < k; i += blockDim.x) {
-      out_s[(size_t)q * k + i] = -INFINITY;
-      out_i[(size_t)q * k + i] = -2;
-    }
-    return;
-  }
-  const int n = s_n;
-  for (int i = warp; i < n; i += nw) {
-    const int row = (int)(uint32_t)cand[i];
-    const float4* x4 = reinterpret_cast<const float4*>(leaf + (size_t)row * D);
-    float acc = 0.f;
+    const int n = s_n;
+    for (int i = warp; i < n; i += nw) {
+      const int row = (int)(uint32_t)cand[i];
+      const float4* x4 = reinterpret_cast<const float4*>(leaf + (size_t)row * D);
+      float acc = 0.f;
 #pragma unroll
-    for (int v = 0; v < VPL; ++v) {
-      const int c = lane + 32 * v;
-      if (c < D4) {
-        const float4 x = __ldg(x4 + c);
-        acc = fmaf(x.x, qv[v].x, acc);
-        acc = fmaf(x.y, qv[v].y, acc);
-        acc = fmaf(x.z, qv[v].z, acc);
-        acc = fmaf(x.w, qv[v].w, acc);
+      for (int v = 0; v < VPL; ++v) {
+        const int c = lane + 32 * v;
+        if (c < D4) {
+          const float4 x = __ldg(x4 + c);
+          acc = fmaf(x.x, qv[v].x, acc);
+          acc = fmaf(x.y, qv[v].y, acc);
+          acc = fmaf(x.z, qv[v].z, acc);
+          acc = fmaf(x.w, qv[v].w, acc);
+        }
       }
-    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(FULL_MASK, acc, o);
-    __syncwarp();
-    if (lane == 0) cand[i] = pack_cand(f2key(acc), (uint32_t)row);
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(FULL_MASK, acc, o);
+      __syncwarp();
+      if (lane == 0) cand[i] = pack_cand(f2key(acc), (uint32_t)row);
+    }
+    for (int i = threadIdx.x; i < run_n; i += blockDim.x) cand[n + i] = run[i];  // merge the running top-k
+    __syncthreads();
+    run_n = block_select_topk<false>(cand, n + run_n, k, sel, selN, scratch);
+    for (int i = threadIdx.x; i < run_n; i += blockDim.x) run[i] = sel[i];
+    __syncthreads();
   }
-  __syncthreads();
-  block_select_topk<false>(cand, n, k, sel, selN, scratch);
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    const unsigned long long c = sel[i];
+    const unsigned long long c = i < run_n ? run[i] : 0ull;
     out_s[(size_t)q * k + i] = c ? key2f(cand_key(c)) : -INFINITY;
     out_i[(size_t)q * k + i] = c ? original_ids[cand_row(c)] : -1;
   }
@@ -784,15 +785,15 @@ static cudaError_t launch_batch_scan(const void* qmap, const void* xmap, const B
 
 template <int VPL>
 static cudaError_t launch_rescore_t(const float* Q, const IndexView& ix, const BatchWorkspace& bw, int B, int k,
-                                    float* out_s, int* out_i, cudaStream_t st) {
-  const size_t smem = (size_t)RESCORE_SMEM_ROWS * 8 + BATCH_MAX_K * 8 + sizeof(SelectScratch) + 16;
+                                    int cap, float* out_s, int* out_i, cudaStream_t st) {
+  const size_t smem = (size_t)(RESCORE_CHUNK + 3 * BATCH_MAX_K) * 8 + sizeof(SelectScratch) + 16;
   static size_t configured = 0;
   if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(k_batch_rescore<VPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured = smem;
   }
-  k_batch_rescore<VPL><<<B, 256, smem, st>>>(Q, ix.leaf, ix.original_ids, ix.D, k, bw.cap, bw.qband, bw.theta,
+  k_batch_rescore<VPL><<<B, 256, smem, st>>>(Q, ix.leaf, ix.original_ids, ix.D, k, cap, bw.qband, bw.theta,
                                              bw.cand_count, bw.cand, out_s, out_i, bw.overflow);
   return cudaGetLastError();
 }
@@ -830,7 +831,9 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   P.slots = bw.slots;
   P.cand_count = bw.cand_count;
   P.cand = bw.cand;
-  P.cap = bw.cap;
+  // candidate entries per query: the workspace's fixed pool shared by the batch
+  // (16,384 per query at full capacity, up to 65,536 for smaller batches)
+  P.cap = (int)std::min<int64_t>(BATCH_CAND_MAX, bw.cand_entries / B);
   P.err = bw.err;
   P.seed_only = 0;
   P.slice_rows = SLICE_ROWS;
@@ -867,14 +870,14 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   // depend on this bucket, so scores match the single-query scan bit for bit)
   const int v = (ix.D / 4 + 31) / 32;
   switch (v <= 1 ? 1 : v <= 2 ? 2 : v <= 3 ? 3 : v <= 4 ? 4 : v <= 6 ? 6 : v <= 8 ? 8 : v <= 12 ? 12 : 16) {
-    case 1: return launch_rescore_t<1>(Q, ix, bw, B, k, out_scores, out_ids, st);
-    case 2: return launch_rescore_t<2>(Q, ix, bw, B, k, out_scores, out_ids, st);
-    case 3: return launch_rescore_t<3>(Q, ix, bw, B, k, out_scores, out_ids, st);
-    case 4: return launch_rescore_t<4>(Q, ix, bw, B, k, out_scores, out_ids, st);
-    case 6: return launch_rescore_t<6>(Q, ix, bw, B, k, out_scores, out_ids, st);
-    case 8: return launch_rescore_t<8>(Q, ix, bw, B, k, out_scores, out_ids, st);
-    case 12: return launch_rescore_t<12>(Q, ix, bw, B, k, out_scores, out_ids, st);
-    default: return launch_rescore_t<16>(Q, ix, bw, B, k, out_scores, out_ids, st);
+    case 1: return launch_rescore_t<1>(Q, ix, bw, B, k, P.cap, out_scores, out_ids, st);
+    case 2: return launch_rescore_t<2>(Q, ix, bw, B, k, P.cap, out_scores, out_ids, st);
+    case 3: return launch_rescore_t<3>(Q, ix, bw, B, k, P.cap, out_scores, out_ids, st);
+    case 4: return launch_rescore_t<4>(Q, ix, bw, B, k, P.cap, out_scores, out_ids, st);
+    case 6: return launch_rescore_t<6>(Q, ix, bw, B, k, P.cap, out_scores, out_ids, st);
+    case 8: return launch_rescore_t<8>(Q, ix, bw, B, k, P.cap, out_scores, out_ids, st);
+    case 12: return launch_rescore_t<12>(Q, ix, bw, B, k, P.cap, out_scores, out_ids, st);
+    default: return launch_rescore_t<16>(Q, ix, bw, B, k, P.cap, out_scores, out_ids, st);
   }
 }
 

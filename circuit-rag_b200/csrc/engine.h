@@ -105,14 +105,16 @@ cudaError_t launch_flat_scan(const float* leaf, int D, int N, const float* q, in
 // ---- batched search (batch_kernels.cu) ----
 constexpr int BATCH_MAX_DIM = 2048;  // the rescoring keeps the query in registers (16 float4 per lane)
 constexpr int BATCH_MAX_K = KMAX;  // any k of the single-query search
-constexpr int BATCH_CAND_CAP = 16384;  // candidate rows appended per query
+constexpr int BATCH_CAND_CAP = 16384;  // candidate entries per query of a full-capacity batch
+constexpr int BATCH_CAND_MAX = 65536;  // per query when the batch is smaller than the workspace
 
 struct BatchWorkspace {
   uint32_t* theta = nullptr;      // [capacity] running k-th best keys
   uint32_t* slots = nullptr;      // [capacity * BATCH_MAX_K] per-query threshold slots
   int* unit_counter = nullptr;    // [2] work-unit counters (main pass, threshold pass)
   int* cand_count = nullptr;      // [capacity]
-  unsigned long long* cand = nullptr;  // [capacity * cap] tf32 key << 32 | row
+  unsigned long long* cand = nullptr;  // [cand_entries] tf32 key << 32 | row
+  int64_t cand_entries = 0;
   int* overflow = nullptr;        // queries whose candidate list overflowed
   int* err = nullptr;
   float* queries = nullptr;       // [capacity * D] staging for host queries

@@ -513,7 +513,10 @@ int circuit_index_opaque::ensure_batch(int B) {
     bw.theta = (uint32_t*)grab(sizeof(uint32_t) * cap_B, "cudaMalloc(theta)");
     bw.slots = (uint32_t*)grab(sizeof(uint32_t) * (size_t)cap_B * cb::BATCH_MAX_K, "cudaMalloc(slots)");
     bw.cand_count = (int*)grab(sizeof(int) * cap_B, "cudaMalloc(cand_count)");
-    bw.cand = (unsigned long long*)grab(sizeof(unsigned long long) * (size_t)cap_B * bw.cap, "cudaMalloc(cand)");
+    // the candidate pool holds at least 4,096 queries x 16,384 entries, so a
+    // smaller batch gets up to BATCH_CAND_MAX entries per query
+    bw.cand_entries = (int64_t)std::max(cap_B, 4096) * bw.cap;
+    bw.cand = (unsigned long long*)grab(sizeof(unsigned long long) * (size_t)bw.cand_entries, "cudaMalloc(cand)");
     bw.overflow = (int*)grab(sizeof(int), "cudaMalloc(overflow)");
     bw.unit_counter = (int*)grab(2 * sizeof(int), "cudaMalloc(unit counters)");
     bw.queries = (float*)grab(sizeof(float) * (size_t)cap_B * D, "cudaMalloc(batch queries)");

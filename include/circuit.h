@@ -178,9 +178,10 @@ int circuit_search_finish_async(circuit_index_t index, const float* dev_query, i
  * k-th best; the candidates are rescored exactly in fp32, so results equal
  * the single-query search's.  Limits: dim <= 2048 with dim % 4 == 0,
  * 1 <= k <= 256 (CIRCUIT_ERR_UNSUPPORTED otherwise).
- * A query with more than 16384 rows
- * appended, or more than 8192 rows inside the band of its final threshold
- * (thousands of near-identical rows), gets id -2 in its first slot;
+ * A query with more candidate rows inside the band than the batch's pool
+ * holds (16,384 per query for a 4,096-query batch, up to 65,536 for smaller
+ * batches; e.g. tens of thousands of near-identical rows) gets id -2 in its
+ * first slot;
  * circuit_batch_overflow counts them and circuit_search_batch answers them
  * with the single-query search.
  * Asynchronous on `stream`; the first call per handle allocates its batch

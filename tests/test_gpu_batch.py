@@ -40,10 +40,10 @@ def _check_batch(X, Q, index, k, scores, ids, compare_single=True):
 
 
 def test_batch_many_ties_within_capacity():
-    """6,000 identical rows: every one is inside the band, fewer than the
-    rescore's 8,192, so the batch answers without the fallback."""
+    """20,000 identical rows: every one is inside the band; the rescore takes
+    them in rounds of 8,192 with a running top-k, no fallback."""
     base = _unit_rows(1, 64, 41)
-    X = torch.cat([base.repeat(6000, 1), _unit_rows(700, 64, 42)])
+    X = torch.cat([base.repeat(20000, 1), _unit_rows(700, 64, 42)])
     index = build_circuit_index(X, num_roots=4, children_per_root=2, rank=2, device=DEV)
     Q = torch.cat([base, _unit_rows(5, 64, 43)])
     scores, ids = circuit_search_batch(Q, index, 10)
@@ -90,12 +90,12 @@ def test_batch_ragged_edges():
 
 
 def test_batch_overflow_falls_back_to_single_query():
-    """17,000 identical rows all sit inside the error band of a query equal to
-    them: its candidate list (16,384 rows appended, 8,192 after the final
-    threshold) overflows, the async call marks it with id -2, and
-    circuit_search_batch answers it with circuit_search."""
+    """70,000 identical rows all sit inside the error band of a query equal to
+    them: its candidate list (at most 65,536 entries for a small batch)
+    overflows, the async call marks it with id -2, and circuit_search_batch
+    answers it with circuit_search."""
     base = _unit_rows(1, 64, 21)
-    X = torch.cat([base.repeat(17000, 1), _unit_rows(500, 64, 22)])
+    X = torch.cat([base.repeat(70000, 1), _unit_rows(500, 64, 22)])
     index = build_circuit_index(X, num_roots=4, children_per_root=2, rank=2, device=DEV)
     Q = torch.cat([base, _unit_rows(3, 64, 23)])
     handle = index.native_handle()
