@@ -68,6 +68,8 @@ void* circuit_index_opaque::dev_alloc(size_t bytes, const char* what) {
 void circuit_index_opaque::release() {
   if (device >= 0 && (stream || !owned.empty() || h_pinned)) cudaSetDevice(device);
   if (stream) cudaStreamSynchronize(stream);
+  for (auto& g : host_graphs) cudaGraphExecDestroy(g.second);
+  host_graphs.clear();
   for (void* p : owned) cudaFree(p);
   owned.clear();
   for (void* p : batch_owned) cudaFree(p);
@@ -431,6 +433,54 @@ int circuit_index_opaque::search_blocking(const float* query, bool host_ptrs, in
   if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice")) return CIRCUIT_ERR_CUDA;
   // reference routing: flat scan for N <= 10000 (gpu_index.cpp:151)
   const int64_t min_hier = 10001;
+  const int hier = ((int64_t)N < min_hier) ? 0 : 1;
+  if (host_ptrs) {
+    // graph replay: one launch instead of seven stream operations
+    const int key = (k << 1) | hier;
+    auto g = host_graphs.find(key);
+    if (g == host_graphs.end() && ++host_graph_calls[key] >= 2) {
+      cudaGraph_t graph = nullptr;
+      cudaGraphExec_t exec = nullptr;
+      bool built = false;
+      if (cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+        bool ok = cudaMemcpyAsync(dev_query, h_query, sizeof(float) * D, cudaMemcpyHostToDevice, stream) == cudaSuccess;
+        ok = ok && cb::launch_search(view, ws, dev_query, k, hier, dev_scores, dev_ids, nullptr, stream, nullptr,
+                                     nullptr) == cudaSuccess;
+        ok = ok && cudaMemcpyAsync(h_scores, dev_scores, sizeof(float) * k, cudaMemcpyDeviceToHost, stream) == cudaSuccess;
+        ok = ok && cudaMemcpyAsync(h_ids, dev_ids, sizeof(int) * k, cudaMemcpyDeviceToHost, stream) == cudaSuccess;
+        ok = ok && cudaMemcpyAsync(h_ctrl, ws.ctrl, cb::CTRL_RESET_BYTES, cudaMemcpyDeviceToHost, stream) == cudaSuccess;
+        const bool ended = cudaStreamEndCapture(stream, &graph) == cudaSuccess;
+        built = ok && ended && graph && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
+        if (graph) cudaGraphDestroy(graph);
+      }
+      cudaGetLastError();  // a failed capture falls back to direct launches
+      if (built) g = host_graphs.emplace(key, exec).first;
+    }
+    if (g != host_graphs.end()) {
+      std::memcpy(h_query, query, sizeof(float) * D);
+      if (!cuda_ok(cudaGraphLaunch(g->second, stream), "graph launch") ||
+          !cuda_ok(cudaStreamSynchronize(stream), "search sync"))
+        return CIRCUIT_ERR_CUDA;
+      last_stream = stream;
+      last_path = hier;
+      last_k = k;
+      std::memcpy(out_scores, h_scores, sizeof(float) * k);
+      std::memcpy(out_ids, h_ids, sizeof(int) * k);
+      have_host_ctrl = true;
+      if (h_ctrl->error) {
+        set_error("device-side wait timed out (error bits " + std::to_string(h_ctrl->error) + ")");
+        return CIRCUIT_ERR_TIMEOUT;
+      }
+      if (trace) {
+        circuit_trace_ex_t tx;
+        fill_trace(*h_ctrl, &tx);
+        trace->latency_us =
+            (float)std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
+        trace->vectors_scored = (int)std::min<int64_t>(tx.vectors_scored, std::numeric_limits<int>::max());
+      }
+      return CIRCUIT_OK;
+    }
+  }
   if (host_ptrs) {
     std::memcpy(h_query, query, sizeof(float) * D);
     if (!cuda_ok(cudaMemcpyAsync(dev_query, h_query, sizeof(float) * D, cudaMemcpyHostToDevice, stream), "H2D query"))

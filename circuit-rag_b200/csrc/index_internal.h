@@ -6,6 +6,7 @@
 
 #include <cstdint>
 #include <string>
+#include <map>
 #include <vector>
 
 #include "../../include/circuit.h"
@@ -37,6 +38,11 @@ struct circuit_index_opaque {
   bool have_host_ctrl = false;
 
   cudaStream_t stream = nullptr;
+  // CUDA graphs of the host-buffer search (query H2D, reset, kernels, result
+  // D2H into the fixed pinned buffers), one per (k, path); built on the second
+  // call with that key, after a direct call has configured the kernels
+  std::map<int, cudaGraphExec_t> host_graphs;
+  std::map<int, int> host_graph_calls;
   cudaStream_t last_stream = nullptr;
   int last_path = 0;
   int last_k = 0;
