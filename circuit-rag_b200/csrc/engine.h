@@ -74,6 +74,21 @@ struct Workspace {
   int scan_grid;
 };
 
+// Endpoints of a blocking search replayed from a CUDA graph.  All four point
+// into mapped pinned host memory except out_indirect (device memory).  The
+// start of the search copies the query from q_host (host-buffer calls) or from
+// the device pointer slots[0] (device-buffer calls) and clears the control
+// header in one kernel; the final merge writes scores / ids to the launch's
+// out_scores / out_ids, or, with slots, to the device pointers slots[1] /
+// slots[2] (staged in out_indirect by the start kernel), and a copy of the
+// control header to ctrl_out.  No copy-engine operation remains in the graph.
+struct HostIO {
+  const float* q_host;               // [D] or null
+  void* const* slots;                // {query, scores, ids} device pointers, or null
+  void** out_indirect;               // [2]
+  SearchCtrl* ctrl_out;              // receives the first CTRL_RESET_BYTES
+};
+
 // ---- launchers (search_kernels.cu); all asynchronous on `stream` ----
 cudaError_t launch_prepare_roots(const IndexView& ix, double* root_cn, double* root_defect, cudaStream_t stream);
 
@@ -83,16 +98,16 @@ cudaError_t launch_prepare_roots(const IndexView& ix, double* root_cn, double* r
 // recorded around the main (dominant) scan kernel.
 cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float* q, int k, int hierarchical,
                           float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
-                          cudaEvent_t ev_scan0, cudaEvent_t ev_scan1);
+                          cudaEvent_t ev_scan0, cudaEvent_t ev_scan1, const HostIO* io = nullptr);
 // The hierarchical search in two phases, so that shards can exchange their seed
 // thresholds in between: seed = reset + root scan + seed scan (writes the seed
 // k-th best score to T_export, -inf if the seed root has fewer than k rows);
 // finish = bounds + main scan with threshold max(own seed, *T_ext).
 cudaError_t launch_search_seed(const IndexView& ix, const Workspace& ws, const float* q, int k, float* T_export,
-                               cudaStream_t stream);
+                               cudaStream_t stream, const HostIO* io = nullptr);
 cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const float* q, int k, const float* T_ext,
                                  float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
-                                 cudaEvent_t ev_scan0, cudaEvent_t ev_scan1);
+                                 cudaEvent_t ev_scan0, cudaEvent_t ev_scan1, const HostIO* io = nullptr);
 
 // Flat exact top-k of leaf[0..N) . q with caller-provided scratch: ctrl (its
 // first CTRL_RESET_BYTES zeroed by the caller), range = {0, 0, N, -1},

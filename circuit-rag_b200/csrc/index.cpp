@@ -162,8 +162,9 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
   dev_query = (float*)dev_alloc(sizeof(float) * D, "cudaMalloc(query)");
   dev_scores = (float*)dev_alloc(sizeof(float) * cb::KMAX, "cudaMalloc(scores)");
   dev_ids = (int*)dev_alloc(sizeof(int) * cb::KMAX, "cudaMalloc(ids)");
+  dev_out_indirect = (void**)dev_alloc(2 * sizeof(void*), "cudaMalloc(out pointers)");
   if (!ws.ctrl || !ws.seed_ranges || !ws.main_ranges || !ws.flat_range || !ws.flat_packed || !ws.root_dots ||
-      !ws.cta_lists || !dev_query || !dev_scores || !dev_ids)
+      !ws.cta_lists || !dev_query || !dev_scores || !dev_ids || !dev_out_indirect)
     return false;
   const int4 fr = make_int4(0, 0, N, -1);
   const unsigned long long fp = (1ull << 32) | (unsigned long long)(uint32_t)N;
@@ -171,13 +172,24 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
       !cuda_ok(cudaMemcpyAsync(ws.flat_packed, &fp, sizeof(fp), cudaMemcpyHostToDevice, stream), "H2D flat packed") ||
       !cuda_ok(cudaMemsetAsync(ws.ctrl, 0, sizeof(cb::SearchCtrl), stream), "memset ctrl"))
     return false;
-  // pinned host staging for the host-pointer search: query, scores, ids, ctrl header
-  const size_t pin_bytes = sizeof(float) * D + (sizeof(float) + sizeof(int)) * cb::KMAX + sizeof(cb::SearchCtrl);
-  if (!cuda_ok(cudaMallocHost(&h_pinned, pin_bytes), "cudaMallocHost")) return false;
+  // pinned, device-mapped host staging for the blocking search: query, scores,
+  // ids, ctrl header, call slots.  Graph replays read the query from it and
+  // write the results into it from the kernels themselves.
+  const size_t pin_bytes =
+      sizeof(float) * D + (sizeof(float) + sizeof(int)) * cb::KMAX + sizeof(cb::SearchCtrl) + 4 * sizeof(void*);
+  if (!cuda_ok(cudaHostAlloc(&h_pinned, pin_bytes, cudaHostAllocMapped), "cudaHostAlloc")) return false;
   h_query = (float*)h_pinned;
   h_scores = h_query + D;
   h_ids = (int*)(h_scores + cb::KMAX);
   h_ctrl = (cb::SearchCtrl*)(h_ids + cb::KMAX);
+  h_slots = (void**)(h_ctrl + 1);
+  void* d_pinned = nullptr;
+  if (!cuda_ok(cudaHostGetDevicePointer(&d_pinned, h_pinned, 0), "cudaHostGetDevicePointer")) return false;
+  const auto alias = [&](const void* h) { return (char*)d_pinned + ((const char*)h - (const char*)h_pinned); };
+  io_host = cb::HostIO{(const float*)alias(h_query), nullptr, dev_out_indirect, (cb::SearchCtrl*)alias(h_ctrl)};
+  io_device = cb::HostIO{nullptr, (void* const*)alias(h_slots), dev_out_indirect, (cb::SearchCtrl*)alias(h_ctrl)};
+  map_scores = (float*)alias(h_scores);
+  map_ids = (int*)alias(h_ids);
   if (!cuda_ok(cudaStreamSynchronize(stream), "index setup")) return false;
   return true;
 }
@@ -434,21 +446,31 @@ int circuit_index_opaque::search_blocking(const float* query, bool host_ptrs, in
   // reference routing: flat scan for N <= 10000 (gpu_index.cpp:151)
   const int64_t min_hier = 10001;
   const int hier = ((int64_t)N < min_hier) ? 0 : 1;
-  if (host_ptrs) {
-    // graph replay: one launch instead of seven stream operations
-    const int key = (k << 1) | hier;
+  // Graph replay: one launch of [prologue kernel, search kernels]; the query
+  // comes from the mapped staging block (host buffers) or from the caller's
+  // device pointer named in its slots, and the final merge writes the results
+  // and the control header straight to their destinations.  Device buffers
+  // need device (or managed) memory of this device, a 16-byte aligned query
+  // (float4 copy) and 4-byte aligned outputs; others take the direct path,
+  // whose copies report a bad pointer as an error.
+  const auto on_device = [&](const void* p, uintptr_t align) {
+    cudaPointerAttributes a{};
+    if (((uintptr_t)p & (align - 1)) != 0) return false;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) { cudaGetLastError(); return false; }
+    return (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) && a.device == device;
+  };
+  const bool graph_ok = host_ptrs || (on_device(query, 16) && on_device(out_scores, 4) && on_device(out_ids, 4));
+  if (graph_ok) {
+    const int key = (k << 2) | (host_ptrs ? 2 : 0) | hier;
     auto g = host_graphs.find(key);
     if (g == host_graphs.end() && ++host_graph_calls[key] >= 2) {
       cudaGraph_t graph = nullptr;
       cudaGraphExec_t exec = nullptr;
       bool built = false;
       if (cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
-        bool ok = cudaMemcpyAsync(dev_query, h_query, sizeof(float) * D, cudaMemcpyHostToDevice, stream) == cudaSuccess;
-        ok = ok && cb::launch_search(view, ws, dev_query, k, hier, dev_scores, dev_ids, nullptr, stream, nullptr,
-                                     nullptr) == cudaSuccess;
-        ok = ok && cudaMemcpyAsync(h_scores, dev_scores, sizeof(float) * k, cudaMemcpyDeviceToHost, stream) == cudaSuccess;
-        ok = ok && cudaMemcpyAsync(h_ids, dev_ids, sizeof(int) * k, cudaMemcpyDeviceToHost, stream) == cudaSuccess;
-        ok = ok && cudaMemcpyAsync(h_ctrl, ws.ctrl, cb::CTRL_RESET_BYTES, cudaMemcpyDeviceToHost, stream) == cudaSuccess;
+        const bool ok = cb::launch_search(view, ws, dev_query, k, hier, host_ptrs ? map_scores : nullptr,
+                                          host_ptrs ? map_ids : nullptr, nullptr, stream, nullptr, nullptr,
+                                          host_ptrs ? &io_host : &io_device) == cudaSuccess;
         const bool ended = cudaStreamEndCapture(stream, &graph) == cudaSuccess;
         built = ok && ended && graph && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
         if (graph) cudaGraphDestroy(graph);
@@ -457,15 +479,23 @@ int circuit_index_opaque::search_blocking(const float* query, bool host_ptrs, in
       if (built) g = host_graphs.emplace(key, exec).first;
     }
     if (g != host_graphs.end()) {
-      std::memcpy(h_query, query, sizeof(float) * D);
+      if (host_ptrs) {
+        std::memcpy(h_query, query, sizeof(float) * D);
+      } else {
+        h_slots[0] = const_cast<float*>(query);
+        h_slots[1] = out_scores;
+        h_slots[2] = out_ids;
+      }
       if (!cuda_ok(cudaGraphLaunch(g->second, stream), "graph launch") ||
           !cuda_ok(cudaStreamSynchronize(stream), "search sync"))
         return CIRCUIT_ERR_CUDA;
       last_stream = stream;
       last_path = hier;
       last_k = k;
-      std::memcpy(out_scores, h_scores, sizeof(float) * k);
-      std::memcpy(out_ids, h_ids, sizeof(int) * k);
+      if (host_ptrs) {
+        std::memcpy(out_scores, h_scores, sizeof(float) * k);
+        std::memcpy(out_ids, h_ids, sizeof(int) * k);
+      }
       have_host_ctrl = true;
       if (h_ctrl->error) {
         set_error("device-side wait timed out (error bits " + std::to_string(h_ctrl->error) + ")");

@@ -35,12 +35,19 @@ struct circuit_index_opaque {
   float* h_scores = nullptr;
   int* h_ids = nullptr;
   cb::SearchCtrl* h_ctrl = nullptr;
+  void** h_slots = nullptr;         // device-buffer calls: {query, scores, ids}
   bool have_host_ctrl = false;
+  // device aliases of the mapped staging block (see cb::HostIO)
+  void** dev_out_indirect = nullptr;
+  cb::HostIO io_host{}, io_device{};
+  float* map_scores = nullptr;
+  int* map_ids = nullptr;
 
   cudaStream_t stream = nullptr;
-  // CUDA graphs of the host-buffer search (query H2D, reset, kernels, result
-  // D2H into the fixed pinned buffers), one per (k, path); built on the second
-  // call with that key, after a direct call has configured the kernels
+  // CUDA graphs of the blocking search (prologue kernel, search kernels; the
+  // final merge writes into the mapped staging block), one per (k, path,
+  // host or device buffers); built on the second call with that key, after a
+  // direct call has configured the kernels
   std::map<int, cudaGraphExec_t> host_graphs;
   std::map<int, int> host_graph_calls;
   cudaStream_t last_stream = nullptr;

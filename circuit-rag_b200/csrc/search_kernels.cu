@@ -1,7 +1,8 @@
 // Single-query exact top-k search kernels for B200 (sm_100a).
 //
 // Pipeline for one query (all on one stream, no host synchronisation):
-//   memset(ctrl header)
+//   memset(ctrl header)   (graph-replayed blocking calls: k_search_prologue,
+//                          which also stages the query)
 //   k_root_scan   warp per root: q.c_r for every root, ||q||^2, argmax root
 //                 (the seed root); its last CTA writes the seed root's leaf
 //                 ranges.                       (reference: search.py:26-41,
@@ -62,6 +63,9 @@ struct ScanParams {
   int* out_ids;
   long long* out_rows;
   const int* original_ids;
+  void* const* out_indirect;                  // final: {scores, ids} device pointers replacing out_scores / out_ids
+  const unsigned long long* ctrl_hdr;         // final: control header, copied to ctrl_out after the merge
+  unsigned long long* ctrl_out;               // (mapped host memory; null = no copy)
 };
 
 template <int VPL> struct ScanShape {
@@ -212,7 +216,9 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     auto merge = [&]() {
       __syncwarp();
       warp_bitonic_desc(tk, SORTN, lane);
-      for (int i = KCAP + lane; i < SORTN; i += 32) tk[i] = 0ull;
+      // only the warp's k best can reach the final list: the rest are cleared,
+      // so the CTA select below sees at most k non-zeros per warp
+      for (int i = k + lane; i < SORTN; i += 32) tk[i] = 0ull;
       __syncwarp();
       cnt = 0;
       const uint32_t kth = cand_key(tk[k - 1]);
@@ -369,20 +375,48 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       if (P.T_export) *P.T_export = T ? key2f(T) : -INFINITY;
     }
   } else {
+    float* out_scores = P.out_scores;
+    int* out_ids = P.out_ids;
+    if (P.out_indirect) {
+      const unsigned long long* ptrs = reinterpret_cast<const unsigned long long*>(P.out_indirect);
+      out_scores = reinterpret_cast<float*>(__ldcg(ptrs));
+      out_ids = reinterpret_cast<int*>(__ldcg(ptrs + 1));
+    }
     for (int i = tid; i < k; i += blockDim.x) {
       const unsigned long long c = sel[i];
       if (c != 0ull) {
         const uint32_t row = cand_row(c);
-        P.out_scores[i] = key2f(cand_key(c));
-        if (P.out_ids) P.out_ids[i] = P.original_ids ? P.original_ids[row] : (int)row;
+        out_scores[i] = key2f(cand_key(c));
+        if (out_ids) out_ids[i] = P.original_ids ? P.original_ids[row] : (int)row;
         if (P.out_rows) P.out_rows[i] = (long long)row;
       } else {
-        P.out_scores[i] = -INFINITY;
-        if (P.out_ids) P.out_ids[i] = -1;
+        out_scores[i] = -INFINITY;
+        if (out_ids) out_ids[i] = -1;
         if (P.out_rows) P.out_rows[i] = -1;
       }
     }
+    // every other CTA's updates of the header precede its ticket
+    if (P.ctrl_out)
+      for (int i = tid; i < (int)(CTRL_RESET_BYTES / 8); i += blockDim.x) P.ctrl_out[i] = __ldcg(P.ctrl_hdr + i);
   }
+}
+
+// ============================================================ search prologue
+// First kernel of a graph-replayed blocking search: stages the query and
+// clears the control header (replaces a host-to-device copy and a memset, two
+// copy-engine operations of a few microseconds each at this size).  The query
+// comes from mapped pinned memory (q_host) or from the device pointer slots[0];
+// slots[1..2] (the caller's device outputs) are staged for the final merge.
+__global__ void __launch_bounds__(128) k_search_prologue(const float4* q_host, void* const* slots, float4* dq, int D4,
+                                                         unsigned long long* ctrl_hdr, void** out_indirect) {
+  const int tid = threadIdx.x;
+  const float4* src = q_host;
+  if (slots) {
+    src = static_cast<const float4*>(slots[0]);
+    if (tid < 2) out_indirect[tid] = slots[tid + 1];
+  }
+  for (int i = tid; i < D4; i += blockDim.x) dq[i] = src[i];
+  if (tid < (int)(CTRL_RESET_BYTES / 8)) ctrl_hdr[tid] = 0ull;
 }
 
 // ============================================================ root scan (K1)
@@ -831,9 +865,26 @@ static ScanParams scan_params(const IndexView& ix, const Workspace& ws, const fl
   return P;
 }
 
+// Clears the control header; with io, also stages the query (see HostIO).
+static cudaError_t search_reset(const IndexView& ix, const Workspace& ws, const float* q, cudaStream_t stream,
+                                const HostIO* io) {
+  if (!io) return cudaMemsetAsync(ws.ctrl, 0, CTRL_RESET_BYTES, stream);
+  k_search_prologue<<<1, 128, 0, stream>>>(reinterpret_cast<const float4*>(io->q_host), io->slots,
+                                           reinterpret_cast<float4*>(const_cast<float*>(q)), ix.D4,
+                                           reinterpret_cast<unsigned long long*>(ws.ctrl), io->out_indirect);
+  return cudaGetLastError();
+}
+
+static void final_io(ScanParams& M, const Workspace& ws, const HostIO* io) {
+  if (!io) return;
+  M.out_indirect = io->slots ? io->out_indirect : nullptr;
+  M.ctrl_hdr = reinterpret_cast<const unsigned long long*>(ws.ctrl);
+  M.ctrl_out = reinterpret_cast<unsigned long long*>(io->ctrl_out);
+}
+
 cudaError_t launch_search_seed(const IndexView& ix, const Workspace& ws, const float* q, int k, float* T_export,
-                               cudaStream_t stream) {
-  cudaError_t e = cudaMemsetAsync(ws.ctrl, 0, CTRL_RESET_BYTES, stream);
+                               cudaStream_t stream, const HostIO* io) {
+  cudaError_t e = search_reset(ix, ws, q, stream, io);
   if (e != cudaSuccess) return e;
   k_root_scan<<<(ix.R + ROOT_SCAN_WARPS - 1) / ROOT_SCAN_WARPS, ROOT_SCAN_WARPS * 32, 0, stream>>>(
       ix, q, ws.ctrl, ws.root_dots, ws.seed_ranges, k);
@@ -850,7 +901,7 @@ cudaError_t launch_search_seed(const IndexView& ix, const Workspace& ws, const f
 
 cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const float* q, int k, const float* T_ext,
                                  float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
-                                 cudaEvent_t ev_scan0, cudaEvent_t ev_scan1) {
+                                 cudaEvent_t ev_scan0, cudaEvent_t ev_scan1, const HostIO* io) {
   cudaError_t e;
   const int chunk_rows = bounds_chunk_rows(ix.D, ix.rank);
   const BoundsLayout BL = bounds_layout(ix.D, ix.rank, chunk_rows);
@@ -872,6 +923,7 @@ cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const
   M.done = &ws.ctrl->main_done;
   M.final_mode = 1;
   M.merge_seed = 1;
+  final_io(M, ws, io);
   if (ev_scan0) cudaEventRecord(ev_scan0, stream);
   e = launch_scan(M, ws.scan_grid, stream);
   if (ev_scan1) cudaEventRecord(ev_scan1, stream);
@@ -880,13 +932,14 @@ cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const
 
 cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float* q, int k, int hierarchical,
                           float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
-                          cudaEvent_t ev_scan0, cudaEvent_t ev_scan1) {
+                          cudaEvent_t ev_scan0, cudaEvent_t ev_scan1, const HostIO* io) {
   if (hierarchical) {
-    cudaError_t e = launch_search_seed(ix, ws, q, k, nullptr, stream);
+    cudaError_t e = launch_search_seed(ix, ws, q, k, nullptr, stream, io);
     if (e != cudaSuccess) return e;
-    return launch_search_finish(ix, ws, q, k, nullptr, out_scores, out_ids, out_rows, stream, ev_scan0, ev_scan1);
+    return launch_search_finish(ix, ws, q, k, nullptr, out_scores, out_ids, out_rows, stream, ev_scan0, ev_scan1,
+                                io);
   }
-  cudaError_t e = cudaMemsetAsync(ws.ctrl, 0, CTRL_RESET_BYTES, stream);
+  cudaError_t e = search_reset(ix, ws, q, stream, io);
   if (e != cudaSuccess) return e;
   ScanParams F = scan_params(ix, ws, q, k, out_scores, out_ids, out_rows);
   F.ranges = ws.flat_range;
@@ -894,6 +947,7 @@ cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float*
   F.done = &ws.ctrl->main_done;
   F.final_mode = 1;
   F.merge_seed = 0;
+  final_io(F, ws, io);
   if (ev_scan0) cudaEventRecord(ev_scan0, stream);
   e = launch_scan(F, ws.scan_grid, stream);
   if (ev_scan1) cudaEventRecord(ev_scan1, stream);

@@ -14,8 +14,8 @@ struct SelectScratch {
   unsigned long long prefix;
   uint32_t need;
   uint32_t count;
-  uint32_t nnz;
-  uint32_t pad;
+  uint32_t done;
+  uint32_t kk;
 };
 
 template <bool GLOBAL>
@@ -57,50 +57,65 @@ static __device__ void warp_bitonic_desc(unsigned long long* a, int n, int lane)
 }
 
 // Selects the k largest non-zero packed candidates of src[0..M) (unique when
-// non-zero; zero = empty slot) by an 8 x 8-bit radix select over the 64-bit
-// packed value, then sorts them.  sel must hold selN >= k entries (power of 2).
-// Returns the number of selected candidates (min(k, non-zeros)); sel[0..ret) is
-// sorted descending and sel[ret..selN) is zero.  All threads of the block call it.
+// non-zero; zero = empty slot) by a most-significant-digit-first radix select
+// over the 64-bit packed value, 8 bits per pass, then sorts them.
+//   - zeros never enter a histogram; the first pass also counts the non-zeros,
+//     so fewer than k of them select them all;
+//   - one shared atomic per distinct bin per warp (lanes with the same bin are
+//     grouped by match.any), so runs of equal digits do not serialise;
+//   - the passes stop as soon as the bin that holds the k-th value holds exactly
+//     the number still needed: the selection is then "everything with this
+//     prefix or above", usually after 2-4 of the 8 digits.
+// sel must hold selN >= k entries (power of 2).  Returns the number selected
+// (min(k, non-zeros)); sel[0..ret) is sorted descending and sel[ret..selN) is
+// zero.  All threads of the block call it; blockDim.x is a multiple of 32.
 template <bool GLOBAL>
 static __device__ int block_select_topk(const unsigned long long* src, int M, int k, unsigned long long* sel,
-                                 int selN, SelectScratch* s) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) { s->nnz = 0; s->count = 0; s->prefix = 0; }
+                                        int selN, SelectScratch* s) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthreads = blockDim.x;
+  for (int i = tid; i < 256; i += nthreads) s->hist[i] = 0;
+  for (int i = tid; i < selN; i += nthreads) sel[i] = 0ull;
+  if (tid == 0) { s->count = 0; s->kk = 0; s->done = 0; }
   __syncthreads();
-  uint32_t local = 0;
-  for (int i = tid; i < M; i += blockDim.x) local += (ld_cand<GLOBAL>(src + i) != 0ull);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(FULL_MASK, local, o);
-  if (lane == 0 && local) atomicAdd(&s->nnz, local);
-  __syncthreads();
-  const int kk = min((int)s->nnz, k);
-  for (int i = tid; i < selN; i += blockDim.x) sel[i] = 0ull;
-  if (kk == 0) { __syncthreads(); return 0; }
-  if (tid == 0) s->need = (uint32_t)kk;
-  __syncthreads();
-  for (int shift = 56; shift >= 0; shift -= 8) {
-    const unsigned long long prefix = s->prefix;
-    const uint32_t need = s->need;
+  unsigned long long prefix = 0ull;
+  uint32_t need = (uint32_t)k;  // the first pass lowers it to min(k, non-zeros)
+  for (int shift = 56;; shift -= 8) {
     const unsigned long long hmask = (shift == 56) ? 0ull : (~0ull << (shift + 8));
-    for (int i = tid; i < 256; i += blockDim.x) s->hist[i] = 0;
-    __syncthreads();
-    for (int i = tid; i < M; i += blockDim.x) {
-      const unsigned long long v = ld_cand<GLOBAL>(src + i);
-      if ((v & hmask) == prefix) atomicAdd(&s->hist[(v >> shift) & 255ull], 1u);
+    for (int base = warp * 32; base < M; base += nthreads) {
+      const int i = base + lane;
+      const unsigned long long v = (i < M) ? ld_cand<GLOBAL>(src + i) : 0ull;
+      const bool in = v != 0ull && (v & hmask) == prefix;
+      const uint32_t bin = in ? (uint32_t)(v >> shift) & 255u : 256u;
+      const uint32_t peers = __match_any_sync(FULL_MASK, bin);
+      if (in && lane == __ffs(peers) - 1) atomicAdd(&s->hist[bin], (uint32_t)__popc(peers));
     }
     __syncthreads();
     if (warp == 0) {
+      // lane l owns bins 255-8l .. 248-8l (descending digit order); the warp
+      // clears them for the next pass while it reads them
       uint32_t c[8], sum = 0;
 #pragma unroll
-      for (int t = 0; t < 8; ++t) { c[t] = s->hist[255 - (lane * 8 + t)]; sum += c[t]; }
+      for (int t = 0; t < 8; ++t) {
+        c[t] = s->hist[255 - (lane * 8 + t)];
+        s->hist[255 - (lane * 8 + t)] = 0;
+        sum += c[t];
+      }
       uint32_t incl = sum;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        uint32_t x = __shfl_up_sync(FULL_MASK, incl, o);
+        const uint32_t x = __shfl_up_sync(FULL_MASK, incl, o);
         if (lane >= o) incl += x;
       }
+      if (shift == 56) {
+        const uint32_t nnz = __shfl_sync(FULL_MASK, incl, 31);
+        need = need < nnz ? need : nnz;
+        if (lane == 0) {
+          s->kk = need;
+          if (need == 0) s->done = 1;
+        }
+      }
       const uint32_t excl = incl - sum;
-      if (excl < need && incl >= need) {
+      if (need > 0 && excl < need && incl >= need) {
         uint32_t acc = excl;
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
@@ -108,6 +123,7 @@ static __device__ int block_select_topk(const unsigned long long* src, int M, in
             const uint32_t d = 255 - (lane * 8 + t);
             s->prefix = prefix | ((unsigned long long)d << shift);
             s->need = need - acc;
+            s->done = (c[t] == need - acc) || shift == 0;
             break;
           }
           acc += c[t];
@@ -115,17 +131,41 @@ static __device__ int block_select_topk(const unsigned long long* src, int M, in
       }
     }
     __syncthreads();
+    const bool done = s->done != 0;
+    prefix = s->prefix;
+    need = s->need;
+    if (done) break;
   }
-  const unsigned long long kth = s->prefix;
-  for (int i = tid; i < M; i += blockDim.x) {
+  const int kk = (int)s->kk;
+  if (kk == 0) return 0;
+  // everything at or above the k-th value's resolved prefix: exactly kk entries
+  for (int i = tid; i < M; i += nthreads) {
     const unsigned long long v = ld_cand<GLOBAL>(src + i);
-    if (v != 0ull && v >= kth) {
+    if (v != 0ull && v >= prefix) {
       const uint32_t pos = atomicAdd(&s->count, 1u);
       if (pos < (uint32_t)selN) sel[pos] = v;
     }
   }
   __syncthreads();
-  block_bitonic_desc(sel, selN);
+  const int n = min((int)s->count, selN);
+  if (n <= nthreads) {
+    // rank sort: each selected value's rank is the number of larger values
+    // (ties broken by position), then one scatter
+    unsigned long long v = 0ull;
+    int r = 0;
+    if (tid < n) {
+      v = sel[tid];
+      for (int j = 0; j < n; ++j) {
+        const unsigned long long u = sel[j];
+        r += (u > v) || (u == v && j < tid);
+      }
+    }
+    __syncthreads();
+    if (tid < n) sel[r] = v;
+    __syncthreads();
+  } else {
+    block_bitonic_desc(sel, selN);
+  }
   return kk;
 }
 

@@ -200,6 +200,64 @@ def test_c_abi_host_and_device_search(tmp_path):
         L.circuit_destroy_index(h)
 
 
+def test_blocking_search_graph_replay_paths(tmp_path):
+    """Blocking calls replay a graph from the second call per (k, path, buffer kind):
+    the query comes from mapped host memory or the caller's device pointer, and the
+    final merge writes results and the control header directly.  Flat and
+    hierarchical indexes, k = 10 and 256, device outputs that move between calls, and
+    a query pointer that is not 16-byte aligned (direct path) all agree with the
+    oracle and with each other, traces included."""
+    w = WORKLOADS["spread-200k"]
+    L = _native.lib()
+    for n, flat in ((6000, True), (30000, False)):
+        X = w.corpus(0, n, device=DEV)
+        idx = build_circuit_index(X, num_roots=32, children_per_root=8, rank=8, device=DEV)
+        path = str(tmp_path / f"g{n}.circuit")
+        idx.save(path)
+        h = L.circuit_load_index(path.encode(), torch.cuda.current_device())
+        assert h, _native.last_error()
+        try:
+            Q = w.query_batch(5, device=DEV)
+            qbuf = torch.empty(Q.shape[1] + 1, device=DEV)
+            for k in (10, 256):
+                out_s = torch.full((len(Q) * k,), float("nan"), device=DEV)
+                out_i = torch.full((len(Q) * k,), -7, dtype=torch.int32, device=DEV)
+                for j, q in enumerate(Q):
+                    qh = q.cpu().numpy().copy()
+                    sh = np.zeros(k, np.float32)
+                    ih = np.zeros(k, np.int32)
+                    tr = _native.Trace()
+                    rc = L.circuit_search(h, qh.ctypes.data, k, sh.ctypes.data, ih.ctypes.data, ctypes.byref(tr))
+                    assert rc == 0, _native.last_error()
+                    oracle.check_topk(_exact(X, q), k, sh, ih)
+                    if flat:
+                        assert tr.vectors_scored == n
+                    else:
+                        assert 0 < tr.vectors_scored <= n
+                    sd, idd = out_s[j * k:(j + 1) * k], out_i[j * k:(j + 1) * k]
+                    tr2 = _native.Trace()
+                    rc = L.circuit_search_device(h, q.contiguous().data_ptr(), k, sd.data_ptr(), idd.data_ptr(),
+                                                 ctypes.byref(tr2))
+                    assert rc == 0, _native.last_error()
+                    assert np.array_equal(sd.cpu().numpy(), sh) and np.array_equal(idd.cpu().numpy(), ih)
+                    assert tr2.vectors_scored == tr.vectors_scored
+                    qbuf[1:].copy_(q)
+                    sd2 = torch.empty(k, device=DEV)
+                    id2 = torch.empty(k, dtype=torch.int32, device=DEV)
+                    rc = L.circuit_search_device(h, qbuf[1:].data_ptr(), k, sd2.data_ptr(), id2.data_ptr(), None)
+                    assert rc == 0, _native.last_error()
+                    assert np.array_equal(sd2.cpu().numpy(), sh) and np.array_equal(id2.cpu().numpy(), ih)
+                # earlier outputs stay untouched by later calls
+                for j, q in enumerate(Q):
+                    oracle.check_topk(_exact(X, q), k, out_s[j * k:(j + 1) * k].cpu().numpy(),
+                                      out_i[j * k:(j + 1) * k].cpu().numpy())
+            tx = _native.TraceEx()
+            assert L.circuit_last_trace(h, ctypes.byref(tx)) == 0
+            assert tx.device_error == 0 and tx.path == (0 if flat else 1)
+        finally:
+            L.circuit_destroy_index(h)
+
+
 def test_cuda_graph_replay_matches():
     w = WORKLOADS["clustered-50k"]
     X = w.corpus(device=DEV)
