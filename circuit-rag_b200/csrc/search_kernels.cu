@@ -24,6 +24,7 @@
 // The flat path (small corpora) is the final scan over one range [0, N).
 #include <cmath>
 #include <cstdio>
+#include <type_traits>
 
 #include "common.cuh"
 #include "engine.h"
@@ -54,6 +55,7 @@ struct ScanParams {
   int row_bytes;
   int k;
   int stages;
+  int min_rows;                               // rows per CTA below which fewer CTAs take part
   int final_mode;                             // 0: seed merge, 1: final merge
   int merge_seed;                             // final: also merge ctrl seed list
   unsigned long long* seed_list;              // [k]
@@ -81,7 +83,7 @@ constexpr int MAX_STAGES = 8;
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct ScanLayout {
-  size_t stage_bytes, stages_off, bars_off, rows_off, n_off, topk_off, sel_off, scratch_off, total;
+  size_t stage_bytes, stages_off, bars_off, rows_off, n_off, side_off, topk_off, sel_off, scratch_off, total;
 };
 __host__ __device__ inline ScanLayout scan_layout(int rows_per_stage, int row_bytes, int stages, int sortn,
                                                   int kcap) {
@@ -91,12 +93,16 @@ __host__ __device__ inline ScanLayout scan_layout(int rows_per_stage, int row_by
   L.bars_off = align_up(L.stages_off + stages * L.stage_bytes, 128);
   L.rows_off = L.bars_off + 2 * MAX_STAGES * sizeof(uint64_t);           // runs: [stage][32] int2
   L.n_off = L.rows_off + (size_t)MAX_STAGES * 32 * sizeof(int2);          // rows, runs per stage
-  L.topk_off = align_up(L.n_off + 2 * MAX_STAGES * sizeof(int), 128);
+  L.side_off = align_up(L.n_off + 2 * MAX_STAGES * sizeof(int), 16);   // [stage] 16 B: threshold snapshot
+  L.topk_off = align_up(L.side_off + (size_t)MAX_STAGES * 16, 128);
   L.sel_off = L.topk_off + (size_t)SCAN_CONSUMER_WARPS * sortn * 8;
   L.scratch_off = align_up(L.sel_off + (size_t)kcap * 8, 128);
   L.total = align_up(L.scratch_off + sizeof(SelectScratch) + 16, 128);
   return L;
 }
+
+// Merges whose survivors number at most this many rank them directly.
+constexpr int RANK_CAP = 256;
 
 template <int VPL, int KCAP>
 __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
@@ -116,7 +122,16 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
   unsigned long long* topk_all = reinterpret_cast<unsigned long long*>(smem + L.topk_off);
   unsigned long long* sel = reinterpret_cast<unsigned long long*>(smem + L.sel_off);
   SelectScratch* scratch = reinterpret_cast<SelectScratch*>(smem + L.scratch_off);
+  // Each stage's bulk copies also bring the 16-byte line holding theta_key, on
+  // the same barrier: consumers refresh the shared threshold from shared memory
+  // instead of waiting on an L2 round trip per stage.
+  const uint32_t* side = reinterpret_cast<const uint32_t*>(smem + L.side_off);
+  const int theta_word = (int)(((uintptr_t)P.theta_key & 15u) >> 2);
   __shared__ int s_is_last, s_err;
+  __shared__ unsigned long long s_pc;
+  __shared__ int4 s_rg0;
+  __shared__ uint32_t s_theta, s_rank_count;
+  __shared__ uint32_t s_warp_theta[SCAN_CONSUMER_WARPS];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int STAGES = P.stages;
@@ -124,6 +139,9 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
 
   for (int i = tid; i < SCAN_CONSUMER_WARPS * SORTN; i += blockDim.x) topk_all[i] = 0ull;
   if (tid == 0) {
+    s_err = 0;
+    s_pc = ld_volatile_u64(P.packed_counts);
+    s_rg0 = __ldcg(P.ranges);  // entry 0 exists whenever ranges do; read beside the count
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], SCAN_CONSUMER_WARPS);
@@ -131,26 +149,41 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     fence_mbar_init();
   }
   __syncthreads();
+  // Small streams use fewer CTAs (at least min_rows rows each): the per-CTA and
+  // grid merges then handle fewer lists, and each warp sees enough rows for its
+  // k-th best to raise the shared threshold.  The others leave before any copy.
+  const uint32_t n_ranges = (uint32_t)(s_pc >> 32), n_rows = (uint32_t)s_pc;
+  const uint32_t G = max(1u, min((uint32_t)gridDim.x, (n_rows + (uint32_t)P.min_rows - 1) / (uint32_t)P.min_rows));
+  if (blockIdx.x >= G) return;
 
   if (warp == SCAN_CONSUMER_WARPS) {
     // ------------------------------------------------------------ producer
+    const uint32_t vb = (uint32_t)(((unsigned long long)blockIdx.x * n_rows) / G);
+    const uint32_t ve = (uint32_t)(((unsigned long long)(blockIdx.x + 1) * n_rows) / G);
+    // first range holding virtual row vb: a 32-way search by the whole warp
+    // (ranges[0].x = 0 <= vb, ranges sorted by .x), 3 L2 round trips for 4,096 ranges
+    int s = 0;
+    int4 rg = make_int4(0, 0, 0, 0);
+    if (vb < ve && n_ranges > 0) {
+      int lo = 0, hi = (int)n_ranges - 1;
+      rg = s_rg0;
+      while (hi > lo) {
+        const int step = (hi - lo + 32) >> 5;
+        const int pos = lo + lane * step;
+        const int4 e = pos <= hi ? __ldcg(&P.ranges[pos]) : make_int4(0x7fffffff, 0, 0, 0);
+        const int j = 31 - __clz(__ballot_sync(FULL_MASK, (uint32_t)e.x <= vb));
+        rg.x = __shfl_sync(FULL_MASK, e.x, j);  // the winner's entry: ranges[new lo]
+        rg.y = __shfl_sync(FULL_MASK, e.y, j);
+        rg.z = __shfl_sync(FULL_MASK, e.z, j);
+        rg.w = __shfl_sync(FULL_MASK, e.w, j);
+        lo += j * step;
+        hi = min(hi, lo + step - 1);
+      }
+      s = lo;
+    }
     if (lane == 0) {
       const uint64_t policy = policy_evict_first();
-      const unsigned long long pc = ld_volatile_u64(P.packed_counts);
-      const uint32_t n_ranges = (uint32_t)(pc >> 32), n_rows = (uint32_t)pc;
-      const uint32_t vb = (uint32_t)(((unsigned long long)blockIdx.x * n_rows) / gridDim.x);
-      const uint32_t ve = (uint32_t)(((unsigned long long)(blockIdx.x + 1) * n_rows) / gridDim.x);
-      int s = 0;
-      int4 rg = make_int4(0, 0, 0, 0);
-      if (vb < ve && n_ranges > 0) {
-        int lo = 0, hi = (int)n_ranges - 1;
-        while (lo < hi) {
-          const int mid = (lo + hi + 1) >> 1;
-          if ((uint32_t)__ldcg(&P.ranges[mid].x) <= vb) lo = mid; else hi = mid - 1;
-        }
-        s = lo;
-        rg = __ldcg(&P.ranges[s]);
-      }
+      const void* theta_line = reinterpret_cast<const void*>((uintptr_t)P.theta_key & ~(uintptr_t)15);
       uint32_t v = vb;
       int it = 0;
       bool ok = true;
@@ -160,7 +193,11 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       int4 rg_next = (s + 1 < (int)n_ranges && vb < ve) ? __ldcg(&P.ranges[s + 1]) : make_int4(0, 0, 0, 0);
       while (v < ve) {
         const int stage = it % STAGES, f = it / STAGES;
-        if (f > 0 && !mbar_wait(&empty[stage], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) { ok = false; break; }
+        if (f > 0 && !mbar_wait(&empty[stage], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) {
+          ok = false;
+          s_err = 1;
+          break;
+        }
         int2* runs = stage_runs + stage * 32;
         int n = 0, nr = 0;
         uint32_t run_end = 0xffffffffu;  // leaf row just past the open run
@@ -182,7 +219,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
         }
         stage_n[stage] = n;
         stage_nr[stage] = nr;
-        mbar_arrive_expect_tx(&full[stage], (uint32_t)n * (uint32_t)P.row_bytes);
+        mbar_arrive_expect_tx(&full[stage], (uint32_t)n * (uint32_t)P.row_bytes + 16u);
+        tma_load_1d(smem + L.side_off + (size_t)stage * 16, theta_line, 16u, &full[stage]);
         unsigned char* dst = smem + L.stages_off + (size_t)stage * L.stage_bytes;
         for (int i = 0; i < nr; ++i) {
           const int2 r0 = runs[i];
@@ -193,7 +231,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
         ++it;
       }
       const int stage = it % STAGES, f = it / STAGES;
-      if (ok && f > 0) mbar_wait(&empty[stage], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY);
+      if (ok && f > 0 && !mbar_wait(&empty[stage], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) s_err = 1;
       stage_n[stage] = -1;
       mbar_arrive(&full[stage]);
     }
@@ -209,16 +247,37 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     unsigned long long* tk = topk_all + warp * SORTN;
     uint32_t theta_w = 0;                                 // this warp's k-th best key
     uint32_t theta = ld_volatile_u32(P.theta_key);        // filter key (max of both)
-    uint32_t g_pending = theta;                           // global key loaded one stage ahead
     int cnt = 0;                                          // buffered candidates
     uint32_t published = 0;
 
+    // tk[0..k) holds the warp's k best (sorted), tk[k..k+cnt) the buffered
+    // candidates, everything above is zero; a merge sorts only the live prefix
+    // (rounded up to a power of two) and clears what falls below the k-th
+    // up to 128 live values are sorted in registers (R per lane), more in shared memory
+    auto sort_regs = [&](auto r_tag) {
+      constexpr int R = decltype(r_tag)::value;
+      unsigned long long v[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) v[r] = tk[lane * R + r];
+      warp_sort_regs_desc<R>(v, lane);
+#pragma unroll
+      for (int r = 0; r < R; ++r) tk[lane * R + r] = (lane * R + r < k) ? v[r] : 0ull;
+    };
     auto merge = [&]() {
       __syncwarp();
-      warp_bitonic_desc(tk, SORTN, lane);
-      // only the warp's k best can reach the final list: the rest are cleared,
-      // so the CTA select below sees at most k non-zeros per warp
-      for (int i = k + lane; i < SORTN; i += 32) tk[i] = 0ull;
+      const int live = k + cnt;  // <= k + BUF <= SORTN
+      if (live <= 32) {
+        sort_regs(std::integral_constant<int, 1>{});
+      } else if (live <= 64) {
+        sort_regs(std::integral_constant<int, 2>{});
+      } else if (live <= 128) {
+        sort_regs(std::integral_constant<int, 4>{});
+      } else {
+        int n2 = 256;
+        while (n2 < live) n2 <<= 1;
+        warp_bitonic_desc(tk, n2, lane);
+        for (int i = k + lane; i < n2; i += 32) tk[i] = 0ull;
+      }
       __syncwarp();
       cnt = 0;
       const uint32_t kth = cand_key(tk[k - 1]);
@@ -235,15 +294,13 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
 
     for (int it = 0;; ++it) {
       const int stage = it % STAGES, f = it / STAGES;
-      if (!mbar_wait(&full[stage], f & 1, P.err, ERR_TIMEOUT_FULL)) break;
+      if (!mbar_wait(&full[stage], f & 1, P.err, ERR_TIMEOUT_FULL)) {
+        s_err = 1;
+        break;
+      }
       const int n = stage_n[stage];
       if (n < 0) break;
-      {
-        // use the global threshold read during the previous stage and issue the
-        // next read now: its L2 round trip overlaps this stage and the next wait
-        theta = max(theta, __shfl_sync(FULL_MASK, g_pending, 0));
-        if (lane == 0) g_pending = ld_volatile_u32(P.theta_key);
-      }
+      theta = max(theta, side[stage * 4 + theta_word]);
       const float4* stage_f4 =
           reinterpret_cast<const float4*>(smem + L.stages_off + (size_t)stage * L.stage_bytes);
       float acc[RPW];
@@ -314,16 +371,22 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       if (bal) {
         const int nn = __popc(bal);
         if (cnt + nn > BUF) merge();
-        if (cand) tk[KCAP + cnt + __popc(bal & lanemask_lt())] = pack_cand(key, (uint32_t)row);
+        if (cand) tk[k + cnt + __popc(bal & lanemask_lt())] = pack_cand(key, (uint32_t)row);
         cnt += nn;
       }
     }
     if (cnt > 0) merge();
+    if (lane == 0) s_warp_theta[warp] = theta;
   }
   __syncthreads();
   // error path: a wait gave up and bulk copies may still land in the stage ring,
   // which the grid merge below reuses
-  if (tid == 0) s_err = ld_volatile_u32(reinterpret_cast<const uint32_t*>(P.err)) != 0u;
+  // (s_err is this CTA's own flag: only its copies can land in its ring)
+  if (tid == 0) {
+    uint32_t t = 0;
+    for (int w = 0; w < SCAN_CONSUMER_WARPS; ++w) t = max(t, s_warp_theta[w]);
+    s_theta = t;
+  }
   __syncthreads();
   if (s_err) {
     if (tid == 0) grace_period();
@@ -331,40 +394,86 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
   }
 
   // ---------------------------------------------------------- CTA merge
+  // theta_key is the k-th best of k distinct scanned rows (or an external
+  // bound), so no candidate below it can reach the final list: both merges
+  // skip those, and usually little more than k candidates remain grid-wide.
+  // The CTA's k-th best is published as a threshold too (k distinct rows).
   const int selN = KCAP;  // KCAP is a power of two >= k
-  const int got = block_select_topk<false>(topk_all, SCAN_CONSUMER_WARPS * SORTN, k, sel, selN, scratch);
-  (void)got;
-  for (int i = tid; i < k; i += blockDim.x) P.cta_lists[(size_t)blockIdx.x * k + i] = sel[i];
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    const uint32_t t = atomicAdd(P.done, 1u);
-    s_is_last = (t == gridDim.x - 1);
+  unsigned long long* ring = reinterpret_cast<unsigned long long*>(smem + L.stages_off);  // idle now
+  if constexpr (KCAP == 32) {
+    // k <= 32: warp 0 merges the eight sorted warp lists in registers (lane j
+    // holds the j-th value) as a tree of independent pairwise merges; left
+    // operands come out descending and right ones ascending, so no list is
+    // reversed between levels.  Warp 0 then takes the CTA's ticket itself.
+    static_assert(SCAN_CONSUMER_WARPS == 8, "three merge levels");
+    if (warp == 0) {
+      unsigned long long r[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        r[i] = warp_merge_top32(topk_all[(2 * i) * SORTN + lane], topk_all[(2 * i + 1) * SORTN + (31 - lane)],
+                                (i & 1) == 0, lane);
+      const unsigned long long s0 = warp_merge_top32(r[0], r[1], true, lane);
+      const unsigned long long s1 = warp_merge_top32(r[2], r[3], false, lane);
+      const unsigned long long m = warp_merge_top32(s0, s1, true, lane);
+      const unsigned long long kth = __shfl_sync(FULL_MASK, m, k - 1);
+      if (lane < k) {
+        P.cta_lists[(size_t)blockIdx.x * k + lane] = m;
+        if (lane == 0 && kth != 0ull && cand_key(kth) > s_theta) atomicMax(P.theta_key, cand_key(kth));
+        __threadfence();
+      }
+      __syncwarp();
+      if (lane == 0) s_is_last = (atomicAdd(P.done, 1u) == G - 1);
+    }
+  } else {
+    const int got = block_rank_topk<RANK_CAP>(topk_all, SCAN_CONSUMER_WARPS * SORTN, k, sel, selN, ring,
+                                              &s_rank_count, s_theta) < 0
+                        ? block_select_topk<false>(topk_all, SCAN_CONSUMER_WARPS * SORTN, k, sel, selN, scratch,
+                                                   s_theta)
+                        : 0;
+    (void)got;
+    static_assert(KMAX <= SCAN_THREADS, "one thread per list entry");
+    if (tid < k) {
+      const unsigned long long c = sel[tid];
+      P.cta_lists[(size_t)blockIdx.x * k + tid] = c;
+      if (tid == k - 1 && c != 0ull && cand_key(c) > s_theta) atomicMax(P.theta_key, cand_key(c));
+      __threadfence();
+    }
   }
   __syncthreads();
+  if (KCAP != 32 && tid == 0) {
+    __threadfence();
+    const uint32_t t = atomicAdd(P.done, 1u);
+    s_is_last = (t == G - 1);
+  }
+  if (KCAP != 32) __syncthreads();
   if (!s_is_last) return;
   __threadfence();
 
   // ---------------------------------------------------------- grid merge (last CTA)
   // The ring is idle now: stage the gathered lists in its shared memory when
   // they fit, so the radix passes run on shared memory instead of L2.
-  const int M = gridDim.x * k + ((P.final_mode && P.merge_seed) ? k : 0);
+  const int mg = (int)G * k;  // gathered lists
+  const int M = mg + ((P.final_mode && P.merge_seed) ? k : 0);
   int cnt_sel;
-  if ((size_t)M * 8 <= (size_t)STAGES * L.stage_bytes) {
-    unsigned long long* buf = reinterpret_cast<unsigned long long*>(smem + L.stages_off);
-    const int mg = gridDim.x * k;
+  if ((size_t)(M + RANK_CAP) * 8 <= (size_t)STAGES * L.stage_bytes) {
+    unsigned long long* buf = ring;
+    // the threshold is re-read beside the gather (every CTA published before
+    // its ticket), so the rank pass usually sees little more than k survivors
+    const uint32_t th = tid == 0 ? ld_volatile_u32(P.theta_key) : 0u;
+#pragma unroll 8
     for (int i = tid; i < mg; i += blockDim.x) buf[i] = __ldcg(P.cta_lists + i);
     for (int i = mg + tid; i < M; i += blockDim.x) buf[i] = P.seed_list[i - mg];
+    if (tid == 0) s_theta = max(s_theta, th);
     __syncthreads();
-    cnt_sel = block_select_topk<false>(buf, M, k, sel, selN, scratch);
+    cnt_sel = block_rank_topk<RANK_CAP>(buf, M, k, sel, selN, buf + M, &s_rank_count, s_theta);
+    if (cnt_sel < 0) cnt_sel = block_select_topk<false>(buf, M, k, sel, selN, scratch, s_theta);
   } else {
     if (P.final_mode && P.merge_seed) {
-      for (int i = tid; i < k; i += blockDim.x) P.cta_lists[(size_t)gridDim.x * k + i] = P.seed_list[i];
+      for (int i = tid; i < k; i += blockDim.x) P.cta_lists[(size_t)mg + i] = P.seed_list[i];
       __threadfence_block();
       __syncthreads();
     }
-    cnt_sel = block_select_topk<true>(P.cta_lists, M, k, sel, selN, scratch);
+    cnt_sel = block_select_topk<true>(P.cta_lists, M, k, sel, selN, scratch, s_theta);
   }
   if (!P.final_mode) {
     for (int i = tid; i < k; i += blockDim.x) P.seed_list[i] = sel[i];
@@ -778,6 +887,12 @@ static int vpl_bucket(int D4) {
 static int kcap_bucket(int k) { return k <= 32 ? 32 : (k <= 128 ? 128 : 256); }
 static int rows_per_stage(int vpl) { return vpl <= 4 ? 32 : (vpl <= 8 ? 16 : 8); }
 static int sortn_for(int kcap) { return kcap + 64 <= 128 ? 128 : (kcap + 64 <= 256 ? 256 : 512); }
+// Rows per CTA below which a scan uses fewer CTAs: 32 (one to four stages),
+// so that every CTA's k-th best (k <= 32) is a useful threshold.
+static int min_rows_for(int row_bytes) {
+  (void)row_bytes;
+  return 32;
+}
 static int stages_for(int vpl, int row_bytes) {
   const size_t sb = align_up((size_t)rows_per_stage(vpl) * row_bytes, 128);
   int s = (int)(147456 / sb);
@@ -856,6 +971,7 @@ static ScanParams scan_params(const IndexView& ix, const Workspace& ws, const fl
   P.row_bytes = ix.D * 4;
   P.k = k;
   P.stages = stages_for(vpl_bucket(ix.D4), P.row_bytes);
+  P.min_rows = min_rows_for(P.row_bytes);
   P.seed_list = ws.ctrl->seed_list;
   P.seed_T_key = &ws.ctrl->seed_T_key;
   P.out_scores = out_scores;
@@ -971,6 +1087,7 @@ cudaError_t launch_flat_scan(const float* leaf, int D, int N, const float* q, in
   F.row_bytes = D * 4;
   F.k = k;
   F.stages = stages_for(vpl, F.row_bytes);
+  F.min_rows = min_rows_for(F.row_bytes);
   F.final_mode = 1;
   F.merge_seed = 0;
   F.seed_list = ctrl->seed_list;

@@ -29,7 +29,7 @@ static __device__ void block_bitonic_desc(unsigned long long* a, int n) {
   for (int size = 2; size <= n; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       for (int i = threadIdx.x; i < (n >> 1); i += blockDim.x) {
-        const int lo = 2 * stride * (i / stride) + (i % stride);
+        const int lo = ((i & ~(stride - 1)) << 1) | (i & (stride - 1));
         const int hi = lo + stride;
         const bool up = (lo & size) == 0;
         const unsigned long long x = a[lo], y = a[hi];
@@ -45,7 +45,7 @@ static __device__ void warp_bitonic_desc(unsigned long long* a, int n, int lane)
   for (int size = 2; size <= n; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       for (int i = lane; i < (n >> 1); i += 32) {
-        const int lo = 2 * stride * (i / stride) + (i % stride);
+        const int lo = ((i & ~(stride - 1)) << 1) | (i & (stride - 1));
         const int hi = lo + stride;
         const bool up = (lo & size) == 0;
         const unsigned long long x = a[lo], y = a[hi];
@@ -54,6 +54,103 @@ static __device__ void warp_bitonic_desc(unsigned long long* a, int n, int lane)
       __syncwarp();
     }
   }
+}
+
+// Warp-wide descending bitonic sort of 32 * R values held in registers: lane l
+// holds elements l*R .. l*R + R-1 in v[0..R).  Strides below R pair registers of
+// one lane; the others pair lanes through shuffles.
+template <int R>
+__device__ __forceinline__ void warp_sort_regs_desc(unsigned long long (&v)[R], int lane) {
+  constexpr int N = 32 * R;
+#pragma unroll
+  for (int size = 2; size <= N; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride < R) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int pr = r ^ stride;
+          if (pr > r) {
+            const bool desc = ((lane * R + r) & size) == 0;  // the lower element keeps the max
+            const unsigned long long a = v[r], b = v[pr];
+            if (desc ? (a < b) : (a > b)) {
+              v[r] = b;
+              v[pr] = a;
+            }
+          }
+        }
+      } else {
+        const int lx = stride / R;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const unsigned long long b = __shfl_xor_sync(FULL_MASK, v[r], lx);
+          const bool desc = ((lane * R + r) & size) == 0;
+          const bool lower = (lane & lx) == 0;
+          v[r] = (lower == desc) ? (v[r] > b ? v[r] : b) : (v[r] < b ? v[r] : b);
+        }
+      }
+    }
+  }
+}
+
+// Top 32 of two sorted 32-value lists held one value per lane: a descending,
+// b ascending.  max(a[j], b[j]) is a bitonic sequence holding exactly the top 32
+// of the union; five half-cleaner steps sort it (descending or ascending).
+__device__ __forceinline__ unsigned long long warp_merge_top32(unsigned long long a_desc, unsigned long long b_asc,
+                                                               bool desc, int lane) {
+  unsigned long long c = a_desc > b_asc ? a_desc : b_asc;
+#pragma unroll
+  for (int st = 16; st > 0; st >>= 1) {
+    const unsigned long long o = __shfl_xor_sync(FULL_MASK, c, st);
+    const bool keep_max = ((lane & st) == 0) == desc;
+    c = keep_max ? (c > o ? c : o) : (c < o ? c : o);
+  }
+  return c;
+}
+
+// Top-k by direct ranking, for merges with few survivors: the non-empty
+// candidates of src[0..M) (shared memory) whose key is not below min_key are
+// compacted into tmp[0..CAP); each one's rank is the number of larger ones
+// (candidates are unique) and ranks below k land in sel.  Returns min(k,
+// survivors) with sel[0..ret) sorted descending and sel[ret..selN) zero, or -1
+// when more than CAP survive (sel is then undefined: use block_select_topk).
+// `count` is a shared word of the caller.  All threads of the block call it.
+template <int CAP>
+static __device__ int block_rank_topk(const unsigned long long* src, int M, int k, unsigned long long* sel, int selN,
+                                      unsigned long long* tmp, uint32_t* count, uint32_t min_key) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthreads = blockDim.x;
+  const unsigned long long floor_v = (unsigned long long)min_key << 32;
+  if (tid == 0) *count = 0;
+  for (int i = tid; i < selN; i += nthreads) sel[i] = 0ull;
+  __syncthreads();
+  for (int base = warp * 32; base < M; base += nthreads) {
+    const int i = base + lane;
+    const unsigned long long v = i < M ? src[i] : 0ull;
+    const bool pass = v != 0ull && v >= floor_v;
+    const uint32_t bal = __ballot_sync(FULL_MASK, pass);
+    uint32_t pos = 0;
+    if (lane == 0 && bal) pos = atomicAdd(count, (uint32_t)__popc(bal));
+    pos = __shfl_sync(FULL_MASK, pos, 0) + __popc(bal & lanemask_lt());
+    if (pass && pos < (uint32_t)CAP) tmp[pos] = v;
+  }
+  __syncthreads();
+  const int n = (int)*count;
+  if (n > CAP) {
+    __syncthreads();  // every thread has read *count before the caller reuses it
+    return -1;
+  }
+  for (int t = tid; t < n; t += nthreads) {
+    const unsigned long long v = tmp[t];
+    int r = 0, j = 0;
+    for (; j + 8 <= n; j += 8) {  // eight independent loads in flight
+#pragma unroll
+      for (int u = 0; u < 8; ++u) r += tmp[j + u] > v;
+    }
+    for (; j < n; ++j) r += tmp[j] > v;
+    if (r < k) sel[r] = v;
+  }
+  __syncthreads();
+  return n < k ? n : k;
 }
 
 // Selects the k largest non-zero packed candidates of src[0..M) (unique when
@@ -66,12 +163,16 @@ static __device__ void warp_bitonic_desc(unsigned long long* a, int n, int lane)
 //   - the passes stop as soon as the bin that holds the k-th value holds exactly
 //     the number still needed: the selection is then "everything with this
 //     prefix or above", usually after 2-4 of the 8 digits.
-// sel must hold selN >= k entries (power of 2).  Returns the number selected
-// (min(k, non-zeros)); sel[0..ret) is sorted descending and sel[ret..selN) is
-// zero.  All threads of the block call it; blockDim.x is a multiple of 32.
+// Candidates whose key (upper 32 bits) is below min_key count as empty (the
+// caller knows they cannot be among the k best); min_key must be the same in
+// every thread.  sel must hold selN >= k entries (power of 2).  Returns the
+// number selected (min(k, non-empty)); sel[0..ret) is sorted descending and
+// sel[ret..selN) is zero.  All threads of the block call it; blockDim.x is a
+// multiple of 32.
 template <bool GLOBAL>
 static __device__ int block_select_topk(const unsigned long long* src, int M, int k, unsigned long long* sel,
-                                        int selN, SelectScratch* s) {
+                                        int selN, SelectScratch* s, uint32_t min_key = 0u) {
+  const unsigned long long floor_v = (unsigned long long)min_key << 32;  // v >= floor_v <=> key >= min_key
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthreads = blockDim.x;
   for (int i = tid; i < 256; i += nthreads) s->hist[i] = 0;
   for (int i = tid; i < selN; i += nthreads) sel[i] = 0ull;
@@ -84,7 +185,7 @@ static __device__ int block_select_topk(const unsigned long long* src, int M, in
     for (int base = warp * 32; base < M; base += nthreads) {
       const int i = base + lane;
       const unsigned long long v = (i < M) ? ld_cand<GLOBAL>(src + i) : 0ull;
-      const bool in = v != 0ull && (v & hmask) == prefix;
+      const bool in = v != 0ull && v >= floor_v && (v & hmask) == prefix;
       const uint32_t bin = in ? (uint32_t)(v >> shift) & 255u : 256u;
       const uint32_t peers = __match_any_sync(FULL_MASK, bin);
       if (in && lane == __ffs(peers) - 1) atomicAdd(&s->hist[bin], (uint32_t)__popc(peers));
@@ -141,7 +242,7 @@ static __device__ int block_select_topk(const unsigned long long* src, int M, in
   // everything at or above the k-th value's resolved prefix: exactly kk entries
   for (int i = tid; i < M; i += nthreads) {
     const unsigned long long v = ld_cand<GLOBAL>(src + i);
-    if (v != 0ull && v >= prefix) {
+    if (v != 0ull && v >= floor_v && v >= prefix) {
       const uint32_t pos = atomicAdd(&s->count, 1u);
       if (pos < (uint32_t)selN) sel[pos] = v;
     }
