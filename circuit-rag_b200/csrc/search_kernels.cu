@@ -379,15 +379,15 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     if (lane == 0) s_warp_theta[warp] = theta;
   }
   __syncthreads();
-  // error path: a wait gave up and bulk copies may still land in the stage ring,
-  // which the grid merge below reuses
-  // (s_err is this CTA's own flag: only its copies can land in its ring)
+  // the merges' threshold: the best any warp of this CTA saw (no L2 read)
   if (tid == 0) {
     uint32_t t = 0;
     for (int w = 0; w < SCAN_CONSUMER_WARPS; ++w) t = max(t, s_warp_theta[w]);
     s_theta = t;
   }
   __syncthreads();
+  // error path: one of this CTA's waits gave up, so its own bulk copies may still
+  // land in the stage ring, which the merges below reuse
   if (s_err) {
     if (tid == 0) grace_period();
     __syncthreads();
@@ -425,12 +425,9 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       if (lane == 0) s_is_last = (atomicAdd(P.done, 1u) == G - 1);
     }
   } else {
-    const int got = block_rank_topk<RANK_CAP>(topk_all, SCAN_CONSUMER_WARPS * SORTN, k, sel, selN, ring,
-                                              &s_rank_count, s_theta) < 0
-                        ? block_select_topk<false>(topk_all, SCAN_CONSUMER_WARPS * SORTN, k, sel, selN, scratch,
-                                                   s_theta)
-                        : 0;
-    (void)got;
+    if (block_rank_topk<RANK_CAP>(topk_all, SCAN_CONSUMER_WARPS * SORTN, k, sel, selN, ring, &s_rank_count,
+                                  s_theta) < 0)
+      block_select_topk<false>(topk_all, SCAN_CONSUMER_WARPS * SORTN, k, sel, selN, scratch, s_theta);
     static_assert(KMAX <= SCAN_THREADS, "one thread per list entry");
     if (tid < k) {
       const unsigned long long c = sel[tid];
@@ -440,18 +437,20 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     }
   }
   __syncthreads();
-  if (KCAP != 32 && tid == 0) {
-    __threadfence();
-    const uint32_t t = atomicAdd(P.done, 1u);
-    s_is_last = (t == G - 1);
+  if constexpr (KCAP != 32) {
+    if (tid == 0) {
+      __threadfence();
+      s_is_last = (atomicAdd(P.done, 1u) == G - 1);
+    }
+    __syncthreads();
   }
-  if (KCAP != 32) __syncthreads();
   if (!s_is_last) return;
   __threadfence();
 
   // ---------------------------------------------------------- grid merge (last CTA)
   // The ring is idle now: stage the gathered lists in its shared memory when
-  // they fit, so the radix passes run on shared memory instead of L2.
+  // they fit (with room for the rank select's survivors), so the selects run on
+  // shared memory instead of L2.
   const int mg = (int)G * k;  // gathered lists
   const int M = mg + ((P.final_mode && P.merge_seed) ? k : 0);
   int cnt_sel;

@@ -87,11 +87,18 @@ typedef struct {
 circuit_index_t circuit_load_index(const char* filepath, int device_id);
 
 /* Host query [dim] -> host out_scores[k] (descending), out_ids[k] (original ids).
- * Blocking.  reference: circuit.h:25-32, gpu_index.cpp:242-330 */
+ * Blocking.  From the second call with the same k (and path) the search replays a
+ * CUDA graph: the kernels read the query from, and write the results into, the
+ * handle's mapped pinned staging block (no copy-engine operation).
+ * reference: circuit.h:25-32, gpu_index.cpp:242-330 */
 int circuit_search(circuit_index_t index, const float* query, int k, float* out_scores, int* out_ids,
                    circuit_trace_t* trace);
 
 /* Device query -> device outputs.  Blocking (synchronises the handle's stream).
+ * Graph replay as above when the query is 16-byte aligned, the outputs 4-byte
+ * aligned and all three are device (or managed) memory of the index's device:
+ * the kernels then read the query from, and write scores / ids to, the caller's
+ * buffers directly.  Other pointers take copies, which report bad ones as errors.
  * reference: circuit.h:36-43, gpu_index.cpp:333-386 */
 int circuit_search_device(circuit_index_t index, const float* dev_query, int k, float* dev_out_scores,
                           int* dev_out_ids, circuit_trace_t* trace);
