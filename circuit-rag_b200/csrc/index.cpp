@@ -475,8 +475,9 @@ int circuit_index_opaque::search_blocking(const float* query, bool host_ptrs, in
         built = ok && ended && graph && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
         if (graph) cudaGraphDestroy(graph);
       }
-      cudaGetLastError();  // a failed capture falls back to direct launches
+      cudaGetLastError();  // a failed capture falls back to direct launches, for good
       if (built) g = host_graphs.emplace(key, exec).first;
+      else host_graph_calls[key] = std::numeric_limits<int>::min();
     }
     if (g != host_graphs.end()) {
       if (host_ptrs) {

@@ -888,10 +888,7 @@ static int rows_per_stage(int vpl) { return vpl <= 4 ? 32 : (vpl <= 8 ? 16 : 8);
 static int sortn_for(int kcap) { return kcap + 64 <= 128 ? 128 : (kcap + 64 <= 256 ? 256 : 512); }
 // Rows per CTA below which a scan uses fewer CTAs: 32 (one to four stages),
 // so that every CTA's k-th best (k <= 32) is a useful threshold.
-static int min_rows_for(int row_bytes) {
-  (void)row_bytes;
-  return 32;
-}
+constexpr int SCAN_MIN_ROWS = 32;
 static int stages_for(int vpl, int row_bytes) {
   const size_t sb = align_up((size_t)rows_per_stage(vpl) * row_bytes, 128);
   int s = (int)(147456 / sb);
@@ -970,7 +967,7 @@ static ScanParams scan_params(const IndexView& ix, const Workspace& ws, const fl
   P.row_bytes = ix.D * 4;
   P.k = k;
   P.stages = stages_for(vpl_bucket(ix.D4), P.row_bytes);
-  P.min_rows = min_rows_for(P.row_bytes);
+  P.min_rows = SCAN_MIN_ROWS;
   P.seed_list = ws.ctrl->seed_list;
   P.seed_T_key = &ws.ctrl->seed_T_key;
   P.out_scores = out_scores;
@@ -1086,7 +1083,7 @@ cudaError_t launch_flat_scan(const float* leaf, int D, int N, const float* q, in
   F.row_bytes = D * 4;
   F.k = k;
   F.stages = stages_for(vpl, F.row_bytes);
-  F.min_rows = min_rows_for(F.row_bytes);
+  F.min_rows = SCAN_MIN_ROWS;
   F.final_mode = 1;
   F.merge_seed = 0;
   F.seed_list = ctrl->seed_list;
