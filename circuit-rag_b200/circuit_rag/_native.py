@@ -48,6 +48,7 @@ EXPORTED_SYMBOLS = (
     "circuit_search_batch_async",
     "circuit_batch_overflow",
     "circuit_search_batch",
+    "circuit_search_batch_device",
 )
 
 
@@ -116,6 +117,7 @@ def _declare(lib):
         "circuit_search_finish_async": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _P, _P]),
         "circuit_batch_overflow": (_I, [_P, _P]),
         "circuit_search_batch": (_I, [_P, _P, _I, _I, _P, _P]),
+        "circuit_search_batch_device": (_I, [_P, _P, _I, _I, _P, _P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -695,6 +695,39 @@ int circuit_search_batch(circuit_index_t index, const float* host_queries, int n
 }
 
 
+int circuit_search_batch_device(circuit_index_t index, const float* dev_queries, int num_queries, int k,
+                                float* dev_out_scores, int* dev_out_ids) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  if (!dev_queries || !dev_out_scores || !dev_out_ids || num_queries < 1) {
+    set_error("null batch pointer or num_queries < 1");
+    return CIRCUIT_ERR_ARG;
+  }
+  cudaStream_t st = index->stream;
+  int rc = index->search_batch_async(dev_queries, num_queries, k, dev_out_scores, dev_out_ids, st);
+  if (rc != CIRCUIT_OK) return rc;
+  int over = 0;
+  if (!cuda_ok(cudaMemcpyAsync(&over, index->bw.overflow, sizeof(int), cudaMemcpyDeviceToHost, st), "D2H overflow") ||
+      !cuda_ok(cudaStreamSynchronize(st), "batch sync"))
+    return CIRCUIT_ERR_CUDA;
+  if (over == 0) return CIRCUIT_OK;
+  // the first id of each row marks an overflowed query (-2): answer those rows
+  // in place with the single-query search, on the same stream
+  std::vector<int> first((size_t)num_queries);
+  if (!cuda_ok(cudaMemcpy2DAsync(first.data(), sizeof(int), dev_out_ids, sizeof(int) * (size_t)k, sizeof(int),
+                                 (size_t)num_queries, cudaMemcpyDeviceToHost, st),
+               "D2H first ids") ||
+      !cuda_ok(cudaStreamSynchronize(st), "batch sync"))
+    return CIRCUIT_ERR_CUDA;
+  const int64_t min_hier = 10001;  // the blocking single-query routing
+  for (int q = 0; q < num_queries; ++q) {
+    if (first[(size_t)q] != -2) continue;
+    rc = index->search_async(dev_queries + (size_t)q * index->D, k, min_hier, dev_out_scores + (size_t)q * k,
+                             dev_out_ids + (size_t)q * k, nullptr, st, nullptr, nullptr);
+    if (rc != CIRCUIT_OK) return rc;
+  }
+  return cuda_ok(cudaStreamSynchronize(st), "fallback sync") ? CIRCUIT_OK : CIRCUIT_ERR_CUDA;
+}
+
 const char* circuit_last_error(void) { return cb::get_error(); }
 int circuit_abi_version(void) { return CIRCUIT_ABI_VERSION; }
 

@@ -111,6 +111,13 @@ def test_batch_overflow_falls_back_to_single_query():
     scores, ids = circuit_search_batch(Q, index, 10)
     assert int(ids.min()) >= 0
     _check_batch(X, Q, index, 10, scores, ids, compare_single=False)
+    # the blocking device-buffer call answers the overflowed row in place
+    s2 = torch.full((4, 10), float("nan"), device=DEV)
+    i2 = torch.full((4, 10), -7, dtype=torch.int32, device=DEV)
+    torch.cuda.synchronize()
+    rc = _native.lib().circuit_search_batch_device(handle, Q.data_ptr(), 4, 10, s2.data_ptr(), i2.data_ptr())
+    assert rc == 0, _native.last_error()
+    assert torch.equal(i2, ids) and torch.equal(s2, scores)
 
 
 def test_batch_host_buffers_through_c_abi():
@@ -125,6 +132,14 @@ def test_batch_host_buffers_through_c_abi():
                                             i.ctypes.data)
     assert rc == 0, _native.last_error()
     _check_batch(X, Qh.to(DEV), index, 10, torch.from_numpy(s).to(DEV), torch.from_numpy(i).to(DEV))
+    Qd = Qh.to(DEV)
+    sd = torch.empty(200, 10, device=DEV)
+    idd = torch.empty(200, 10, dtype=torch.int32, device=DEV)
+    torch.cuda.synchronize()
+    rc = _native.lib().circuit_search_batch_device(index.native_handle(), Qd.data_ptr(), 200, 10, sd.data_ptr(),
+                                                   idd.data_ptr())
+    assert rc == 0, _native.last_error()
+    assert np.array_equal(sd.cpu().numpy(), s) and np.array_equal(idd.cpu().numpy(), i)
 
 
 def test_batch_rejects_unsupported():
