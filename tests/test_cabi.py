@@ -46,6 +46,28 @@ def test_abi_version_and_null_handles():
     L.circuit_destroy_index(None)  # no-op
 
 
+def test_extension_entry_points_reject_null_handles():
+    """Every entry point that takes an index handle returns CIRCUIT_ERR_NULL (-1)
+    for a null one before any CUDA call (the reference's convention, extended)."""
+    L = _native.lib()
+    q = np.zeros(8, np.float32)
+    s = np.zeros(8, np.float32)
+    i = np.zeros(8, np.int32)
+    n = ctypes.c_int(0)
+    info = (ctypes.c_int64 * 8)()
+    tx = _native.TraceEx()
+    P = lambda a: a.ctypes.data  # noqa: E731
+    assert L.circuit_search_batch(None, P(q), 2, 4, P(s), P(i)) == -1
+    assert L.circuit_search_batch_device(None, P(q), 2, 4, P(s), P(i)) == -1
+    assert L.circuit_search_batch_async(None, P(q), 2, 4, P(s), P(i), None, None, None) == -1
+    assert L.circuit_batch_overflow(None, ctypes.byref(n)) == -1
+    assert L.circuit_search_async(None, P(q), 4, 10001, P(s), P(i), None, None, None, None) == -1
+    assert L.circuit_search_seed_async(None, P(q), 4, P(s), None) == -1
+    assert L.circuit_search_finish_async(None, P(q), 4, P(s), P(s), P(i), None, None, None, None) == -1
+    assert L.circuit_index_info(None, info) == -1
+    assert L.circuit_last_trace(None, ctypes.byref(tx)) == -1
+
+
 @pytest.mark.parametrize("mutate,msg", [
     (lambda d: b"XXXXXXXX" + d[8:], "magic"),
     (lambda d: d[:9], "too small"),
