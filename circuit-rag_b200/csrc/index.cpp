@@ -493,23 +493,7 @@ int circuit_index_opaque::search_blocking(const float* query, bool host_ptrs, in
       last_stream = stream;
       last_path = hier;
       last_k = k;
-      if (host_ptrs) {
-        std::memcpy(out_scores, h_scores, sizeof(float) * k);
-        std::memcpy(out_ids, h_ids, sizeof(int) * k);
-      }
-      have_host_ctrl = true;
-      if (h_ctrl->error) {
-        set_error("device-side wait timed out (error bits " + std::to_string(h_ctrl->error) + ")");
-        return CIRCUIT_ERR_TIMEOUT;
-      }
-      if (trace) {
-        circuit_trace_ex_t tx;
-        fill_trace(*h_ctrl, &tx);
-        trace->latency_us =
-            (float)std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
-        trace->vectors_scored = (int)std::min<int64_t>(tx.vectors_scored, std::numeric_limits<int>::max());
-      }
-      return CIRCUIT_OK;
+      return finish_blocking(host_ptrs, k, out_scores, out_ids, trace, t0);
     }
   }
   if (host_ptrs) {
@@ -529,6 +513,13 @@ int circuit_index_opaque::search_blocking(const float* query, bool host_ptrs, in
       !cuda_ok(cudaMemcpyAsync(h_ctrl, ws.ctrl, cb::CTRL_RESET_BYTES, cudaMemcpyDeviceToHost, stream), "copy ctrl") ||
       !cuda_ok(cudaStreamSynchronize(stream), "search sync"))
     return CIRCUIT_ERR_CUDA;
+  return finish_blocking(host_ptrs, k, out_scores, out_ids, trace, t0);
+}
+
+// End of a blocking search once its stream has synchronised: host results leave
+// the staging block, a device-side timeout becomes an error, the trace is filled.
+int circuit_index_opaque::finish_blocking(bool host_ptrs, int k, float* out_scores, int* out_ids,
+                                          circuit_trace_t* trace, std::chrono::steady_clock::time_point t0) {
   if (host_ptrs) {
     std::memcpy(out_scores, h_scores, sizeof(float) * k);
     std::memcpy(out_ids, h_ids, sizeof(int) * k);

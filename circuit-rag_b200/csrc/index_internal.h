@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <string>
 #include <map>
+#include <chrono>
 #include <vector>
 
 #include "../../include/circuit.h"
@@ -75,6 +76,8 @@ struct circuit_index_opaque {
                    cudaStream_t st, cudaEvent_t e0, cudaEvent_t e1);
   int search_blocking(const float* query, bool host_ptrs, int k, float* out_scores, int* out_ids,
                       circuit_trace_t* trace);
+  int finish_blocking(bool host_ptrs, int k, float* out_scores, int* out_ids, circuit_trace_t* trace,
+                      std::chrono::steady_clock::time_point t0);
   void fill_trace(const cb::SearchCtrl& c, circuit_trace_ex_t* t) const;
   int ensure_batch(int B);
   int search_batch_async(const float* dq, int B, int k, float* dscores, int* dids, cudaStream_t st,

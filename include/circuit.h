@@ -202,9 +202,11 @@ int circuit_batch_overflow(circuit_index_t index, int* out_count);
 /* Blocking host-buffer variant of circuit_search_batch_async (host_scores / host_ids [num_queries, k]). */
 int circuit_search_batch(circuit_index_t index, const float* host_queries, int num_queries, int k, float* host_scores,
                          int* host_ids);
-/* Blocking device-buffer variant (synchronises the handle's stream): like
- * circuit_search_batch_async, and rows whose candidate list overflowed are
- * answered in place by the single-query search, so no id -2 remains. */
+/* Blocking device-buffer variant (runs on and synchronises the handle's own
+ * stream, so the caller makes sure the queries are ready, e.g. by synchronising
+ * the stream that wrote them): like circuit_search_batch_async, and rows whose
+ * candidate list overflowed are answered in place by the single-query search,
+ * so no id -2 remains. */
 int circuit_search_batch_device(circuit_index_t index, const float* dev_queries, int num_queries, int k,
                                 float* dev_out_scores, int* dev_out_ids);
 
