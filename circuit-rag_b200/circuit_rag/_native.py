@@ -43,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "circuit_plan_shards",
     "circuit_flat_search_noalloc",
     "circuit_selftest_wait_timeout",
+    "circuit_selftest_batch_wait_timeout",
     "circuit_search_seed_async",
     "circuit_search_finish_async",
     "circuit_search_batch_async",
@@ -114,6 +115,7 @@ def _declare(lib):
         "circuit_search_batch_async": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _P]),
         "circuit_search_seed_async": (_I, [_P, _P, _I, _P, _P]),
         "circuit_selftest_wait_timeout": (_I, [_I, _P]),
+        "circuit_selftest_batch_wait_timeout": (_I, [_P, _P]),
         "circuit_search_finish_async": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _P, _P]),
         "circuit_batch_overflow": (_I, [_P, _P]),
         "circuit_search_batch": (_I, [_P, _P, _I, _I, _P, _P]),

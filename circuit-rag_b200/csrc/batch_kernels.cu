@@ -748,12 +748,9 @@ template <int KB>
 static cudaError_t launch_batch_scan(const void* qmap, const void* xmap, const BatchScanParams& P, int max_pairs,
                                        cudaStream_t st) {
   const int smem = batch_scan_smem(P.stages);
-  static int configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(k_batch_scan<KB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  static SmemOptIn opt_in;
+  cudaError_t e = opt_in.ensure(reinterpret_cast<const void*>(k_batch_scan<KB>), smem);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -766,16 +763,20 @@ static cudaError_t launch_batch_scan(const void* qmap, const void* xmap, const B
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   // pairs that can be resident at once: a persistent grid larger than that
-  // would leave late pairs a second wave
-  static int resident = 0, resident_smem = 0;
-  if (resident_smem != smem) {
+  // would leave late pairs a second wave.  Cached per device (the shared-memory
+  // size is a constant of the build, so it needs no key of its own).
+  static std::atomic<int> resident_by_dev[SmemOptIn::kMaxDevices] = {};
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  int resident = (dev >= 0 && dev < SmemOptIn::kMaxDevices) ? resident_by_dev[dev].load() : 0;
+  if (resident < 1) {
     cfg.gridDim = dim3(2 * max_pairs);
     int n = 0;
-    cudaError_t e = cudaOccupancyMaxActiveClusters(&n, k_batch_scan<KB>, &cfg);
+    e = cudaOccupancyMaxActiveClusters(&n, k_batch_scan<KB>, &cfg);
     if (e != cudaSuccess) return e;
     if (n < 1) return cudaErrorInvalidConfiguration;
     resident = n;
-    resident_smem = smem;
+    if (dev >= 0 && dev < SmemOptIn::kMaxDevices) resident_by_dev[dev].store(n);
   }
   const int pairs = std::min(std::min(P.units, max_pairs), resident);
   cfg.gridDim = dim3(2 * pairs);
@@ -787,12 +788,9 @@ template <int VPL>
 static cudaError_t launch_rescore_t(const float* Q, const IndexView& ix, const BatchWorkspace& bw, int B, int k,
                                     int cap, float* out_s, int* out_i, cudaStream_t st) {
   const size_t smem = (size_t)(RESCORE_CHUNK + 3 * BATCH_MAX_K) * 8 + sizeof(SelectScratch) + 16;
-  static size_t configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(k_batch_rescore<VPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  static SmemOptIn opt_in;
+  cudaError_t e = opt_in.ensure(reinterpret_cast<const void*>(k_batch_rescore<VPL>), (int)smem);
+  if (e != cudaSuccess) return e;
   k_batch_rescore<VPL><<<B, 256, smem, st>>>(Q, ix.leaf, ix.original_ids, ix.D, k, cap, bw.qband, bw.theta,
                                              bw.cand_count, bw.cand, out_s, out_i, bw.overflow);
   return cudaGetLastError();
@@ -805,6 +803,8 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   if ((e = cudaMemsetAsync(bw.theta, 0, sizeof(uint32_t) * B, st)) != cudaSuccess) return e;
   if ((e = cudaMemsetAsync(bw.cand_count, 0, sizeof(int) * B, st)) != cudaSuccess) return e;
   if ((e = cudaMemsetAsync(bw.overflow, 0, sizeof(int), st)) != cudaSuccess) return e;
+  // a wait that gave up in an earlier batch must not send this one down the error path
+  if ((e = cudaMemsetAsync(bw.err, 0, sizeof(int), st)) != cudaSuccess) return e;
   if ((e = cudaMemsetAsync(bw.slots, 0, sizeof(uint32_t) * (size_t)B * k, st)) != cudaSuccess) return e;
   if ((e = cudaMemsetAsync(bw.unit_counter, 0, 2 * sizeof(int), st)) != cudaSuccess) return e;
   BatchScanParams P{};

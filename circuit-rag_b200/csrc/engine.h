@@ -3,11 +3,40 @@
 // is the only public header.
 #pragma once
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
+#include <mutex>
 #include <cuda_runtime.h>
 
 namespace cb {
+
+// Dynamic shared-memory opt-in of one kernel, raised on demand.  The attribute
+// set by cudaFuncSetAttribute belongs to the current device's context, so the
+// size already configured is remembered per device: a process that searches on
+// several GPUs configures each one before its first launch there.  Thread-safe
+// (the slow path takes a mutex; the size recorded for a device only grows).
+class SmemOptIn {
+ public:
+  static constexpr int kMaxDevices = 64;
+  cudaError_t ensure(const void* func, int bytes) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices)
+      return cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (set_[dev].load(std::memory_order_acquire) >= bytes) return cudaSuccess;
+    std::lock_guard<std::mutex> lock(mu_);
+    if (set_[dev].load(std::memory_order_relaxed) >= bytes) return cudaSuccess;
+    e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) set_[dev].store(bytes, std::memory_order_release);
+    return e;
+  }
+
+ private:
+  std::mutex mu_;
+  std::atomic<int> set_[kMaxDevices] = {};
+};
 
 constexpr int KMAX = 256;          // largest k a search accepts
 constexpr int MAX_RANK = 64;       // largest rank r of a parent basis
@@ -155,6 +184,10 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
                                 cudaEvent_t ev_scan_end);
 
 int scan_smem_bytes(int D);
+// One kernel whose mbarrier wait nothing satisfies, run through the bounded
+// wait every search kernel uses: after the limit it or-s ERR_TIMEOUT_FULL into
+// *err and returns (merge_kernels.cu).
+cudaError_t launch_selftest_wait(int* err, cudaStream_t stream);
 int sm_count(int device);
 
 }  // namespace cb

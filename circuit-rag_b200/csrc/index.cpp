@@ -630,6 +630,23 @@ int circuit_index_opaque::search_batch_async(const float* dq, int B, int k, floa
   return CIRCUIT_OK;
 }
 
+int circuit_index_opaque::batch_status(cudaStream_t st, int* overflow) {
+  *overflow = 0;
+  if (!batch_ready || !bw.overflow) return CIRCUIT_OK;
+  int err = 0;
+  if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice") ||
+      !cuda_ok(cudaMemcpyAsync(overflow, bw.overflow, sizeof(int), cudaMemcpyDeviceToHost, st), "D2H overflow") ||
+      !cuda_ok(cudaMemcpyAsync(&err, bw.err, sizeof(int), cudaMemcpyDeviceToHost, st), "D2H batch error bits") ||
+      !cuda_ok(cudaStreamSynchronize(st), "batch sync"))
+    return CIRCUIT_ERR_CUDA;
+  if (err) {
+    set_error("batched search: a device-side wait timed out (error bits " + std::to_string(err) +
+              "); the batch's results are incomplete");
+    return CIRCUIT_ERR_TIMEOUT;
+  }
+  return CIRCUIT_OK;
+}
+
 // ---------------------------------------------------------------- C ABI
 extern "C" {
 
@@ -644,14 +661,7 @@ int circuit_search_batch_async(circuit_index_t index, const float* dev_queries, 
 int circuit_batch_overflow(circuit_index_t index, int* out_count) {
   if (!index) return CIRCUIT_ERR_NULL;
   if (!out_count) { set_error("null out_count"); return CIRCUIT_ERR_ARG; }
-  *out_count = 0;
-  if (!index->batch_ready || !index->bw.overflow) return CIRCUIT_OK;
-  if (!cuda_ok(cudaSetDevice(index->device), "cudaSetDevice") ||
-      !cuda_ok(cudaMemcpyAsync(out_count, index->bw.overflow, sizeof(int), cudaMemcpyDeviceToHost, index->last_stream),
-               "D2H overflow") ||
-      !cuda_ok(cudaStreamSynchronize(index->last_stream), "overflow sync"))
-    return CIRCUIT_ERR_CUDA;
-  return CIRCUIT_OK;
+  return index->batch_status(index->last_stream, out_count);
 }
 
 int circuit_search_batch(circuit_index_t index, const float* host_queries, int num_queries, int k,
@@ -672,9 +682,10 @@ int circuit_search_batch(circuit_index_t index, const float* host_queries, int n
   const size_t ob = (size_t)num_queries * k;
   if (!cuda_ok(cudaMemcpyAsync(host_scores, index->bw.out_scores, sizeof(float) * ob, cudaMemcpyDeviceToHost, st),
                "D2H scores") ||
-      !cuda_ok(cudaMemcpyAsync(host_ids, index->bw.out_ids, sizeof(int) * ob, cudaMemcpyDeviceToHost, st), "D2H ids") ||
-      !cuda_ok(cudaStreamSynchronize(st), "batch sync"))
+      !cuda_ok(cudaMemcpyAsync(host_ids, index->bw.out_ids, sizeof(int) * ob, cudaMemcpyDeviceToHost, st), "D2H ids"))
     return CIRCUIT_ERR_CUDA;
+  int over = 0;
+  if ((rc = index->batch_status(st, &over)) != CIRCUIT_OK) return rc;
   // a query whose candidate list overflowed is answered by the single-query search
   for (int q = 0; q < num_queries; ++q) {
     if (host_ids[(size_t)q * k] != -2) continue;
@@ -697,9 +708,7 @@ int circuit_search_batch_device(circuit_index_t index, const float* dev_queries,
   int rc = index->search_batch_async(dev_queries, num_queries, k, dev_out_scores, dev_out_ids, st);
   if (rc != CIRCUIT_OK) return rc;
   int over = 0;
-  if (!cuda_ok(cudaMemcpyAsync(&over, index->bw.overflow, sizeof(int), cudaMemcpyDeviceToHost, st), "D2H overflow") ||
-      !cuda_ok(cudaStreamSynchronize(st), "batch sync"))
-    return CIRCUIT_ERR_CUDA;
+  if ((rc = index->batch_status(st, &over)) != CIRCUIT_OK) return rc;
   if (over == 0) return CIRCUIT_OK;
   // the first id of each row marks an overflowed query (-2): answer those rows
   // in place with the single-query search, on the same stream
@@ -717,6 +726,21 @@ int circuit_search_batch_device(circuit_index_t index, const float* dev_queries,
     if (rc != CIRCUIT_OK) return rc;
   }
   return cuda_ok(cudaStreamSynchronize(st), "fallback sync") ? CIRCUIT_OK : CIRCUIT_ERR_CUDA;
+}
+
+int circuit_selftest_batch_wait_timeout(circuit_index_t index, int* out_error_bits) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  if (!out_error_bits) { set_error("null out_error_bits"); return CIRCUIT_ERR_ARG; }
+  int rc = index->ensure_batch(1);
+  if (rc != CIRCUIT_OK) return rc;
+  cudaStream_t st = index->stream;
+  if (!cuda_ok(cudaSetDevice(index->device), "cudaSetDevice") ||
+      !cuda_ok(cb::launch_selftest_wait(index->bw.err, st), "selftest launch") ||
+      !cuda_ok(cudaMemcpyAsync(out_error_bits, index->bw.err, sizeof(int), cudaMemcpyDeviceToHost, st), "D2H bits") ||
+      !cuda_ok(cudaStreamSynchronize(st), "selftest sync"))
+    return CIRCUIT_ERR_CUDA;
+  index->last_stream = st;
+  return CIRCUIT_OK;
 }
 
 const char* circuit_last_error(void) { return cb::get_error(); }

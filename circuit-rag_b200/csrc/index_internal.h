@@ -82,5 +82,8 @@ struct circuit_index_opaque {
   int ensure_batch(int B);
   int search_batch_async(const float* dq, int B, int k, float* dscores, int* dids, cudaStream_t st,
                          cudaEvent_t ev_scan_begin = nullptr, cudaEvent_t ev_scan_end = nullptr);
+  // Synchronises `st` and reads the last batch's overflow count and device
+  // error bits: CIRCUIT_ERR_TIMEOUT when a bounded wait of that batch gave up.
+  int batch_status(cudaStream_t st, int* overflow);
   static float key_to_float(uint32_t k);
 };

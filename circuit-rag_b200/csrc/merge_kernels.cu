@@ -77,6 +77,11 @@ __global__ void k_selftest_wait(int* err) {
   }
 }
 
+cudaError_t launch_selftest_wait(int* err, cudaStream_t stream) {
+  k_selftest_wait<<<1, 32, 0, stream>>>(err);
+  return cudaGetLastError();
+}
+
 }  // namespace cb
 
 extern "C" {
@@ -113,14 +118,10 @@ int circuit_merge_topk_batch(const float* scores, const int* ids, int num_querie
   while (selN < k) selN <<= 1;
   const int n = world * k_in;
   const size_t smem = sizeof(unsigned long long) * (size_t)(n + selN) + sizeof(cb::SelectScratch) + 16;
-  static size_t configured = 0;
-  if (smem > 48 * 1024 && smem > configured) {
-    if (!cb::cuda_ok(
-            cudaFuncSetAttribute(cb::k_merge_topk_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-            "merge batch smem"))
-      return CIRCUIT_ERR_CUDA;
-    configured = smem;
-  }
+  static cb::SmemOptIn opt_in;
+  if (smem > 48 * 1024 &&
+      !cb::cuda_ok(opt_in.ensure(reinterpret_cast<const void*>(cb::k_merge_topk_batch), (int)smem), "merge batch smem"))
+    return CIRCUIT_ERR_CUDA;
   cb::k_merge_topk_batch<<<num_queries, cb::MERGE_THREADS, smem, (cudaStream_t)stream>>>(
       scores, ids, world, k_in, (size_t)num_queries * k_in, k, selN, out_scores, out_ids);
   return cb::cuda_ok(cudaGetLastError(), "merge_topk_batch launch") ? CIRCUIT_OK : CIRCUIT_ERR_CUDA;
@@ -139,13 +140,10 @@ int circuit_merge_topk(const float* scores, const int* ids, int n, int k, float*
   int selN = 1;
   while (selN < k) selN <<= 1;
   const size_t smem = sizeof(unsigned long long) * (size_t)(n + selN) + sizeof(cb::SelectScratch) + 16;
-  static size_t configured = 0;
-  if (smem > 48 * 1024 && smem > configured) {
-    if (!cb::cuda_ok(cudaFuncSetAttribute(cb::k_merge_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                     "merge smem"))
-      return CIRCUIT_ERR_CUDA;
-    configured = smem;
-  }
+  static cb::SmemOptIn opt_in;
+  if (smem > 48 * 1024 &&
+      !cb::cuda_ok(opt_in.ensure(reinterpret_cast<const void*>(cb::k_merge_topk), (int)smem), "merge smem"))
+    return CIRCUIT_ERR_CUDA;
   cb::k_merge_topk<<<1, cb::MERGE_THREADS, smem, (cudaStream_t)stream>>>(scores, ids, n, k, selN, out_scores, out_ids);
   return cb::cuda_ok(cudaGetLastError(), "merge_topk launch") ? CIRCUIT_OK : CIRCUIT_ERR_CUDA;
 }

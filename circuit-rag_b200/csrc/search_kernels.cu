@@ -911,12 +911,9 @@ static cudaError_t launch_scan_t(const ScanParams& P0, int grid, cudaStream_t st
   int st = (int)((SMEM_BUDGET - fixed) / sb);
   P.stages = st < 2 ? 2 : (st > MAX_STAGES ? MAX_STAGES : st);
   const ScanLayout L = scan_layout(ScanShape<VPL>::ROWS, P.row_bytes, P.stages, TopkShape<KCAP>::SORTN, KCAP);
-  static int configured_bytes = 0;  // per instantiation; the attribute is process-wide
-  if ((int)L.total > configured_bytes) {
-    cudaError_t e = cudaFuncSetAttribute(k_scan<VPL, KCAP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
-    if (e != cudaSuccess) return e;
-    configured_bytes = (int)L.total;
-  }
+  static SmemOptIn opt_in;  // per instantiation, per device
+  cudaError_t e = opt_in.ensure(reinterpret_cast<const void*>(k_scan<VPL, KCAP>), (int)L.total);
+  if (e != cudaSuccess) return e;
   k_scan<VPL, KCAP><<<grid, SCAN_THREADS, L.total, stream>>>(P);
   return cudaGetLastError();
 }
@@ -1017,13 +1014,8 @@ cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const
   cudaError_t e;
   const int chunk_rows = bounds_chunk_rows(ix.D, ix.rank);
   const BoundsLayout BL = bounds_layout(ix.D, ix.rank, chunk_rows);
-  static int bounds_configured = 0;
-  if ((int)BL.total > bounds_configured) {
-    if ((e = cudaFuncSetAttribute(k_bounds, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BL.total)) !=
-        cudaSuccess)
-      return e;
-    bounds_configured = (int)BL.total;
-  }
+  static SmemOptIn bounds_opt_in;
+  if ((e = bounds_opt_in.ensure(reinterpret_cast<const void*>(k_bounds), (int)BL.total)) != cudaSuccess) return e;
   int grid_b = (ix.R + BOUNDS_WARPS - 1) / BOUNDS_WARPS;
   if (grid_b > 2 * ws.scan_grid) grid_b = 2 * ws.scan_grid;
   k_bounds<<<grid_b, BOUNDS_WARPS * 32, BL.total, stream>>>(ix, q, ws.ctrl, ws.root_dots, ws.main_ranges, chunk_rows,

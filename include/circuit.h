@@ -11,8 +11,13 @@
  *   reference native/src/api.cpp:7-51                (NULL / -1 conventions)
  *
  * Differences a caller can observe (all deliberate):
- *   - k is not clamped to 32; any 1 <= k <= CIRCUIT_MAX_K (and k <= N) works.
- *     (reference clamps at gpu_index.cpp:243, :334)
+ *   - k is not clamped to 32; any 1 <= k <= CIRCUIT_MAX_K works (reference
+ *     clamps at gpu_index.cpp:243, :334).  When k exceeds the number of rows
+ *     N, every row is returned first (in score order) and the remaining
+ *     k - N slots hold score -INFINITY and id -1, so the output buffers are
+ *     always fully written (the reference's Python path instead shortens the
+ *     result to N, circuit_rag/search.py:51; the Python package here does the
+ *     same).  This holds for every single-query, batched and no-alloc call.
  *   - pruning is on: the hierarchical path seeds an on-device threshold and
  *     prunes with rigorously inflated bounds; the reference native path runs
  *     with threshold -1e9 (gpu_index.cpp:279) and never prunes.  Results are
@@ -117,6 +122,13 @@ int circuit_abi_version(void);
  * returns; *out_error_bits receives the bits (1 = a "full" wait timed out).
  * Blocking; the context stays usable.  No reference counterpart. */
 int circuit_selftest_wait_timeout(int device_id, int* out_error_bits);
+/* Diagnostic for the batched path's error reporting: runs the same
+ * never-satisfied bounded wait (2 s) with the handle's batch workspace as its
+ * error target, exactly as a k_batch_scan wait that gave up would leave it.
+ * Afterwards circuit_batch_overflow returns CIRCUIT_ERR_TIMEOUT; the next
+ * batched search clears the bits and runs normally.  Blocking.  No reference
+ * counterpart. */
+int circuit_selftest_batch_wait_timeout(circuit_index_t index, int* out_error_bits);
 
 /* Wrap index arrays that already live on `device_id` (borrowed: the caller keeps
  * them alive and unmodified until circuit_destroy_index).  Shapes as in the
@@ -197,7 +209,11 @@ int circuit_search_finish_async(circuit_index_t index, const float* dev_query, i
 int circuit_search_batch_async(circuit_index_t index, const float* dev_queries, int num_queries, int k,
                                float* dev_out_scores, int* dev_out_ids, void* stream, void* ev_scan_begin,
                                void* ev_scan_end);
-/* Queries of the last batch whose candidate list overflowed (synchronises its stream). */
+/* Queries of the last batch whose candidate list overflowed (synchronises its
+ * stream).  Returns CIRCUIT_ERR_TIMEOUT (with *out_count still written) when a
+ * bounded device-side wait of that batch gave up, i.e. its results are
+ * incomplete; every batch starts with the error bits cleared.  The blocking
+ * calls below return the same code for such a batch. */
 int circuit_batch_overflow(circuit_index_t index, int* out_count);
 /* Blocking host-buffer variant of circuit_search_batch_async (host_scores / host_ids [num_queries, k]). */
 int circuit_search_batch(circuit_index_t index, const float* host_queries, int num_queries, int k, float* host_scores,

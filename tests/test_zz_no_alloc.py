@@ -83,3 +83,31 @@ def test_noalloc_rejects_sizes_beyond_its_limit():
     assert "128" in _native.last_error()
     assert L.circuit_flat_search_noalloc(X.data_ptr(), 64, 30, q.data_ptr(), 5, s.data_ptr(), i.data_ptr(),
                                          None) != 0
+
+
+@pytest.mark.parametrize("n,k", [(1, 10), (5, 10), (100, 10), (148, 128), (3000, 128)])
+def test_noalloc_small_corpora_match_existing_entry_point(n, k):
+    """Fewer rows than k (the slots past n hold -inf / -1, as for every entry
+    point) and fewer rows than SMs: two calls in a row, each equal to the
+    existing entry point's result and to the oracle."""
+    L = _native.lib()
+    w = WORKLOADS["spread-5k"]
+    X = w.corpus(0, n, device=DEV)
+    Q = w.query_batch(2, device=DEV)
+    idx = _one_child_index(X)
+    h = idx.native_handle()
+    stream = torch.cuda.current_stream()
+    for q in Q:
+        s_new, i_new = _noalloc(L, X, q, k, stream)
+        s_ref = torch.empty(k, device=DEV)
+        i_ref = torch.empty(k, dtype=torch.int32, device=DEV)
+        assert L.circuit_search_async(h, q.data_ptr(), k, 1 << 62, s_ref.data_ptr(), i_ref.data_ptr(), None,
+                                      stream.cuda_stream, None, None) == 0, _native.last_error()
+        torch.cuda.synchronize()
+        m = min(n, k)
+        exact = (X.double() @ q.double()).cpu().numpy()
+        oracle.check_topk(exact, m, s_new[:m].cpu().numpy(), i_new[:m].cpu().numpy())
+        assert torch.equal(s_new, s_ref) and torch.equal(i_new, i_ref)
+        if n < k:
+            assert torch.all(torch.isneginf(s_new[n:])) and torch.all(i_new[n:] == -1)
+    idx.close()
