@@ -71,6 +71,7 @@ class TraceEx(ctypes.Structure):
         ("best_root", ctypes.c_int32),
         ("seed_threshold", ctypes.c_float),
         ("device_error", ctypes.c_int32),
+        ("seed_sample_rows", ctypes.c_int32),
     ]
 
 

@@ -129,6 +129,10 @@ __device__ __forceinline__ void tma_load_1d_stream(void* dst_smem, const void* s
 __device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
+// Brings the 128-byte line holding p into L2 (no completion to wait for).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -140,6 +144,16 @@ __device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
 __device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
   return *reinterpret_cast<const volatile unsigned long long*>(p);
 }
+
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialisation may start while the kernel before it on the stream is still
+// running; griddep_wait() blocks until that kernel has completed and its
+// memory is visible, so everything before it must only read data that existed
+// before that kernel was launched.  griddep_launch() lets the next kernel of
+// the stream start early (it still waits for this one's completion before it
+// reads any result).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---------------------------------------------------------------- warp helpers
 __device__ __forceinline__ float warp_sum(float v) {

@@ -46,12 +46,11 @@ constexpr int SCAN_THREADS = (SCAN_CONSUMER_WARPS + 1) * 32;  // + one TMA produ
 constexpr int BOUNDS_WARPS = 4;
 constexpr int ROOT_SCAN_WARPS = 8;
 
-// Per-query control block.  The first CTRL_RESET_BYTES are zeroed by one
-// cudaMemsetAsync at the start of every search; seed_list is always fully
-// rewritten by the seed merge before it is read.
+// Per-query control block, zeroed at the start of every search (by the search
+// prologue kernel, or by the caller of launch_flat_scan).
 struct SearchCtrl {
   unsigned long long best_packed;  // argmax root: prio<<62 | key<<30 | (2^30-1-root)
-  unsigned long long seed_packed;  // seed range list: n_ranges<<32 | n_rows
+  unsigned long long seed_packed;  // rows scored by the seed sample
   unsigned long long main_packed;  // main range list: n_ranges<<32 | n_rows (atomicAdd)
   uint32_t k1_done;                // last-CTA tickets
   uint32_t seed_done;
@@ -64,10 +63,9 @@ struct SearchCtrl {
   int best_root;
   int error;                       // cb::ERR_* bits
   uint32_t pad[8];
-  unsigned long long seed_list[KMAX];
 };
 constexpr size_t CTRL_RESET_BYTES = 96;
-static_assert(offsetof(SearchCtrl, seed_list) == CTRL_RESET_BYTES, "ctrl layout");
+static_assert(sizeof(SearchCtrl) == CTRL_RESET_BYTES, "ctrl layout");
 
 // Read-only device view of one index (all pointers are device pointers).
 struct IndexView {
@@ -85,6 +83,7 @@ struct IndexView {
   // derived once per index by prepare()
   const int* root_child_ptr;    // [R+1]  CSR over non-empty children, grouped by parent
   const int* root_child_list;   // [nnz children]
+  const int2* root_child_span;  // [nnz] per CSR entry: {leaf offset, first row within its root's rows}
   const int* root_rows;         // [R]  leaf rows under each root
   const double* root_cn;        // [R]  upper bound of ||c_r||
   const double* root_defect;    // [R]  upper bound of ||V_r^T V_r - I||_2
@@ -94,11 +93,11 @@ struct IndexView {
 // Device workspace owned by one index handle (one in-flight search at a time).
 struct Workspace {
   SearchCtrl* ctrl;
-  int4* seed_ranges;                 // [max children of a root]
   int4* main_ranges;                 // [C]
   int4* flat_range;                  // [1] = {0, 0, N, -1}
   unsigned long long* flat_packed;   // [1] = 1<<32 | N
-  float* root_dots;                  // [R]
+  float* ub_root;                    // [R] rigorous root bounds (rounded up to float)
+  float* ub_child;                   // [C] rigorous child bounds
   unsigned long long* cta_lists;     // [scan_grid * KMAX]
   int scan_grid;
 };
@@ -121,17 +120,18 @@ struct HostIO {
 // ---- launchers (search_kernels.cu); all asynchronous on `stream` ----
 cudaError_t launch_prepare_roots(const IndexView& ix, double* root_cn, double* root_defect, cudaStream_t stream);
 
-// One single-query search.  hierarchical != 0 runs root scan -> seed scan ->
-// bounds -> main scan; otherwise one flat scan over all rows.  Outputs k
+// One single-query search.  hierarchical != 0 runs prologue -> root scan (with
+// the seed sample) -> bounds -> main scan; otherwise prologue -> one flat scan
+// over all rows.  Outputs k
 // results sorted by (score desc, row asc).  ev_scan0/1 (may be null) are
 // recorded around the main (dominant) scan kernel.
 cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float* q, int k, int hierarchical,
                           float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
                           cudaEvent_t ev_scan0, cudaEvent_t ev_scan1, const HostIO* io = nullptr);
 // The hierarchical search in two phases, so that shards can exchange their seed
-// thresholds in between: seed = reset + root scan + seed scan (writes the seed
-// k-th best score to T_export, -inf if the seed root has fewer than k rows);
-// finish = bounds + main scan with threshold max(own seed, *T_ext).
+// thresholds in between: seed = reset + root scan with the seed sample (writes
+// the k-th best sampled score to T_export, -inf if fewer than k rows were
+// sampled); finish = bounds + main scan with threshold max(own seed, *T_ext).
 cudaError_t launch_search_seed(const IndexView& ix, const Workspace& ws, const float* q, int k, float* T_export,
                                cudaStream_t stream, const HostIO* io = nullptr);
 cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const float* q, int k, const float* T_ext,

@@ -133,17 +133,30 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
   int* d_ptr = (int*)dev_alloc(sizeof(int) * ptr.size(), "cudaMalloc(root_child_ptr)");
   int* d_list = (int*)dev_alloc(sizeof(int) * std::max<size_t>(list.size(), 1), "cudaMalloc(root_child_list)");
   int* d_rows = (int*)dev_alloc(sizeof(int) * rows.size(), "cudaMalloc(root_rows)");
+  // per CSR entry: the child's leaf offset and where its rows start among its root's rows
+  std::vector<int2> span(std::max<size_t>(list.size(), 1), make_int2(0, 0));
+  for (int p = 0; p < R; ++p) {
+    int v = 0;
+    for (int i = ptr[p]; i < ptr[p + 1]; ++i) {
+      span[i] = make_int2(offsets[list[i]], v);
+      v += sizes[list[i]];
+    }
+  }
+  int2* d_span = (int2*)dev_alloc(sizeof(int2) * span.size(), "cudaMalloc(root_child_span)");
   double* d_cn = (double*)dev_alloc(sizeof(double) * R, "cudaMalloc(root_cn)");
   double* d_def = (double*)dev_alloc(sizeof(double) * R, "cudaMalloc(root_defect)");
-  if (!d_ptr || !d_list || !d_rows || !d_cn || !d_def) return false;
+  if (!d_ptr || !d_list || !d_rows || !d_cn || !d_def || !d_span) return false;
   if (!cuda_ok(cudaMemcpyAsync(d_ptr, ptr.data(), sizeof(int) * ptr.size(), cudaMemcpyHostToDevice, stream), "H2D ptr") ||
       (!list.empty() && !cuda_ok(cudaMemcpyAsync(d_list, list.data(), sizeof(int) * list.size(),
                                                  cudaMemcpyHostToDevice, stream),
                                  "H2D list")) ||
-      !cuda_ok(cudaMemcpyAsync(d_rows, rows.data(), sizeof(int) * rows.size(), cudaMemcpyHostToDevice, stream), "H2D rows"))
+      !cuda_ok(cudaMemcpyAsync(d_rows, rows.data(), sizeof(int) * rows.size(), cudaMemcpyHostToDevice, stream), "H2D rows") ||
+      !cuda_ok(cudaMemcpyAsync(d_span, span.data(), sizeof(int2) * span.size(), cudaMemcpyHostToDevice, stream),
+               "H2D spans"))
     return false;
   view.root_child_ptr = d_ptr;
   view.root_child_list = d_list;
+  view.root_child_span = d_span;
   view.root_rows = d_rows;
   view.root_cn = d_cn;
   view.root_defect = d_def;
@@ -152,18 +165,18 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
   // workspace
   ws.scan_grid = cb::sm_count(device);
   ws.ctrl = (cb::SearchCtrl*)dev_alloc(sizeof(cb::SearchCtrl), "cudaMalloc(ctrl)");
-  ws.seed_ranges = (int4*)dev_alloc(sizeof(int4) * std::max(max_children, 1), "cudaMalloc(seed_ranges)");
   ws.main_ranges = (int4*)dev_alloc(sizeof(int4) * std::max(C, 1), "cudaMalloc(main_ranges)");
   ws.flat_range = (int4*)dev_alloc(sizeof(int4), "cudaMalloc(flat_range)");
   ws.flat_packed = (unsigned long long*)dev_alloc(sizeof(unsigned long long), "cudaMalloc(flat_packed)");
-  ws.root_dots = (float*)dev_alloc(sizeof(float) * R, "cudaMalloc(root_dots)");
+  ws.ub_root = (float*)dev_alloc(sizeof(float) * R, "cudaMalloc(ub_root)");
+  ws.ub_child = (float*)dev_alloc(sizeof(float) * C, "cudaMalloc(ub_child)");
   ws.cta_lists = (unsigned long long*)dev_alloc(sizeof(unsigned long long) * (size_t)(ws.scan_grid + 1) * cb::KMAX,
                                                 "cudaMalloc(cta_lists)");
   dev_query = (float*)dev_alloc(sizeof(float) * D, "cudaMalloc(query)");
   dev_scores = (float*)dev_alloc(sizeof(float) * cb::KMAX, "cudaMalloc(scores)");
   dev_ids = (int*)dev_alloc(sizeof(int) * cb::KMAX, "cudaMalloc(ids)");
   dev_out_indirect = (void**)dev_alloc(2 * sizeof(void*), "cudaMalloc(out pointers)");
-  if (!ws.ctrl || !ws.seed_ranges || !ws.main_ranges || !ws.flat_range || !ws.flat_packed || !ws.root_dots ||
+  if (!ws.ctrl || !ws.main_ranges || !ws.flat_range || !ws.flat_packed || !ws.ub_root || !ws.ub_child ||
       !ws.cta_lists || !dev_query || !dev_scores || !dev_ids || !dev_out_indirect)
     return false;
   const int4 fr = make_int4(0, 0, N, -1);
@@ -416,11 +429,12 @@ void circuit_index_opaque::fill_trace(const cb::SearchCtrl& c, circuit_trace_ex_
   t->total_children = C;
   t->device_error = c.error;
   if (last_path) {
-    t->vectors_scored = (int64_t)(uint32_t)c.seed_packed + (int64_t)(uint32_t)c.main_packed;
+    t->vectors_scored = (int64_t)(uint32_t)c.main_packed;
     t->surviving_roots = (int32_t)c.n_surv_roots;
     t->surviving_children = (int32_t)c.n_surv_children;
     t->best_root = c.best_root;
     t->seed_threshold = c.seed_T_key ? key_to_float(c.seed_T_key) : -std::numeric_limits<float>::infinity();
+    t->seed_sample_rows = (int32_t)(uint32_t)c.seed_packed;
   } else {
     t->vectors_scored = N;
     t->surviving_roots = R;

@@ -4,12 +4,12 @@
 //   memset(ctrl header)   (graph-replayed blocking calls: k_search_prologue,
 //                          which also stages the query)
 //   k_root_scan   warp per root: q.c_r for every root, ||q||^2, argmax root
-//                 (the seed root); its last CTA writes the seed root's leaf
-//                 ranges.                       (reference: search.py:26-41,
+//                 (the seed root); its last CTA scores an evenly spaced
+//                 sample of the seed root's rows (bulk copies into shared
+//                 memory, the leaf scan's exact arithmetic) and publishes
+//                 T = k-th best sampled score on the device.
+//                                               (reference: search.py:26-41,
 //                                                 root_bounds.cu:31-54)
-//   k_scan<seed>  streams the seed root's leaves, fused top-k; its last CTA
-//                 merges the per-CTA lists into the seed list and publishes
-//                 T = k-th best seed score on the device.
 //   k_bounds      warp per root: rigorous root bound, rank-r projection of q
 //                 (basis staged in shared memory by TMA), rigorous child box
 //                 bounds, compaction of surviving children into leaf ranges.
@@ -18,13 +18,14 @@
 //   k_scan<final> streams the surviving leaves (TMA bulk copies into a
 //                 3..8-stage shared-memory ring, one producer warp, eight
 //                 consumer warps), fused top-k; its last CTA merges all lists
-//                 plus the seed list and writes scores / original ids.
+//                 and writes scores / original ids.
 //                                               (reference: dense_score.cu:116-164,
 //                                                 topk.cu:56-170, search.py:77-84)
 // The flat path (small corpora) is the final scan over one range [0, N).
 #include <cmath>
 #include <cstdio>
 #include <type_traits>
+#include <utility>
 
 #include "common.cuh"
 #include "engine.h"
@@ -56,11 +57,6 @@ struct ScanParams {
   int k;
   int stages;
   int min_rows;                               // rows per CTA below which fewer CTAs take part
-  int final_mode;                             // 0: seed merge, 1: final merge
-  int merge_seed;                             // final: also merge ctrl seed list
-  unsigned long long* seed_list;              // [k]
-  uint32_t* seed_T_key;
-  float* T_export;                            // seed mode: the seed threshold as a float (optional)
   float* out_scores;
   int* out_ids;
   long long* out_rows;
@@ -130,7 +126,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
   __shared__ int s_is_last, s_err;
   __shared__ unsigned long long s_pc;
   __shared__ int4 s_rg0;
-  __shared__ uint32_t s_theta, s_rank_count;
+  __shared__ uint32_t s_theta, s_rank_count, s_fin_count;
   __shared__ uint32_t s_warp_theta[SCAN_CONSUMER_WARPS];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -138,8 +134,13 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
   const int k = P.k;
 
   for (int i = tid; i < SCAN_CONSUMER_WARPS * SORTN; i += blockDim.x) topk_all[i] = 0ull;
+  // launched as a programmatic dependent of the kernel that writes its ranges
+  // (bounds) or clears its control words (search prologue): everything above
+  // overlaps that kernel, everything below reads its results
+  griddep_wait();
   if (tid == 0) {
     s_err = 0;
+    s_fin_count = 0;
     s_pc = ld_volatile_u64(P.packed_counts);
     s_rg0 = __ldcg(P.ranges);  // entry 0 exists whenever ranges do; read beside the count
     for (int s = 0; s < STAGES; ++s) {
@@ -181,55 +182,92 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       }
       s = lo;
     }
-    if (lane == 0) {
-      const uint64_t policy = policy_evict_first();
-      const void* theta_line = reinterpret_cast<const void*>((uintptr_t)P.theta_key & ~(uintptr_t)15);
-      uint32_t v = vb;
-      int it = 0;
-      bool ok = true;
-      const char* leaf_bytes = reinterpret_cast<const char*>(P.leaf);
-      // the next range entry is loaded one transition ahead, so walking from
-      // one child's rows to the next never waits on L2
-      int4 rg_next = (s + 1 < (int)n_ranges && vb < ve) ? __ldcg(&P.ranges[s + 1]) : make_int4(0, 0, 0, 0);
-      while (v < ve) {
-        const int stage = it % STAGES, f = it / STAGES;
-        if (f > 0 && !mbar_wait(&empty[stage], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) {
-          ok = false;
-          s_err = 1;
-          break;
-        }
-        int2* runs = stage_runs + stage * 32;
-        int n = 0, nr = 0;
-        uint32_t run_end = 0xffffffffu;  // leaf row just past the open run
-        while (n < ROWS && v < ve) {
-          const uint32_t rlen = (uint32_t)(rg.z - rg.y);
-          if (v >= (uint32_t)rg.x + rlen) {
-            ++s;
-            if (s >= (int)n_ranges) { atomicOr(P.err, ERR_BAD_RANGE); v = ve; break; }
-            rg = rg_next;
-            if (s + 1 < (int)n_ranges) rg_next = __ldcg(&P.ranges[s + 1]);
-            continue;
+    // The whole warp walks the ranges: lane j holds entry base + j of the
+    // current 32-entry window and of the next one (loaded a window ahead), so
+    // moving from one child's rows to the next is a register shuffle; an L2
+    // round trip happens once per 32 ranges and overlaps the stages in flight.
+    // Short children (a few rows each) no longer stall the stream.  Lane j
+    // records and issues the stage's run j, so up to 32 bulk copies per stage
+    // go out in parallel.
+    const uint64_t policy = policy_evict_first();
+    const void* theta_line = reinterpret_cast<const void*>((uintptr_t)P.theta_key & ~(uintptr_t)15);
+    const char* leaf_bytes = reinterpret_cast<const char*>(P.leaf);
+    uint32_t v = vb;
+    int it = 0;
+    bool ok = true;
+    int base = s & ~31;
+    const auto load_window = [&](int b) {
+      const int idx = b + lane;
+      return (vb < ve && idx < (int)n_ranges) ? __ldcg(&P.ranges[idx]) : make_int4(0, 0, 0, 0);
+    };
+    int4 win = load_window(base), win_next = load_window(base + 32);
+    while (v < ve) {
+      const int stage = it % STAGES, f = it / STAGES;
+      bool free_stage = true;
+      if (lane == 0 && f > 0) free_stage = mbar_wait(&empty[stage], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY);
+      if (!__shfl_sync(FULL_MASK, free_stage, 0)) {
+        ok = false;
+        if (lane == 0) s_err = 1;
+        break;
+      }
+      int n = 0, nr = 0;
+      uint32_t run_end = 0xffffffffu;  // leaf row just past the open run
+      int my_slot = 0, my_row = 0;     // this lane's run (lane < nr)
+      while (n < ROWS && v < ve) {
+        const uint32_t rlen = (uint32_t)(rg.z - rg.y);
+        if (v >= (uint32_t)rg.x + rlen) {
+          ++s;
+          if (s >= (int)n_ranges) {
+            if (lane == 0) atomicOr(P.err, ERR_BAD_RANGE);
+            v = ve;
+            break;
           }
-          const uint32_t row = (uint32_t)rg.y + (v - (uint32_t)rg.x);
-          const uint32_t take = min(min((uint32_t)(ROWS - n), ve - v), (uint32_t)rg.z - row);
-          if (row != run_end) runs[nr++] = make_int2(n, (int)row);  // adjacent children extend the open run
-          run_end = row + take;
-          n += (int)take;
-          v += take;
+          if (s - base == 32) {
+            base += 32;
+            win = win_next;
+            win_next = load_window(base + 32);
+          }
+          rg.x = __shfl_sync(FULL_MASK, win.x, s - base);
+          rg.y = __shfl_sync(FULL_MASK, win.y, s - base);
+          rg.z = __shfl_sync(FULL_MASK, win.z, s - base);
+          rg.w = __shfl_sync(FULL_MASK, win.w, s - base);
+          continue;
         }
+        const uint32_t row = (uint32_t)rg.y + (v - (uint32_t)rg.x);
+        const uint32_t take = min(min((uint32_t)(ROWS - n), ve - v), (uint32_t)rg.z - row);
+        if (row != run_end) {  // adjacent children extend the open run
+          if (lane == nr) {
+            my_slot = n;
+            my_row = (int)row;
+          }
+          ++nr;
+        }
+        run_end = row + take;
+        n += (int)take;
+        v += take;
+      }
+      // run j covers slots [start_j, start_{j+1}) (the last one up to n)
+      const int next_slot = __shfl_down_sync(FULL_MASK, my_slot, 1);
+      const int slot_end = (lane + 1 < nr) ? next_slot : n;
+      if (lane < nr) stage_runs[stage * 32 + lane] = make_int2(my_slot, my_row);
+      if (lane == 0) {
         stage_n[stage] = n;
         stage_nr[stage] = nr;
+      }
+      __syncwarp();  // the stage's run table is written before lane 0's arrive releases it
+      if (lane == 0) {
         mbar_arrive_expect_tx(&full[stage], (uint32_t)n * (uint32_t)P.row_bytes + 16u);
         tma_load_1d(smem + L.side_off + (size_t)stage * 16, theta_line, 16u, &full[stage]);
-        unsigned char* dst = smem + L.stages_off + (size_t)stage * L.stage_bytes;
-        for (int i = 0; i < nr; ++i) {
-          const int2 r0 = runs[i];
-          const int slot_end = (i + 1 < nr) ? runs[i + 1].x : n;
-          tma_load_1d_stream(dst + (size_t)r0.x * P.row_bytes, leaf_bytes + (size_t)r0.y * P.row_bytes,
-                             (uint32_t)(slot_end - r0.x) * (uint32_t)P.row_bytes, &full[stage], policy);
-        }
-        ++it;
       }
+      __syncwarp();
+      if (lane < nr) {
+        unsigned char* dst = smem + L.stages_off + (size_t)stage * L.stage_bytes;
+        tma_load_1d_stream(dst + (size_t)my_slot * P.row_bytes, leaf_bytes + (size_t)my_row * P.row_bytes,
+                           (uint32_t)(slot_end - my_slot) * (uint32_t)P.row_bytes, &full[stage], policy);
+      }
+      ++it;
+    }
+    if (lane == 0) {
       const int stage = it % STAGES, f = it / STAGES;
       if (ok && f > 0 && !mbar_wait(&empty[stage], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) s_err = 1;
       stage_n[stage] = -1;
@@ -448,73 +486,86 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
   __threadfence();
 
   // ---------------------------------------------------------- grid merge (last CTA)
-  // The ring is idle now: stage the gathered lists in its shared memory when
-  // they fit (with room for the rank select's survivors), so the selects run on
-  // shared memory instead of L2.
-  const int mg = (int)G * k;  // gathered lists
-  const int M = mg + ((P.final_mode && P.merge_seed) ? k : 0);
-  int cnt_sel;
-  if ((size_t)(M + RANK_CAP) * 8 <= (size_t)STAGES * L.stage_bytes) {
-    unsigned long long* buf = ring;
-    // the threshold is re-read beside the gather (every CTA published before
-    // its ticket), so the rank pass usually sees little more than k survivors
-    const uint32_t th = tid == 0 ? ld_volatile_u32(P.theta_key) : 0u;
-#pragma unroll 8
-    for (int i = tid; i < mg; i += blockDim.x) buf[i] = __ldcg(P.cta_lists + i);
-    for (int i = mg + tid; i < M; i += blockDim.x) buf[i] = P.seed_list[i - mg];
-    if (tid == 0) s_theta = max(s_theta, th);
-    __syncthreads();
-    cnt_sel = block_rank_topk<RANK_CAP>(buf, M, k, sel, selN, buf + M, &s_rank_count, s_theta);
-    if (cnt_sel < 0) cnt_sel = block_select_topk<false>(buf, M, k, sel, selN, scratch, s_theta);
-  } else {
-    if (P.final_mode && P.merge_seed) {
-      for (int i = tid; i < k; i += blockDim.x) P.cta_lists[(size_t)mg + i] = P.seed_list[i];
-      __threadfence_block();
-      __syncthreads();
-    }
-    cnt_sel = block_select_topk<true>(P.cta_lists, M, k, sel, selN, scratch, s_theta);
+  // Every CTA published its k-th best before its ticket, so the global
+  // threshold is final here; the last CTA's threads load the G lists (eight
+  // entries in flight per thread), keep what is not below it -- usually little
+  // more than k entries -- rank those directly and write each result to its
+  // slot: one block barrier between the loads and the outputs.
+  // The control header is final too (every CTA updated it before its ticket).
+  if (P.ctrl_out)
+    for (int i = tid; i < (int)(CTRL_RESET_BYTES / 8); i += blockDim.x) P.ctrl_out[i] = __ldcg(P.ctrl_hdr + i);
+  float* out_scores = P.out_scores;
+  int* out_ids = P.out_ids;
+  if (P.out_indirect) {
+    const unsigned long long* ptrs = reinterpret_cast<const unsigned long long*>(P.out_indirect);
+    out_scores = reinterpret_cast<float*>(__ldcg(ptrs));
+    out_ids = reinterpret_cast<int*>(__ldcg(ptrs + 1));
   }
-  if (!P.final_mode) {
-    for (int i = tid; i < k; i += blockDim.x) P.seed_list[i] = sel[i];
-    if (tid == 0) {
-      const uint32_t T = (cnt_sel == k) ? cand_key(sel[k - 1]) : 0u;
-      *P.seed_T_key = T;
-      if (T > *P.theta_key) *P.theta_key = T;
-      if (P.T_export) *P.T_export = T ? key2f(T) : -INFINITY;
+  const auto emit = [&](int r, unsigned long long c) {
+    if (c != 0ull) {
+      const uint32_t row = cand_row(c);
+      out_scores[r] = key2f(cand_key(c));
+      if (out_ids) out_ids[r] = P.original_ids ? P.original_ids[row] : (int)row;
+      if (P.out_rows) P.out_rows[r] = (long long)row;
+    } else {
+      out_scores[r] = -INFINITY;
+      if (out_ids) out_ids[r] = -1;
+      if (P.out_rows) P.out_rows[r] = -1;
     }
-  } else {
-    float* out_scores = P.out_scores;
-    int* out_ids = P.out_ids;
-    if (P.out_indirect) {
-      const unsigned long long* ptrs = reinterpret_cast<const unsigned long long*>(P.out_indirect);
-      out_scores = reinterpret_cast<float*>(__ldcg(ptrs));
-      out_ids = reinterpret_cast<int*>(__ldcg(ptrs + 1));
+  };
+  const int M = (int)G * k;  // gathered lists
+  uint32_t th = 0u;
+  if (lane == 0) th = ld_volatile_u32(P.theta_key);
+  th = max(__shfl_sync(FULL_MASK, th, 0), s_theta);  // per warp; any of these bounds is valid
+  unsigned long long* tmp = ring;                       // idle now; holds RANK_CAP entries
+  for (int b0 = 0; b0 < M; b0 += 8 * SCAN_THREADS) {
+    unsigned long long v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = b0 + u * SCAN_THREADS + warp * 32 + lane;
+      v[u] = i < M ? __ldcg(P.cta_lists + i) : 0ull;
     }
-    for (int i = tid; i < k; i += blockDim.x) {
-      const unsigned long long c = sel[i];
-      if (c != 0ull) {
-        const uint32_t row = cand_row(c);
-        out_scores[i] = key2f(cand_key(c));
-        if (out_ids) out_ids[i] = P.original_ids ? P.original_ids[row] : (int)row;
-        if (P.out_rows) P.out_rows[i] = (long long)row;
-      } else {
-        out_scores[i] = -INFINITY;
-        if (out_ids) out_ids[i] = -1;
-        if (P.out_rows) P.out_rows[i] = -1;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const bool pass = v[u] != 0ull && cand_key(v[u]) >= th;
+      const uint32_t bal = __ballot_sync(FULL_MASK, pass);
+      uint32_t pos = 0;
+      if (lane == 0 && bal) pos = atomicAdd(&s_fin_count, (uint32_t)__popc(bal));
+      pos = __shfl_sync(FULL_MASK, pos, 0) + __popc(bal & lanemask_lt());
+      if (pass && pos < (uint32_t)RANK_CAP) tmp[pos] = v[u];
+    }
+  }
+  __syncthreads();
+  const int n = (int)s_fin_count;
+  if (n <= RANK_CAP) {
+    // rank = number of larger kept entries (entries are unique); for every
+    // entry of the true top-k all larger entries were kept, whatever bound
+    // each warp used, so these ranks are the global ranks
+    for (int t = tid; t < n; t += blockDim.x) {
+      const unsigned long long c = tmp[t];
+      int r = 0, j = 0;
+      for (; j + 8 <= n; j += 8) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) r += tmp[j + u] > c;
       }
+      for (; j < n; ++j) r += tmp[j] > c;
+      if (r < k) emit(r, c);
     }
-    // every other CTA's updates of the header precede its ticket
-    if (P.ctrl_out)
-      for (int i = tid; i < (int)(CTRL_RESET_BYTES / 8); i += blockDim.x) P.ctrl_out[i] = __ldcg(P.ctrl_hdr + i);
+    for (int r = n + tid; r < k; r += blockDim.x) emit(r, 0ull);
+  } else {
+    block_select_topk<true>(P.cta_lists, M, k, sel, selN, scratch, s_theta);
+    for (int i = tid; i < k; i += blockDim.x) emit(i, sel[i]);
   }
 }
 
 // ============================================================ search prologue
-// First kernel of a graph-replayed blocking search: stages the query and
-// clears the control header (replaces a host-to-device copy and a memset, two
-// copy-engine operations of a few microseconds each at this size).  The query
-// comes from mapped pinned memory (q_host) or from the device pointer slots[0];
-// slots[1..2] (the caller's device outputs) are staged for the final merge.
+// First kernel of every search: clears the control header and, in a
+// graph-replayed blocking search, stages the query (replacing a host-to-device
+// copy and a memset, two copy-engine operations of a few microseconds each at
+// this size).  The query comes from mapped pinned memory (q_host) or from the
+// device pointer slots[0]; slots[1..2] (the caller's device outputs) are staged
+// for the final merge; with neither, only the header is cleared.  The kernels
+// after it are its programmatic dependents.
 __global__ void __launch_bounds__(128) k_search_prologue(const float4* q_host, void* const* slots, float4* dq, int D4,
                                                          unsigned long long* ctrl_hdr, void** out_indirect) {
   const int tid = threadIdx.x;
@@ -523,21 +574,55 @@ __global__ void __launch_bounds__(128) k_search_prologue(const float4* q_host, v
     src = static_cast<const float4*>(slots[0]);
     if (tid < 2) out_indirect[tid] = slots[tid + 1];
   }
-  for (int i = tid; i < D4; i += blockDim.x) dq[i] = src[i];
+  if (src)
+    for (int i = tid; i < D4; i += blockDim.x) dq[i] = src[i];
   if (tid < (int)(CTRL_RESET_BYTES / 8)) ctrl_hdr[tid] = 0ull;
 }
 
 // ============================================================ root scan (K1)
+// Seed threshold (reference search.py:26-41 takes the k-th best score of every
+// row of the best root, after four host syncs): the last CTA of the root scan
+// scores a sample of up to min(rows of the seed root, max(4k, 128), 1024) of
+// its rows -- blocks of up to 16 consecutive rows (one bulk copy each) starting
+// at evenly spaced positions -- and keeps T = the k-th best sampled score.
+// Any k distinct rows give a valid threshold (T never exceeds the global k-th
+// best), and the sampled scores use the leaf scan's exact arithmetic (per lane
+// FMAs over float4 columns lane, lane + 32, ...; then one xor butterfly), so T
+// equals the main scan's own score of a real row.  The seed root's rows are
+// scanned by the main scan like any surviving root's.
+constexpr int SEED_SAMPLE_MAX = 1024;
+constexpr int SEED_BLOCK = 16;  // consecutive rows per bulk copy of the sample
+constexpr int SEED_RING_BYTES = 192 * 1024;
+
+struct RootScanLayout {
+  int ring_rows;
+  size_t keys_off, rows_off, sel_off, scratch_off, q_off, bar_off, total;
+};
+__host__ __device__ inline RootScanLayout root_scan_layout(int row_bytes) {
+  RootScanLayout L;
+  L.ring_rows = SEED_RING_BYTES / row_bytes < 128 ? SEED_RING_BYTES / row_bytes : 128;
+  L.keys_off = align_up((size_t)L.ring_rows * row_bytes, 128);
+  L.rows_off = L.keys_off + (size_t)SEED_SAMPLE_MAX * 8;
+  L.sel_off = align_up(L.rows_off + (size_t)(SEED_SAMPLE_MAX / SEED_BLOCK) * 3 * 4, 16);
+  L.scratch_off = L.sel_off + (size_t)KMAX * 8;
+  L.q_off = align_up(L.scratch_off + sizeof(SelectScratch), 16);
+  L.bar_off = L.q_off + (size_t)MAX_DIM * 4;
+  L.total = L.bar_off + 16;
+  return L;
+}
+
 __global__ void __launch_bounds__(ROOT_SCAN_WARPS * 32) k_root_scan(IndexView ix, const float* __restrict__ q,
-                                                                     SearchCtrl* ctrl, float* __restrict__ root_dots,
-                                                                     int4* __restrict__ seed_ranges, int k) {
+                                                                     SearchCtrl* ctrl, int k,
+                                                                     float* __restrict__ T_export) {
+  extern __shared__ __align__(128) unsigned char smem[];
   __shared__ unsigned long long s_best[ROOT_SCAN_WARPS];
-  __shared__ int s_last;
+  __shared__ int s_last, s_nsample, s_ok, s_nblk;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int p = blockIdx.x * ROOT_SCAN_WARPS + warp;
+  griddep_wait();    // the control header is cleared (and the query staged) by the kernel before
+  griddep_launch();  // the bounds kernel's threshold-free phase runs beside this one
   const float4* q4 = reinterpret_cast<const float4*>(q);
   unsigned long long packed = 0ull;
-  if (p < ix.R) {
+  for (int p = blockIdx.x * ROOT_SCAN_WARPS + warp; p < ix.R; p += gridDim.x * ROOT_SCAN_WARPS) {
     const float4* c4 = reinterpret_cast<const float4*>(ix.root_centers + (size_t)p * ix.D);
     float acc = 0.f;
     for (int c = lane; c < ix.D4; c += 32) {
@@ -548,10 +633,11 @@ __global__ void __launch_bounds__(ROOT_SCAN_WARPS * 32) k_root_scan(IndexView ix
       acc = fmaf(a.w, b.w, acc);
     }
     const float dot = warp_sum(acc);
-    if (lane == 0) root_dots[p] = dot;
     const int rows = ix.root_rows[p];
     const unsigned long long prio = rows >= k ? 2ull : (rows > 0 ? 1ull : 0ull);
-    packed = (prio << 62) | ((unsigned long long)f2key(dot) << 30) | (unsigned long long)(0x3fffffff - p);
+    const unsigned long long pk =
+        (prio << 62) | ((unsigned long long)f2key(dot) << 30) | (unsigned long long)(0x3fffffff - p);
+    packed = pk > packed ? pk : packed;
   }
   if (blockIdx.x == 0 && warp == 0) {
     float acc = 0.f;
@@ -576,30 +662,164 @@ __global__ void __launch_bounds__(ROOT_SCAN_WARPS * 32) k_root_scan(IndexView ix
     s_last = (t == gridDim.x - 1);
   }
   __syncthreads();
-  if (!s_last || warp != 0) return;
+  if (!s_last) return;
   __threadfence();
-  const unsigned long long best = ld_volatile_u64(&ctrl->best_packed);
-  int pb = 0x3fffffff - (int)(best & 0x3fffffffull);
-  if (pb < 0 || pb >= ix.R) pb = 0;  // only reachable with NaN scores; keeps the CSR reads in bounds
-  const int cb = ix.root_child_ptr[pb], ce = ix.root_child_ptr[pb + 1];
-  uint32_t n = 0, vrow = 0;
-  for (int c0 = cb; c0 < ce; c0 += 32) {
-    const int ci = c0 + lane;
-    int c = -1, off = 0, size = 0;
-    if (ci < ce) {
-      c = ix.root_child_list[ci];
-      off = ix.leaf_offsets[c];
-      size = ix.leaf_sizes[c];
+
+  // ---- last CTA: the seed sample
+  const RootScanLayout L = root_scan_layout(ix.D * 4);
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem + L.keys_off);
+  int* blk = reinterpret_cast<int*>(smem + L.rows_off);  // [SEED_BLOCKS] leaf row, length, sample position
+  unsigned long long* sel = reinterpret_cast<unsigned long long*>(smem + L.sel_off);
+  SelectScratch* scratch = reinterpret_cast<SelectScratch*>(smem + L.scratch_off);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+  // the children of the seed root (the first SEED_SAMPLE_MAX of them in CSR
+  // order) as row intervals within the root: ch_v[c] = first row, ch_off[c] =
+  // its leaf row (precomputed per CSR entry); the key area is free until the
+  // sample is scored
+  int* ch_v = reinterpret_cast<int*>(keys);
+  int* ch_off = ch_v + SEED_SAMPLE_MAX;
+  if (warp == 0) {
+    const unsigned long long best = ld_volatile_u64(&ctrl->best_packed);
+    int pb = 0x3fffffff - (int)(best & 0x3fffffffull);
+    if (pb < 0 || pb >= ix.R) pb = 0;  // only reachable with NaN scores; keeps the CSR reads in bounds
+    const int cb = ix.root_child_ptr[pb];
+    const int nall = ix.root_child_ptr[pb + 1] - cb;
+    const int nch = min(nall, SEED_SAMPLE_MAX);
+    for (int ci = lane; ci < nch; ci += 32) {
+      const int2 sp = __ldg(ix.root_child_span + cb + ci);
+      ch_off[ci] = sp.x;
+      ch_v[ci] = sp.y;
     }
-    const int incl = warp_incl_scan(size, lane);
-    if (ci < ce) seed_ranges[n + lane] = make_int4((int)vrow + incl - size, off, off + size, c);
-    n += (uint32_t)min(32, ce - c0);
-    vrow += (uint32_t)__shfl_sync(FULL_MASK, incl, 31);
+    // rows of those children: the whole root, or up to the first child left out
+    const int vrows = nall > nch ? __ldg(ix.root_child_span + cb + nch).y : ix.root_rows[pb];
+    __syncwarp();
+    // blocks of up to SEED_BLOCK consecutive rows starting at evenly spaced
+    // virtual rows, each inside one child (one bulk copy per block); block b
+    // ends before block b + 1 starts, so no row is sampled twice
+    const int want = min(min(vrows, max(4 * k, 128)), SEED_SAMPLE_MAX);
+    const int nb = (want + SEED_BLOCK - 1) / SEED_BLOCK;
+    int pos_base = 0;
+    for (int b0 = 0; b0 < nb; b0 += 32) {
+      const int b = b0 + lane;
+      int row = 0, len = 0;
+      if (b < nb) {
+        // exact in double: vrows < 2^31, nb <= 64
+        const int v = (int)floor((double)b * (double)vrows / (double)nb);
+        const int v_next = (b + 1 < nb) ? (int)floor((double)(b + 1) * (double)vrows / (double)nb) : vrows;
+        int lo = 0, hi = nch - 1;
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (ch_v[mid] <= v) lo = mid; else hi = mid - 1;
+        }
+        const int child_end = (lo + 1 < nch) ? ch_v[lo + 1] : vrows;
+        len = min(min(SEED_BLOCK, v_next - v), child_end - v);
+        row = ch_off[lo] + (v - ch_v[lo]);
+      }
+      const int incl = warp_incl_scan(len, lane);
+      if (b < nb) {
+        blk[3 * b] = row;
+        blk[3 * b + 1] = len;
+        blk[3 * b + 2] = pos_base + incl - len;
+      }
+      pos_base += __shfl_sync(FULL_MASK, incl, 31);
+    }
+    if (lane == 0) {
+      s_nblk = nb;
+      s_nsample = pos_base;
+      s_ok = 1;
+      ctrl->best_root = pb;
+      mbar_init(bar, 1);
+      fence_mbar_init();
+    }
   }
-  if (lane == 0) {
-    ctrl->best_root = pb;
-    ctrl->seed_packed = ((unsigned long long)n << 32) | vrow;
-    ctrl->n_surv_children = n;
+  __syncthreads();
+  const int S = s_nsample, nb = s_nblk;
+  const int rb = ix.D * 4;
+  // the query in shared memory: this code runs once per search on a cold
+  // instruction cache, so the scoring loop below is kept compact
+  float4* sq4 = reinterpret_cast<float4*>(smem + L.q_off);
+  for (int c = threadIdx.x; c < ix.D4; c += blockDim.x) sq4[c] = __ldg(q4 + c);
+  uint32_t phase = 0;
+  for (int r0 = 0; r0 < S; r0 += L.ring_rows) {
+    const int nr = min(L.ring_rows, S - r0);
+    if (warp == 0) {
+      if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(nr * rb));
+      __syncwarp();
+      // the part of each block that falls into this round's sample positions
+      for (int b = lane; b < nb; b += 32) {
+        const int p0 = blk[3 * b + 2], p1 = p0 + blk[3 * b + 1];
+        const int a = max(p0, r0), e = min(p1, r0 + nr);
+        if (a < e)
+          tma_load_1d(smem + (size_t)(a - r0) * rb, ix.leaf + (size_t)(blk[3 * b] + (a - p0)) * ix.D,
+                      (uint32_t)((e - a) * rb), bar);
+      }
+    }
+    if (threadIdx.x == 0 && !mbar_wait(bar, phase, &ctrl->error, ERR_TIMEOUT_FULL)) s_ok = 0;
+    __syncthreads();
+    if (!s_ok) break;
+    phase ^= 1u;
+    // four rows per warp at a time (independent FMA chains); each row's score
+    // is computed exactly as the leaf scan computes it
+    for (int i0 = warp * 4; i0 < nr; i0 += ROOT_SCAN_WARPS * 4) {
+      const float4* r0p = reinterpret_cast<const float4*>(smem + (size_t)i0 * rb);
+      const int rstride = rb / 16, live = min(4, nr - i0);
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int c = lane; c < ix.D4; c += 32) {
+        const float4 a = sq4[c];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float4 x = t < live ? r0p[t * rstride + c] : make_float4(0.f, 0.f, 0.f, 0.f);
+          acc[t] = fmaf(x.x, a.x, acc[t]);
+          acc[t] = fmaf(x.y, a.y, acc[t]);
+          acc[t] = fmaf(x.z, a.z, acc[t]);
+          acc[t] = fmaf(x.w, a.w, acc[t]);
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) acc[t] = warp_sum(acc[t]);
+      if (lane < live) {
+        const float dot = lane == 0 ? acc[0] : (lane == 1 ? acc[1] : (lane == 2 ? acc[2] : acc[3]));
+        keys[r0 + i0 + lane] = pack_cand(f2key(dot), (uint32_t)(r0 + i0 + lane));
+      }
+    }
+    __syncthreads();  // the ring is refilled by the next round
+  }
+  if (!s_ok) {
+    if (threadIdx.x == 0) grace_period();  // copies of the round that gave up may still land
+    __syncthreads();
+  }
+  // T = k-th best sampled key (0 = no threshold: fewer than k rows sampled)
+  uint32_t T = 0u;
+  if (s_ok && S >= k) {
+    if (S <= 128) {
+      // warp 0, four keys per lane: the largest t with at least k keys >= t,
+      // decided bit by bit (that t is the k-th largest key)
+      if (warp == 0) {
+        uint32_t kv[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) kv[r] = (lane * 4 + r < S) ? cand_key(keys[lane * 4 + r]) : 0u;
+        uint32_t t = 0u;
+        for (int bit = 31; bit >= 0; --bit) {
+          const uint32_t tr = t | (1u << bit);
+          int cnt = 0;
+#pragma unroll
+          for (int r = 0; r < 4; ++r) cnt += __popc(__ballot_sync(FULL_MASK, kv[r] >= tr));
+          if (cnt >= k) t = tr;
+        }
+        T = t;
+      }
+    } else {
+      int selN = 1;
+      while (selN < k) selN <<= 1;
+      if (block_select_topk<false>(keys, S, k, sel, selN, scratch) == k) T = cand_key(sel[k - 1]);
+    }
+  }
+  if (threadIdx.x == 0) {
+    ctrl->seed_T_key = T;
+    ctrl->seed_packed = (unsigned long long)(uint32_t)S;  // rows scored by the sample
+    if (T > ctrl->theta_key) ctrl->theta_key = T;
+    if (T_export) *T_export = T ? key2f(T) : -INFINITY;
   }
 }
 
@@ -618,13 +838,25 @@ __host__ __device__ inline BoundsLayout bounds_layout(int D, int rank, int chunk
   return L;
 }
 
+// Two phases, so that the bound arithmetic overlaps the root scan (the kernel
+// is launched as a programmatic dependent of it):
+//  1. before griddep_wait(): per root (warp per root), fl(q.c) and ||q||^2
+//     recomputed here (any fp32 order is covered by the error terms), the
+//     rigorous root bound, the projection a = V^T q with the basis staged by
+//     TMA, and every child's rigorous bound; all rounded up to float and kept
+//     in ub_root[R] / ub_child[C].  None of this depends on the threshold.
+//  2. after griddep_wait(): T = max(seed threshold, T_ext) is known; roots and
+//     children whose bound is below T are skipped, the survivors are compacted
+//     into leaf ranges (one packed 64-bit atomic per 32 children).
 // T_ext (optional): a threshold from outside this index (the max of all shards'
 // seed thresholds); the bounds and the main scan use max(own seed, T_ext).
 __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, const float* __restrict__ q,
-                                                               SearchCtrl* ctrl, const float* __restrict__ root_dots,
+                                                               SearchCtrl* ctrl, float* __restrict__ ub_root,
+                                                               float* __restrict__ ub_child,
                                                                int4* __restrict__ main_ranges, int chunk_rows,
                                                                const float* __restrict__ T_ext) {
   extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int s_abort;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int D = ix.D, r = ix.rank;
   const BoundsLayout L = bounds_layout(D, r, chunk_rows);
@@ -637,47 +869,31 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
   float* ss = sa + 64;                                             // [64]
   uint64_t* bars = reinterpret_cast<uint64_t*>(ss + 64);
 
-  for (int i = threadIdx.x; i < D; i += blockDim.x) sq[i] = q[i];
+  // the query was complete before the kernel this one depends on was launched
+  // (an earlier kernel of the search, or the caller's own work): read through L2
+  for (int i = threadIdx.x; i < D; i += blockDim.x) sq[i] = __ldcg(q + i);
+  if (threadIdx.x == 0) s_abort = 0;
   if (lane == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
     fence_mbar_init();
   }
   __syncthreads();
+  griddep_launch();
 
-  uint32_t Tkey = ctrl->seed_T_key;
-  if (T_ext) {
-    const float te = *T_ext;
-    if (te > -INFINITY) {
-      const uint32_t ek = f2key(te);
-      if (ek > Tkey) Tkey = ek;
-      // the main scan starts from the raised threshold (it runs after this kernel)
-      if (blockIdx.x == 0 && threadIdx.x == 0) atomicMax(&ctrl->theta_key, ek);
-    }
-  }
-  const double T = Tkey ? (double)key2f(Tkey) : -INFINITY;
-  const int best = ctrl->best_root;
   const double gD = gamma_n(D);
-  const double QN = sqrt((double)ctrl->qn2 / (1.0 - gD)) * (1.0 + 1e-15);
+  // QN >= ||q||: fl(sum q_i^2) errs by at most gamma_D sum q_i^2 in any order
+  float qacc = 0.f;
+  for (int d = lane; d < D; d += 32) qacc = fmaf(sq[d], sq[d], qacc);
+  const double QN = sqrt((double)warp_sum(qacc) / (1.0 - gD)) * (1.0 + 1e-15);
   const int n_chunks = (D + chunk_rows - 1) / chunk_rows;
   uint32_t ph0 = 0, ph1 = 0;
-  uint32_t surv_roots = 0, surv_children = 0;
   bool abort_all = false;
 
+  // ---- phase 1: bounds (independent of the threshold)
   for (int p = blockIdx.x * BOUNDS_WARPS + warp; p < ix.R && !abort_all; p += gridDim.x * BOUNDS_WARPS) {
-    if (p == best) { ++surv_roots; continue; }
     if (ix.root_rows[p] == 0) continue;
-    const double dot = (double)root_dots[p];
-    const double cn = ix.root_cn[p];
-    const double rad = (double)ix.root_radii[p];
-    const double e_dot = gD * QN * cn;            // |fl(q.c) - q.c|
-    const double e_leaf = gD * QN * (cn + rad);   // |fl(q.x) - q.x| for ||x|| <= ||c|| + rad
-    double ub_root = dot + e_dot + QN * rad + e_leaf;
-    ub_root += 1e-12 * (fabs(dot) + QN * rad + e_dot + e_leaf);
-    if (ub_root < T) continue;
-    ++surv_roots;
-
-    // ---- projection a = V^T q (and s = |V|^T |q|) with the basis staged by TMA
+    // the basis copies go out first; q.c_r is computed while they are in flight
     const char* Vp = reinterpret_cast<const char*>(ix.bases + (size_t)p * D * r);
     if (lane == 0) {
       const int nr0 = min(chunk_rows, D);
@@ -689,6 +905,28 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
         tma_load_1d(buf1, Vp + (size_t)chunk_rows * r * 4, (uint32_t)(nr1 * r * 4), &bars[1]);
       }
     }
+    const float* cp = ix.root_centers + (size_t)p * D;
+    float dacc = 0.f;
+    for (int d = lane; d < D; d += 32) dacc = fmaf(sq[d], __ldg(cp + d), dacc);
+    const double dot = (double)warp_sum(dacc);
+    const double cn = ix.root_cn[p];
+    const double rad = (double)ix.root_radii[p];
+    const double e_dot = gD * QN * cn;            // |fl(q.c) - q.c|
+    const double e_leaf = gD * QN * (cn + rad);   // |fl(q.x) - q.x| for ||x|| <= ||c|| + rad
+    double ub_r = dot + e_dot + QN * rad + e_leaf;
+    ub_r += 1e-12 * (fabs(dot) + QN * rad + e_dot + e_leaf);
+    if (lane == 0) ub_root[p] = __double2float_ru(ub_r);
+    // the children's boxes and radii are read after the projection: start
+    // bringing them into L2 while the basis copies are in flight
+    const int cb = ix.root_child_ptr[p], ce = ix.root_child_ptr[p + 1];
+    for (int ci = cb + lane; ci < ce; ci += 32) {
+      const int c = ix.root_child_list[ci];
+      prefetch_l2(ix.child_l + (size_t)c * r);
+      prefetch_l2(ix.child_u + (size_t)c * r);
+      prefetch_l2(ix.child_radii + c);
+    }
+
+    // ---- projection a = V^T q (and s = |V|^T |q|)
     float a0 = 0.f, a1 = 0.f, s0 = 0.f, s1 = 0.f;
     for (int ch = 0; ch < n_chunks; ++ch) {
       const int b = ch & 1;
@@ -750,7 +988,7 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
     }
     __syncwarp();
 
-    // ---- rigorous residual norm ||q - V a|| (upper bound), see DESIGN notes
+    // ---- rigorous residual norm ||q - V a|| (upper bound)
     double an2 = 0.0, sad = 0.0;
     for (int j = 0; j < r; ++j) {
       const double aj = sa[j];
@@ -764,6 +1002,70 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
     const double an = sqrt(an2) * (1.0 + 1e-15);
 
     // ---- children: lane per child
+    for (int c0 = cb; c0 < ce; c0 += 32) {
+      const int ci = c0 + lane;
+      if (ci >= ce) continue;
+      const int c = ix.root_child_list[ci];
+      const float* lp = ix.child_l + (size_t)c * r;
+      const float* up = ix.child_u + (size_t)c * r;
+      double box = 0.0, ebox = 0.0, wn2 = 0.0;
+      if ((r & 3) == 0) {
+        for (int j = 0; j < r; j += 4) {
+          const float4 l4 = __ldg(reinterpret_cast<const float4*>(lp + j));
+          const float4 u4 = __ldg(reinterpret_cast<const float4*>(up + j));
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const double aj = sa[j + t];
+            box += fmax(aj * lv[t], aj * uv[t]);
+            const double w = fmax(fabs((double)lv[t]), fabs((double)uv[t]));
+            ebox += (double)ss[j + t] * w;
+            wn2 += w * w;
+          }
+        }
+      } else {
+        for (int j = 0; j < r; ++j) {
+          const double aj = sa[j];
+          const double lv = lp[j], uv = up[j];
+          box += fmax(aj * lv, aj * uv);
+          const double w = fmax(fabs(lv), fabs(uv));
+          ebox += (double)ss[j] * w;
+          wn2 += w * w;
+        }
+      }
+      ebox *= gD * (1.0 + 2.0 * gD);
+      const double rho = (double)ix.child_radii[c];
+      double ub = dot + e_dot + box + ebox + an * E * sqrt(wn2) * (1.0 + 1e-15) + perp * rho + e_leaf;
+      ub += 1e-12 * (fabs(dot) + fabs(box) + perp * rho + e_dot + e_leaf + ebox);
+      ub_child[c] = __double2float_ru(ub);
+    }
+    __syncwarp();  // sa / ss are rewritten for the next root
+  }
+  if (abort_all) {
+    if (lane == 0) grace_period();  // basis copies may still be in flight into this warp's buffers
+    s_abort = 1;                    // this CTA's roots are then all kept (the error bit is set)
+  }
+  __syncthreads();
+
+  // ---- phase 2: the threshold is known
+  griddep_wait();
+  uint32_t Tkey = ctrl->seed_T_key;
+  if (T_ext) {
+    const float te = *T_ext;
+    if (te > -INFINITY) {
+      const uint32_t ek = f2key(te);
+      if (ek > Tkey) Tkey = ek;
+      // the main scan starts from the raised threshold (it runs after this kernel)
+      if (blockIdx.x == 0 && threadIdx.x == 0) atomicMax(&ctrl->theta_key, ek);
+    }
+  }
+  const float T = Tkey ? key2f(Tkey) : -INFINITY;
+  const bool keep_all = s_abort != 0;
+  uint32_t surv_roots = 0, surv_children = 0;
+  for (int p = blockIdx.x * BOUNDS_WARPS + warp; p < ix.R; p += gridDim.x * BOUNDS_WARPS) {
+    if (ix.root_rows[p] == 0) continue;
+    if (!keep_all && __ldcg(ub_root + p) < T) continue;
+    ++surv_roots;
     const int cb = ix.root_child_ptr[p], ce = ix.root_child_ptr[p + 1];
     for (int c0 = cb; c0 < ce; c0 += 32) {
       const int ci = c0 + lane;
@@ -773,38 +1075,7 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
         c = ix.root_child_list[ci];
         off = ix.leaf_offsets[c];
         size = ix.leaf_sizes[c];
-        const float* lp = ix.child_l + (size_t)c * r;
-        const float* up = ix.child_u + (size_t)c * r;
-        double box = 0.0, ebox = 0.0, wn2 = 0.0;
-        if ((r & 3) == 0) {
-          for (int j = 0; j < r; j += 4) {
-            const float4 l4 = __ldg(reinterpret_cast<const float4*>(lp + j));
-            const float4 u4 = __ldg(reinterpret_cast<const float4*>(up + j));
-            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const double aj = sa[j + t];
-              box += fmax(aj * lv[t], aj * uv[t]);
-              const double w = fmax(fabs((double)lv[t]), fabs((double)uv[t]));
-              ebox += (double)ss[j + t] * w;
-              wn2 += w * w;
-            }
-          }
-        } else {
-          for (int j = 0; j < r; ++j) {
-            const double aj = sa[j];
-            const double lv = lp[j], uv = up[j];
-            box += fmax(aj * lv, aj * uv);
-            const double w = fmax(fabs(lv), fabs(uv));
-            ebox += (double)ss[j] * w;
-            wn2 += w * w;
-          }
-        }
-        ebox *= gD * (1.0 + 2.0 * gD);
-        const double rho = (double)ix.child_radii[c];
-        double ub = dot + e_dot + box + ebox + an * E * sqrt(wn2) * (1.0 + 1e-15) + perp * rho + e_leaf;
-        ub += 1e-12 * (fabs(dot) + fabs(box) + perp * rho + e_dot + e_leaf + ebox);
-        surv = !(ub < T);
+        surv = keep_all || !(__ldcg(ub_child + c) < T);
       }
       const uint32_t bal = __ballot_sync(FULL_MASK, surv);
       const int rows_l = surv ? size : 0;
@@ -826,7 +1097,6 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
   if (lane == 0) {
     if (surv_roots) atomicAdd(&ctrl->n_surv_roots, surv_roots);
     if (surv_children) atomicAdd(&ctrl->n_surv_children, surv_children);
-    if (abort_all) grace_period();  // basis copies may still be in flight into this warp's buffers
   }
 }
 
@@ -901,6 +1171,24 @@ int scan_smem_bytes(int D) {
   return (int)L.total;
 }
 
+// Launches `kern` as a programmatic dependent of the previous kernel on `stream`
+// (it may start while that kernel runs and waits in griddep_wait()).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_dependent(void (*kern)(KArgs...), int grid, int block, size_t smem, cudaStream_t stream,
+                                    Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 template <int VPL, int KCAP>
 static cudaError_t launch_scan_t(const ScanParams& P0, int grid, cudaStream_t stream) {
   // as many ring stages as the shared-memory budget leaves after the top-k areas
@@ -914,8 +1202,7 @@ static cudaError_t launch_scan_t(const ScanParams& P0, int grid, cudaStream_t st
   static SmemOptIn opt_in;  // per instantiation, per device
   cudaError_t e = opt_in.ensure(reinterpret_cast<const void*>(k_scan<VPL, KCAP>), (int)L.total);
   if (e != cudaSuccess) return e;
-  k_scan<VPL, KCAP><<<grid, SCAN_THREADS, L.total, stream>>>(P);
-  return cudaGetLastError();
+  return launch_dependent(k_scan<VPL, KCAP>, grid, SCAN_THREADS, L.total, stream, P);
 }
 
 template <int VPL>
@@ -965,8 +1252,6 @@ static ScanParams scan_params(const IndexView& ix, const Workspace& ws, const fl
   P.k = k;
   P.stages = stages_for(vpl_bucket(ix.D4), P.row_bytes);
   P.min_rows = SCAN_MIN_ROWS;
-  P.seed_list = ws.ctrl->seed_list;
-  P.seed_T_key = &ws.ctrl->seed_T_key;
   P.out_scores = out_scores;
   P.out_ids = out_ids;
   P.out_rows = out_rows;
@@ -974,13 +1259,16 @@ static ScanParams scan_params(const IndexView& ix, const Workspace& ws, const fl
   return P;
 }
 
-// Clears the control header; with io, also stages the query (see HostIO).
+// First kernel of a search (an ordinary launch, so it starts only after the
+// previous search on the stream has finished with the workspace): clears the
+// control header; with io, also stages the query (see HostIO).
 static cudaError_t search_reset(const IndexView& ix, const Workspace& ws, const float* q, cudaStream_t stream,
                                 const HostIO* io) {
-  if (!io) return cudaMemsetAsync(ws.ctrl, 0, CTRL_RESET_BYTES, stream);
-  k_search_prologue<<<1, 128, 0, stream>>>(reinterpret_cast<const float4*>(io->q_host), io->slots,
+  k_search_prologue<<<1, 128, 0, stream>>>(io ? reinterpret_cast<const float4*>(io->q_host) : nullptr,
+                                           io ? io->slots : nullptr,
                                            reinterpret_cast<float4*>(const_cast<float*>(q)), ix.D4,
-                                           reinterpret_cast<unsigned long long*>(ws.ctrl), io->out_indirect);
+                                           reinterpret_cast<unsigned long long*>(ws.ctrl),
+                                           io ? io->out_indirect : nullptr);
   return cudaGetLastError();
 }
 
@@ -995,17 +1283,12 @@ cudaError_t launch_search_seed(const IndexView& ix, const Workspace& ws, const f
                                cudaStream_t stream, const HostIO* io) {
   cudaError_t e = search_reset(ix, ws, q, stream, io);
   if (e != cudaSuccess) return e;
-  k_root_scan<<<(ix.R + ROOT_SCAN_WARPS - 1) / ROOT_SCAN_WARPS, ROOT_SCAN_WARPS * 32, 0, stream>>>(
-      ix, q, ws.ctrl, ws.root_dots, ws.seed_ranges, k);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  ScanParams S = scan_params(ix, ws, q, k, nullptr, nullptr, nullptr);
-  S.ranges = ws.seed_ranges;
-  S.packed_counts = &ws.ctrl->seed_packed;
-  S.done = &ws.ctrl->seed_done;
-  S.final_mode = 0;
-  S.merge_seed = 0;
-  S.T_export = T_export;
-  return launch_scan(S, ws.scan_grid, stream);
+  const RootScanLayout RL = root_scan_layout(ix.D * 4);
+  static SmemOptIn root_opt_in;
+  if ((e = root_opt_in.ensure(reinterpret_cast<const void*>(k_root_scan), (int)RL.total)) != cudaSuccess) return e;
+  int grid = (ix.R + ROOT_SCAN_WARPS - 1) / ROOT_SCAN_WARPS;
+  if (grid > ws.scan_grid) grid = ws.scan_grid;
+  return launch_dependent(k_root_scan, grid, ROOT_SCAN_WARPS * 32, RL.total, stream, ix, q, ws.ctrl, k, T_export);
 }
 
 cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const float* q, int k, const float* T_ext,
@@ -1018,15 +1301,13 @@ cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const
   if ((e = bounds_opt_in.ensure(reinterpret_cast<const void*>(k_bounds), (int)BL.total)) != cudaSuccess) return e;
   int grid_b = (ix.R + BOUNDS_WARPS - 1) / BOUNDS_WARPS;
   if (grid_b > 2 * ws.scan_grid) grid_b = 2 * ws.scan_grid;
-  k_bounds<<<grid_b, BOUNDS_WARPS * 32, BL.total, stream>>>(ix, q, ws.ctrl, ws.root_dots, ws.main_ranges, chunk_rows,
-                                                             T_ext);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if ((e = launch_dependent(k_bounds, grid_b, BOUNDS_WARPS * 32, BL.total, stream, ix, q, ws.ctrl, ws.ub_root,
+                            ws.ub_child, ws.main_ranges, chunk_rows, T_ext)) != cudaSuccess)
+    return e;
   ScanParams M = scan_params(ix, ws, q, k, out_scores, out_ids, out_rows);
   M.ranges = ws.main_ranges;
   M.packed_counts = &ws.ctrl->main_packed;
   M.done = &ws.ctrl->main_done;
-  M.final_mode = 1;
-  M.merge_seed = 1;
   final_io(M, ws, io);
   if (ev_scan0) cudaEventRecord(ev_scan0, stream);
   e = launch_scan(M, ws.scan_grid, stream);
@@ -1049,8 +1330,6 @@ cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float*
   F.ranges = ws.flat_range;
   F.packed_counts = ws.flat_packed;
   F.done = &ws.ctrl->main_done;
-  F.final_mode = 1;
-  F.merge_seed = 0;
   final_io(F, ws, io);
   if (ev_scan0) cudaEventRecord(ev_scan0, stream);
   e = launch_scan(F, ws.scan_grid, stream);
@@ -1076,10 +1355,6 @@ cudaError_t launch_flat_scan(const float* leaf, int D, int N, const float* q, in
   F.k = k;
   F.stages = stages_for(vpl, F.row_bytes);
   F.min_rows = SCAN_MIN_ROWS;
-  F.final_mode = 1;
-  F.merge_seed = 0;
-  F.seed_list = ctrl->seed_list;
-  F.seed_T_key = &ctrl->seed_T_key;
   F.out_scores = out_scores;
   F.out_ids = out_ids;
   F.out_rows = nullptr;

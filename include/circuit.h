@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define CIRCUIT_ABI_VERSION 1
+#define CIRCUIT_ABI_VERSION 2
 #define CIRCUIT_MAX_K 256
 #define CIRCUIT_MAX_RANK 64
 #define CIRCUIT_MAX_DIM 2048
@@ -75,14 +75,17 @@ typedef struct {
 typedef struct {
   float latency_us;            /* host wall time of the call (0 for async calls) */
   int32_t path;                /* 0 = flat scan, 1 = hierarchical */
-  int64_t vectors_scored;      /* leaf rows whose score was computed */
+  int64_t vectors_scored;      /* leaf rows scanned for the result (rows of surviving children) */
   int64_t vectors_total;       /* N */
   int32_t surviving_roots;     /* roots not pruned (seed root included) */
   int32_t surviving_children;  /* non-empty children scanned */
   int32_t total_children;      /* num_total_children */
   int32_t best_root;           /* the seed root */
-  float seed_threshold;        /* k-th best score among the seed root's rows (-inf if none) */
+  float seed_threshold;        /* k-th best score among the sampled rows of the seed root (-inf if none) */
   int32_t device_error;        /* device error bits of the last search (0 = none) */
+  int32_t seed_sample_rows;    /* rows of the seed root scored beforehand for the threshold (not in
+                                  vectors_scored; scanned again when their children survive);
+                                  ABI version 2 */
 } circuit_trace_ex_t;
 
 /* ------------------------------------------------------------------ reference ABI */
@@ -173,9 +176,10 @@ int circuit_trace_decode(circuit_index_t index, const void* snapshot, int path, 
 
 /* The hierarchical search in two phases, for a corpus sharded over several
  * GPUs (no reference counterpart).  circuit_search_seed_async resets the
- * handle's search state, scans the roots and the best root's rows, and writes
- * this shard's seed threshold (k-th best score of k of its rows, -inf if the
- * best root holds fewer than k rows) to dev_threshold_out[0] (float, device).
+ * handle's search state, scans the roots, scores an evenly spaced sample of
+ * the best root's rows (max(4k, 128) of them, at most 1,024) and writes this
+ * shard's seed threshold (k-th best sampled score, -inf if fewer than k rows
+ * were sampled) to dev_threshold_out[0] (float, device).
  * The caller may replace it by the maximum over all shards (e.g. an NCCL
  * all-reduce MAX): each shard's value is the k-th best of k real rows, so the
  * maximum never exceeds the global k-th best score.  circuit_search_finish_async

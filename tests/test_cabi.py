@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_null_handles():
     L = _native.lib()
-    assert L.circuit_abi_version() == 1
+    assert L.circuit_abi_version() == 2
     # reference convention: -1 for a null index (api.cpp:28-29, :41-42)
     q = np.zeros(8, np.float32)
     s = np.zeros(4, np.float32)
