@@ -425,113 +425,187 @@ def _eig_basis(gram: torch.Tensor, rank: int) -> torch.Tensor:
     return Q.to(torch.float32)
 
 
+def _part_hierarchy(leaf, orig, part_off, part_root, centers, children_per_root, rank, random_state, device,
+                    sub=1 << 17):
+    """Children and certificates of each part (a root, or a contiguous slice of
+    a root's rows) laid out in leaf[part_off[j]:part_off[j+1]]: the PCA basis
+    of the part's rows (top eigenvectors of the float64 Gram matrix of x - c,
+    QR, float32), k-means children (generator seeded by (random_state, root,
+    first row of the part), so a part's children do not depend on which rank
+    builds it), rows reordered child-contiguous in place, and the float64
+    certificates of build_circuit_index.  Returns the per-part / per-child arrays."""
+    P = len(part_root)
+    dim = leaf.shape[1]
+    C = P * children_per_root
+    f32 = dict(dtype=torch.float32, device=device)
+    out = dict(root_centers=torch.zeros((P, dim), **f32), root_radii=torch.zeros(P, **f32),
+               bases=torch.zeros((P, dim, rank), **f32), child_intervals_l=torch.zeros((C, rank), **f32),
+               child_intervals_u=torch.zeros((C, rank), **f32), child_radii=torch.zeros(C, **f32),
+               child_parent_ids=torch.zeros(C, dtype=torch.int32, device=device),
+               leaf_offsets=torch.zeros(C, dtype=torch.int32, device=device),
+               leaf_sizes=torch.zeros(C, dtype=torch.int32, device=device))
+    for j in range(P):
+        o_p, n_p = int(part_off[j]), int(part_off[j + 1] - part_off[j])
+        for ci in range(children_per_root):
+            out["child_parent_ids"][j * children_per_root + ci] = j
+        c32 = centers[int(part_root[j])]
+        out["root_centers"][j] = c32
+        if n_p == 0:
+            continue
+        c64 = c32.double()
+        gram = torch.zeros((dim, dim), dtype=torch.float64, device=device)
+        rad = torch.zeros((), dtype=torch.float64, device=device)
+        for a in range(o_p, o_p + n_p, sub):
+            d = leaf[a:min(o_p + n_p, a + sub)].double() - c64
+            gram += d.T @ d
+            rad = torch.maximum(rad, d.norm(dim=1).max())
+        out["root_radii"][j] = _round_up_f32(rad + _EPS)
+        Q32 = _eig_basis(gram, rank)
+        out["bases"][j] = Q32
+        Q64 = Q32.double()
+        k_c = min(children_per_root, n_p)
+        if k_c > 1:
+            gen = torch.Generator(device="cpu")
+            gen.manual_seed((random_state * 1_000_003 + int(part_root[j]) * 7919 + int(orig[o_p]) * 31) % (2 ** 62))
+            cc = _kmeans(leaf[o_p:o_p + min(n_p, 1 << 16)], k_c, 5, gen)
+            clab = torch.cat([_assign(leaf[a:min(o_p + n_p, a + sub)], cc) for a in range(o_p, o_p + n_p, sub)])
+        else:
+            clab = torch.zeros(n_p, dtype=torch.long, device=device)
+        perm = torch.argsort(clab, stable=True)
+        leaf[o_p:o_p + n_p] = leaf[o_p:o_p + n_p][perm]
+        orig[o_p:o_p + n_p] = orig[o_p:o_p + n_p][perm]
+        ccounts = torch.bincount(clab, minlength=k_c).tolist()
+        cs = o_p
+        for ci in range(k_c):
+            g = j * children_per_root + ci
+            m = ccounts[ci]
+            if m == 0:
+                continue
+            lo = torch.full((rank,), float("inf"), dtype=torch.float64, device=device)
+            hi = torch.full((rank,), float("-inf"), dtype=torch.float64, device=device)
+            rr = torch.zeros((), dtype=torch.float64, device=device)
+            for a in range(cs, cs + m, sub):
+                d = leaf[a:min(cs + m, a + sub)].double() - c64
+                z = d @ Q64
+                lo = torch.minimum(lo, z.min(dim=0).values)
+                hi = torch.maximum(hi, z.max(dim=0).values)
+                rr = torch.maximum(rr, (d - z @ Q64.T).norm(dim=1).max())
+            out["child_intervals_l"][g] = _round_down_f32(lo - _EPS)
+            out["child_intervals_u"][g] = _round_up_f32(hi + _EPS)
+            out["child_radii"][g] = _round_up_f32(rr + _EPS)
+            out["leaf_offsets"][g] = cs
+            out["leaf_sizes"][g] = m
+            cs += m
+    return out
+
+
 def build_circuit_index_streaming(rows_fn, n: int, dim: int, num_roots: int, children_per_root: int, rank: int,
                                   random_state: int = 42, device: str = "cuda", chunk: int = 1 << 18,
-                                  sample: int = 1 << 19) -> CircuitIndex:
-    """Build an index over a corpus too large to hold twice: ``rows_fn(start,
-    stop)`` must return rows [start, stop) deterministically (as the seeded
-    generators of circuit_rag.synthetic do).  Two generation passes: the first
-    assigns roots (k-means centres fitted on the first ``sample`` rows), the
-    second scatters rows straight into their root-major slot.  Per root, the
-    Gram matrix, child k-means, child ordering and certificates are computed in
-    row sub-chunks, so extra memory is one root's rows plus a float64 chunk.
-    Certificates are exact for the stored float32 data, as in build_circuit_index."""
+                                  sample: int = 1 << 19, shard_rank: int = 0, world: int = 1, group=None,
+                                  max_imbalance: float = 1.05, block_rows: int = 64) -> CircuitIndex:
+    """Build an index over a corpus too large to hold twice, or this rank's
+    shard of it: ``rows_fn(start, stop)`` must return rows [start, stop)
+    deterministically (as the seeded generators of circuit_rag.synthetic do).
+
+    1. Root centres: k-means on the first ``sample`` rows (rank 0; broadcast
+       to the other ranks).
+    2. Root of every row (max inner product): each rank labels its 1/world of
+       the rows and the labels are all-gathered, so every rank sees the same
+       assignment.
+    3. Shard plan (circuit_plan_shard_parts over blocks of ``block_rows`` rows
+       of each root, in row order): whole roots, largest first, to the
+       least-loaded rank; a root that does not fit within ``max_imbalance`` x
+       the mean shard is cut into contiguous row ranges (parts), each becoming a
+       root of its rank's index with the same centre.  world = 1: one part per
+       root, the whole corpus.
+    4. Second generation pass: every rank scatters the rows of its parts
+       straight into their part-major slots.
+    5. Per part: PCA basis, k-means children, certificates in float64
+       (exact for the stored float32 data, as in build_circuit_index).
+
+    The returned index holds this rank's parts only; ``original_ids`` are
+    global row numbers; ``shard_info`` records the plan."""
     if not 1 <= rank <= MAX_RANK:
         raise ValueError(f"rank must be in [1, {MAX_RANK}]")
+    if world > 1:
+        import torch.distributed as dist
     gen = torch.Generator(device="cpu")
     gen.manual_seed(random_state)
     allow = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = True  # assignments only pick clusters; certificates are fp64
     try:
-        S = rows_fn(0, min(sample, n)).to(device)
-        root_centers = _kmeans(S, num_roots, 8, gen)
-        del S
-        labels = torch.empty(n, dtype=torch.int32, device=device)
-        for s in range(0, n, chunk):
-            e = min(n, s + chunk)
-            labels[s:e] = _assign(rows_fn(s, e).to(device), root_centers).to(torch.int32)
-        counts = torch.bincount(labels, minlength=num_roots)
-        root_off = torch.cumsum(counts, 0) - counts
-        leaf = torch.empty((n, dim), dtype=torch.float32, device=device)
-        orig = torch.empty(n, dtype=torch.int32, device=device)
-        cursor = root_off.clone()
-        for s in range(0, n, chunk):
-            e = min(n, s + chunk)
-            X = rows_fn(s, e).to(device)
-            lab = labels[s:e].long()
-            order = torch.argsort(lab, stable=True)
-            ls = lab[order]
-            cnt = torch.bincount(ls, minlength=num_roots)
-            first = torch.cumsum(cnt, 0) - cnt
-            pos = cursor[ls] + (torch.arange(e - s, device=device) - first[ls])
-            leaf[pos] = X[order]
-            orig[pos] = (order + s).to(torch.int32)
-            cursor += cnt
+        # 1. root centres
+        if shard_rank == 0:
+            S = rows_fn(0, min(sample, n)).to(device)
+            centers = _kmeans(S, num_roots, 8, gen)
+            del S
+        else:
+            centers = torch.empty((num_roots, dim), dtype=torch.float32, device=device)
+        if world > 1:
+            dist.broadcast(centers, 0, group=group)
+        # 2. labels: this rank's slice, then all-gathered
+        per = (n + world - 1) // world
+        lo_r, hi_r = min(n, shard_rank * per), min(n, (shard_rank + 1) * per)
+        mine = torch.full((per,), -1, dtype=torch.int32, device=device)
+        for s in range(lo_r, hi_r, chunk):
+            e = min(hi_r, s + chunk)
+            mine[s - lo_r:e - lo_r] = _assign(rows_fn(s, e).to(device), centers).to(torch.int32)
+        if world > 1:
+            labels = torch.empty(per * world, dtype=torch.int32, device=device)
+            dist.all_gather_into_tensor(labels, mine, group=group)
+            labels = labels[:n]
+        else:
+            labels = mine[:n]
+        del mine
+        counts = torch.bincount(labels.long(), minlength=num_roots)
+        root_start = torch.cumsum(counts, 0) - counts
+        # 3. plan over blocks of rows of each root (host, identical on every rank)
+        from circuit_rag.shard import plan_shard_parts
+
+        counts_h = counts.cpu().numpy().astype(np.int64)
+        nblk = (counts_h + block_rows - 1) // block_rows
+        atom_ptr = np.concatenate([[0], np.cumsum(nblk)]).astype(np.int64)
+        atom_rows = np.full(int(atom_ptr[-1]), block_rows, dtype=np.int64)
+        last = atom_ptr[1:] - 1
+        has = nblk > 0
+        atom_rows[last[has]] = counts_h[has] - (nblk[has] - 1) * block_rows
+        plan = plan_shard_parts(atom_rows, atom_ptr, world, max_imbalance)
+        own = np.nonzero(plan["part_rank"] == shard_rank)[0]
+        part_root = plan["part_root"][own]
+        # rows of part j: positions [r0, r1) among its root's rows (row order)
+        r0 = (plan["part_atom_begin"][own] - atom_ptr[part_root]) * block_rows
+        r1 = np.minimum((plan["part_atom_end"][own] - atom_ptr[part_root]) * block_rows, counts_h[part_root])
+        part_off = np.concatenate([[0], np.cumsum(r1 - r0)]).astype(np.int64)
+        n_own = int(part_off[-1])
+        # 4. slot of every owned row: the rows of root p in row order are
+        # order[root_start[p] : root_start[p] + counts[p]]
+        order = torch.argsort(labels, stable=True)
         del labels
-        C = num_roots * children_per_root
-        f32 = dict(dtype=torch.float32, device=device)
-        root_radii = torch.zeros(num_roots, **f32)
-        bases = torch.zeros((num_roots, dim, rank), **f32)
-        child_l = torch.zeros((C, rank), **f32)
-        child_u = torch.zeros((C, rank), **f32)
-        child_radii = torch.zeros(C, **f32)
-        child_parent = torch.zeros(C, dtype=torch.int32, device=device)
-        leaf_offsets = torch.zeros(C, dtype=torch.int32, device=device)
-        leaf_sizes = torch.zeros(C, dtype=torch.int32, device=device)
-        counts_l = counts.tolist()
-        offs_l = root_off.tolist()
-        sub = 1 << 17
-        for p in range(num_roots):
-            n_p, o_p = counts_l[p], offs_l[p]
-            if n_p == 0:
+        slot = torch.full((n,), -1, dtype=torch.int64, device=device)
+        for j in range(len(own)):
+            a = int(root_start[int(part_root[j])]) + int(r0[j])
+            b = a + int(r1[j] - r0[j])
+            slot[order[a:b]] = torch.arange(int(part_off[j]), int(part_off[j + 1]), device=device)
+        del order
+        leaf = torch.empty((n_own, dim), dtype=torch.float32, device=device)
+        orig = torch.empty(n_own, dtype=torch.int32, device=device)
+        for s in range(0, n, chunk):
+            e = min(n, s + chunk)
+            sl = slot[s:e]
+            keep = torch.nonzero(sl >= 0).flatten()
+            if keep.numel() == 0:
                 continue
-            c64 = root_centers[p].double()
-            gram = torch.zeros((dim, dim), dtype=torch.float64, device=device)
-            rad = torch.zeros((), dtype=torch.float64, device=device)
-            for a in range(o_p, o_p + n_p, sub):
-                d = leaf[a:min(o_p + n_p, a + sub)].double() - c64
-                gram += d.T @ d
-                rad = torch.maximum(rad, d.norm(dim=1).max())
-            root_radii[p] = _round_up_f32(rad + _EPS)
-            Q32 = _eig_basis(gram, rank)
-            bases[p] = Q32
-            Q64 = Q32.double()
-            k_c = min(children_per_root, n_p)
-            if k_c > 1:
-                cc = _kmeans(leaf[o_p:o_p + min(n_p, 1 << 16)], k_c, 5, gen)
-                clab = torch.cat([_assign(leaf[a:min(o_p + n_p, a + sub)], cc) for a in range(o_p, o_p + n_p, sub)])
-            else:
-                clab = torch.zeros(n_p, dtype=torch.long, device=device)
-            perm = torch.argsort(clab, stable=True)
-            leaf[o_p:o_p + n_p] = leaf[o_p:o_p + n_p][perm]
-            orig[o_p:o_p + n_p] = orig[o_p:o_p + n_p][perm]
-            ccounts = torch.bincount(clab, minlength=k_c).tolist()
-            cs = o_p
-            for ci in range(k_c):
-                g = p * children_per_root + ci
-                child_parent[g] = p
-                m = ccounts[ci]
-                if m == 0:
-                    continue
-                lo = torch.full((rank,), float("inf"), dtype=torch.float64, device=device)
-                hi = torch.full((rank,), float("-inf"), dtype=torch.float64, device=device)
-                rr = torch.zeros((), dtype=torch.float64, device=device)
-                for a in range(cs, cs + m, sub):
-                    d = leaf[a:min(cs + m, a + sub)].double() - c64
-                    z = d @ Q64
-                    lo = torch.minimum(lo, z.min(dim=0).values)
-                    hi = torch.maximum(hi, z.max(dim=0).values)
-                    rr = torch.maximum(rr, (d - z @ Q64.T).norm(dim=1).max())
-                child_l[g] = _round_down_f32(lo - _EPS)
-                child_u[g] = _round_up_f32(hi + _EPS)
-                child_radii[g] = _round_up_f32(rr + _EPS)
-                leaf_offsets[g] = cs
-                leaf_sizes[g] = m
-                cs += m
+            X = rows_fn(s, e).to(device)
+            leaf[sl[keep]] = X[keep]
+            orig[sl[keep]] = (keep + s).to(torch.int32)
+        del slot
+        # 5. per part: basis, children, certificates
+        arrays = _part_hierarchy(leaf, orig, part_off, part_root, centers, children_per_root, rank, random_state,
+                                 device)
     finally:
         torch.backends.cuda.matmul.allow_tf32 = allow
-    return CircuitIndex(
-        root_centers=root_centers, root_radii=root_radii, bases=bases, child_intervals_l=child_l,
-        child_intervals_u=child_u, child_radii=child_radii, child_parent_ids=child_parent,
-        leaf_offsets=leaf_offsets, leaf_sizes=leaf_sizes, leaf_vectors=leaf, original_ids=orig, dim=dim,
-        rank=rank, device=device)
+    idx = CircuitIndex(leaf_vectors=leaf, original_ids=orig, dim=dim, rank=rank, device=device, **arrays)
+    idx.shard_info = {"rank": shard_rank, "world": world, "part_root": part_root.tolist(),
+                      "rows": n_own, "rank_rows": plan["rank_rows"].tolist(),
+                      "parts_total": int(len(plan["part_root"])), "roots": num_roots}
+    return idx

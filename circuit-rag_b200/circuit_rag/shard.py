@@ -1,10 +1,12 @@
 """Multi-GPU exact search: the corpus sharded by root cluster, one process per GPU.
 
-* ``plan_shards`` assigns roots to ranks by longest-processing-time on leaf rows
-  (Zipf-sized clusters make round-robin unbalanced).
-* ``load_shard`` reads a .circuit file and keeps only the roots one rank owns:
+* ``plan_shard_parts`` assigns roots to ranks largest first and cuts a root
+  too large for its rank between children (Zipf-sized clusters make whole-root
+  plans unbalanced); ``plan_shards`` is the whole-root plan.
+* ``load_shard`` reads a .circuit file and keeps only the parts one rank owns:
   their centres, bases, children and leaf rows (read as byte ranges of the
-  file, never the whole corpus) with their global original ids.
+  file, never the whole corpus) with their global original ids.  The native
+  loader circuit_load_shard does the same without Python.
 * ``ShardedSearcher.search`` runs the local exact search on the rank's GPU,
   all-gathers the k (score, id) candidates of every rank (NCCL over
   NVLink/NVSwitch; gloo works for CPU tests) and merges them on the device
@@ -16,7 +18,7 @@ merge of all shard lists is the global top-k (same (score desc, id asc) order).
 import ctypes
 import datetime
 import mmap
-from typing import Callable, Optional, Sequence, Tuple
+from typing import Callable, Dict, Optional, Sequence, Tuple
 
 import numpy as np
 import torch
@@ -27,7 +29,8 @@ from circuit_rag.storage.format import TENSOR_ORDER, read_header
 
 
 def plan_shards(root_rows: Sequence[int], world: int) -> np.ndarray:
-    """root -> rank by longest-processing-time on leaf rows (circuit_plan_shards)."""
+    """root -> rank by longest-processing-time on leaf rows, whole roots only
+    (circuit_plan_shards)."""
     rows = np.ascontiguousarray(root_rows, dtype=np.int64)
     out = np.empty(len(rows), dtype=np.int32)
     _native.check(_native.lib().circuit_plan_shards(rows.ctypes.data, len(rows), int(world), out.ctypes.data, None),
@@ -35,13 +38,55 @@ def plan_shards(root_rows: Sequence[int], world: int) -> np.ndarray:
     return out
 
 
-def _root_rows(parent: np.ndarray, sizes: np.ndarray, num_roots: int) -> np.ndarray:
-    live = sizes > 0
-    return np.bincount(parent[live], weights=sizes[live].astype(np.int64), minlength=num_roots).astype(np.int64)
+def plan_shard_parts(atom_rows: Sequence[int], root_atom_ptr: Sequence[int], world: int,
+                     max_imbalance: float = 1.05) -> Dict[str, np.ndarray]:
+    """Shard plan that cuts oversized roots between atoms (circuit_plan_shard_parts).
+    Root p's rows are the atoms atom_rows[root_atom_ptr[p]:root_atom_ptr[p+1]]
+    (its children in leaf order, or blocks of rows).  Returns arrays part_root,
+    part_atom_begin, part_atom_end, part_rank (ordered by rank, root, first
+    atom) and rank_rows."""
+    atoms = np.ascontiguousarray(atom_rows, dtype=np.int64)
+    ptr = np.ascontiguousarray(root_atom_ptr, dtype=np.int64)
+    R = len(ptr) - 1
+    cap = R + 2 * int(world) + 8
+    while True:
+        pr = np.empty(cap, np.int32)
+        pb = np.empty(cap, np.int64)
+        pe = np.empty(cap, np.int64)
+        rk = np.empty(cap, np.int32)
+        npart = ctypes.c_int(0)
+        rr = np.empty(int(world), np.int64)
+        rc = _native.lib().circuit_plan_shard_parts(atoms.ctypes.data, ptr.ctypes.data, R, int(world),
+                                                    float(max_imbalance), pr.ctypes.data, pb.ctypes.data,
+                                                    pe.ctypes.data, rk.ctypes.data, cap, ctypes.byref(npart),
+                                                    rr.ctypes.data)
+        if rc == 0:
+            m = npart.value
+            return {"part_root": pr[:m], "part_atom_begin": pb[:m], "part_atom_end": pe[:m], "part_rank": rk[:m],
+                    "rank_rows": rr}
+        if npart.value <= cap:
+            _native.check(rc, "plan_shard_parts")
+        cap = npart.value
 
 
-def load_shard(filepath: str, rank: int, world: int, device: str = "cuda") -> CircuitIndex:
-    """The part of a .circuit index that `rank` of `world` owns (complete roots)."""
+def _root_children(parent: np.ndarray, offsets: np.ndarray, sizes: np.ndarray, num_roots: int):
+    """CSR of each root's non-empty children in leaf order: (ptr [R+1], children)."""
+    live = np.nonzero(sizes > 0)[0]
+    order = live[np.lexsort((offsets[live], parent[live]))]
+    counts = np.bincount(parent[order], minlength=num_roots)
+    ptr = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
+    return ptr, order
+
+
+def load_shard(filepath: str, rank: int, world: int, device: str = "cuda",
+               max_imbalance: float = 1.05) -> CircuitIndex:
+    """The part of a .circuit index that `rank` of `world` owns.  The plan
+    (plan_shard_parts over each root's children in leaf order) places whole
+    roots where they fit and cuts a root too large for
+    ``max_imbalance`` x the mean shard between children: each part becomes a
+    root of the shard with the original centre, radius and basis, and keeps a
+    contiguous range of its children.  Only the owned parts' byte ranges of the
+    file are read; original ids stay global."""
     meta = read_header(filepath)
     R, C, D, r = (int(meta[k]) for k in ("num_roots", "num_total_children", "dim", "rank"))
     with open(filepath, "rb") as f:
@@ -53,11 +98,11 @@ def load_shard(filepath: str, rank: int, world: int, device: str = "cuda") -> Ci
                               shape=tuple(info["shape"]))
 
         parent, offsets, sizes = (arr(n).copy() for n in ("child_parent_ids", "leaf_offsets", "leaf_sizes"))
-        owner = plan_shards(_root_rows(parent, sizes, R), world)
-        roots = np.nonzero(owner == rank)[0]
-        live = sizes > 0
-        kids = [np.nonzero(live & (parent == p))[0] for p in roots]
-        kids = [k[np.argsort(offsets[k], kind="stable")] for k in kids]
+        ptr, kids_all = _root_children(parent, offsets, sizes, R)
+        plan = plan_shard_parts(sizes[kids_all].astype(np.int64), ptr, world, max_imbalance)
+        own = np.nonzero(plan["part_rank"] == rank)[0]
+        roots = plan["part_root"][own]
+        kids = [kids_all[int(a):int(b)] for a, b in zip(plan["part_atom_begin"][own], plan["part_atom_end"][own])]
         cpr = max([len(k) for k in kids] + [1])
         Rs, Cs = len(roots), max(1, len(roots)) * cpr
         n_rows = int(sum(int(sizes[k].sum()) for k in kids))
@@ -71,7 +116,7 @@ def load_shard(filepath: str, rank: int, world: int, device: str = "cuda") -> Ci
             "leaf_offsets": np.zeros(Cs, np.int32), "leaf_sizes": np.zeros(Cs, np.int32),
         }
         cur = 0
-        for i, (p, ks) in enumerate(zip(roots, kids)):
+        for i, ks in enumerate(kids):
             for j, c in enumerate(ks):
                 g = i * cpr + j
                 o, n = int(offsets[c]), int(sizes[c])
@@ -91,9 +136,13 @@ def load_shard(filepath: str, rank: int, world: int, device: str = "cuda") -> Ci
     finally:
         mm.close()
     if Rs == 0:
-        raise ValueError(f"rank {rank} owns no roots (world {world} > non-empty roots)")
-    return CircuitIndex(root_centers=centers, root_radii=radii, bases=bases, leaf_vectors=leaf, original_ids=ids,
-                        dim=D, rank=r, device=device, **new)
+        raise ValueError(f"rank {rank} owns no rows (world {world} > non-empty children)")
+    idx = CircuitIndex(root_centers=centers, root_radii=radii, bases=bases, leaf_vectors=leaf, original_ids=ids,
+                       dim=D, rank=r, device=device, **new)
+    idx.shard_info = {"rank": rank, "world": world, "part_root": roots.tolist(), "rows": n_rows,
+                      "rank_rows": plan["rank_rows"].tolist(), "parts_total": int(len(plan["part_root"])),
+                      "roots": R}
+    return idx
 
 
 def _aligned(q: torch.Tensor) -> torch.Tensor:

@@ -170,4 +170,91 @@ int circuit_plan_shards(const int64_t* root_rows, int num_roots, int world, int*
   return CIRCUIT_OK;
 }
 
+int circuit_plan_shard_parts(const int64_t* atom_rows, const int64_t* root_atom_ptr, int num_roots, int world,
+                             double max_imbalance, int* part_root, int64_t* part_atom_begin, int64_t* part_atom_end,
+                             int* part_rank, int max_parts, int* num_parts, int64_t* rank_rows) {
+  if (!atom_rows || !root_atom_ptr || !part_root || !part_atom_begin || !part_atom_end || !part_rank || !num_parts ||
+      num_roots < 1 || world < 1 || max_parts < 1 || !(max_imbalance >= 1.0)) {
+    cb::set_error("plan_shard_parts: bad arguments");
+    return CIRCUIT_ERR_ARG;
+  }
+  struct Item {
+    int64_t rows;
+    int root;
+    int64_t a0, a1;  // atom range
+  };
+  std::vector<Item> items;
+  int64_t total = 0;
+  for (int p = 0; p < num_roots; ++p) {
+    const int64_t a0 = root_atom_ptr[p], a1 = root_atom_ptr[p + 1];
+    if (a0 < 0 || a1 < a0) {
+      cb::set_error("plan_shard_parts: root_atom_ptr must be non-decreasing from 0");
+      return CIRCUIT_ERR_ARG;
+    }
+    int64_t r = 0;
+    for (int64_t a = a0; a < a1; ++a) {
+      if (atom_rows[a] < 0) {
+        cb::set_error("plan_shard_parts: negative atom size");
+        return CIRCUIT_ERR_ARG;
+      }
+      r += atom_rows[a];
+    }
+    if (r > 0) items.push_back({r, p, a0, a1});
+    total += r;
+  }
+  const double allowed = max_imbalance * (double)total / (double)world;
+  // largest first; ties by root (deterministic on every rank)
+  const auto before = [](const Item& x, const Item& y) { return x.rows != y.rows ? x.rows > y.rows : x.root < y.root; };
+  std::sort(items.begin(), items.end(), before);
+  std::vector<int64_t> load(world, 0);
+  struct Part {
+    int rank, root;
+    int64_t a0, a1;
+  };
+  std::vector<Part> parts;
+  size_t head = 0;
+  while (head < items.size()) {
+    const Item it = items[head++];
+    int r = 0;
+    for (int w = 1; w < world; ++w)
+      if (load[w] < load[r]) r = w;
+    if ((double)(load[r] + it.rows) <= allowed || it.a1 - it.a0 == 1) {
+      parts.push_back({r, it.root, it.a0, it.a1});
+      load[r] += it.rows;
+      continue;
+    }
+    // the longest prefix of atoms that fits (at least one atom)
+    int64_t a = it.a0, taken = 0;
+    while (a < it.a1 && (double)(load[r] + taken + atom_rows[a]) <= allowed) taken += atom_rows[a++];
+    if (a == it.a0) taken += atom_rows[a++];
+    parts.push_back({r, it.root, it.a0, a});
+    load[r] += taken;
+    Item rest{it.rows - taken, it.root, a, it.a1};
+    if (rest.rows > 0 || rest.a1 > rest.a0) {
+      // keep the pending items sorted: insert the remainder at its place
+      auto pos = std::lower_bound(items.begin() + head, items.end(), rest, before);
+      items.insert(pos, rest);
+    }
+  }
+  std::sort(parts.begin(), parts.end(), [](const Part& x, const Part& y) {
+    if (x.rank != y.rank) return x.rank < y.rank;
+    if (x.root != y.root) return x.root < y.root;
+    return x.a0 < y.a0;
+  });
+  *num_parts = (int)parts.size();
+  if ((int)parts.size() > max_parts) {
+    cb::set_error("plan_shard_parts: more parts than max_parts");
+    return CIRCUIT_ERR_ARG;
+  }
+  for (size_t i = 0; i < parts.size(); ++i) {
+    part_root[i] = parts[i].root;
+    part_atom_begin[i] = parts[i].a0;
+    part_atom_end[i] = parts[i].a1;
+    part_rank[i] = parts[i].rank;
+  }
+  if (rank_rows)
+    for (int w = 0; w < world; ++w) rank_rows[w] = load[w];
+  return CIRCUIT_OK;
+}
+
 }  // extern "C"

@@ -39,6 +39,27 @@ int circuit_merge_topk_batch(const float* scores, const int* ids, int num_querie
  * written; rank_rows[world] (optional) receives each rank's total rows. */
 int circuit_plan_shards(const int64_t* root_rows, int num_roots, int world, int* root_to_rank, int64_t* rank_rows);
 
+/* Host-only shard plan that splits oversized roots (no reference counterpart).
+ * Root p's rows come as the ordered atoms atom_rows[root_atom_ptr[p] ..
+ * root_atom_ptr[p + 1]) -- its children in leaf order, or fixed blocks of rows
+ * for a builder that has not clustered children yet; root_atom_ptr has
+ * num_roots + 1 entries.  Roots are taken largest first and placed whole on the
+ * least-loaded rank when that keeps it within max_imbalance x (total rows /
+ * world); otherwise the root is cut between atoms: the least-loaded rank takes
+ * the longest prefix that fits (at least one atom) and the rest is planned
+ * again.  Every part is a contiguous atom range of one root; a split root's
+ * centre and basis are shared by its parts.  A rank exceeds the limit only by
+ * less than one atom.  Writes up to max_parts parts (part_root, part_atom_begin,
+ * part_atom_end, part_rank), ordered by (rank, root, first atom); *num_parts
+ * receives the count; rank_rows[world] (optional) each rank's rows.  With
+ * max_imbalance > 1 every split fills a rank, so there are about num_roots +
+ * world parts; when max_parts is too small the call returns CIRCUIT_ERR_ARG
+ * with *num_parts set to the number needed (num_roots + total atoms always
+ * suffices). */
+int circuit_plan_shard_parts(const int64_t* atom_rows, const int64_t* root_atom_ptr, int num_roots, int world,
+                             double max_imbalance, int* part_root, int64_t* part_atom_begin, int64_t* part_atom_end,
+                             int* part_rank, int max_parts, int* num_parts, int64_t* rank_rows);
+
 #ifdef __cplusplus
 }
 #endif

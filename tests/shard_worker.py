@@ -84,3 +84,26 @@ def search_worker(rank, world, port, root, index_path, queries_path, out_path, k
         dist.destroy_process_group()
     except Exception:
         pass
+
+
+def build_worker(rank, world, port, root, n, out_path):
+    """Builds this rank's shard of a small clustered corpus with the
+    shard-aware streaming builder (gloo collectives: broadcast of the root
+    centres, all-gather of the row labels) and saves it."""
+    _paths(root)
+    import datetime
+
+    import torch.distributed as dist
+
+    from circuit_rag.hierarchy.build import build_circuit_index_streaming
+    from circuit_rag.synthetic import WORKLOADS
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+    w = WORKLOADS["zipf-10m"]
+    idx = build_circuit_index_streaming(lambda s, e: w.corpus(s, e), n, w.dim, 12, 4, 6, device="cpu",
+                                        chunk=1500, sample=4000, shard_rank=rank, world=world, block_rows=16)
+    idx.save(out_path)
+    with open(out_path + ".json", "w") as f:
+        json.dump(idx.shard_info, f)
+    dist.destroy_process_group()
