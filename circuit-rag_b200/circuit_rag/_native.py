@@ -42,6 +42,7 @@ EXPORTED_SYMBOLS = (
     "circuit_merge_topk_batch",
     "circuit_plan_shards",
     "circuit_plan_shard_parts",
+    "circuit_load_shard",
     "circuit_flat_search_noalloc",
     "circuit_selftest_wait_timeout",
     "circuit_selftest_batch_wait_timeout",
@@ -114,6 +115,7 @@ def _declare(lib):
         "circuit_merge_topk_batch": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P]),
         "circuit_plan_shards": (_I, [_P, _I, _I, _P, _P]),
         "circuit_plan_shard_parts": (_I, [_P, _P, _I, _I, ctypes.c_double, _P, _P, _P, _P, _I, _P, _P]),
+        "circuit_load_shard": (_P, [ctypes.c_char_p, _I, _I, _I, ctypes.c_double]),
         "circuit_flat_search_noalloc": (_I, [_P, _I64, _I, _P, _I, _P, _P, _P]),
         "circuit_search_batch_async": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _P]),
         "circuit_search_seed_async": (_I, [_P, _P, _I, _P, _P]),

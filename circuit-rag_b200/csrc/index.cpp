@@ -24,6 +24,7 @@
 #include <vector>
 
 #include "../../include/circuit.h"
+#include "../../include/circuit_shard.h"
 #include "engine.h"
 #include "index_internal.h"
 #include "json_min.h"
@@ -234,10 +235,57 @@ struct TensorInfo {
   std::vector<int64_t> shape;
   int64_t offset = 0, nbytes = 0;
 };
+
+// Host -> device copies through two pinned 64 MiB staging buffers: the memcpy
+// into one buffer overlaps the DMA out of the other.
+class StagedUpload {
+ public:
+  explicit StagedUpload(cudaStream_t st) : st_(st) {
+    ok_ = cuda_ok(cudaMallocHost(&stage_[0], kChunk), "cudaMallocHost(stage)") &&
+          cuda_ok(cudaMallocHost(&stage_[1], kChunk), "cudaMallocHost(stage)") &&
+          cuda_ok(cudaEventCreateWithFlags(&done_[0], cudaEventDisableTiming), "cudaEventCreate") &&
+          cuda_ok(cudaEventCreateWithFlags(&done_[1], cudaEventDisableTiming), "cudaEventCreate");
+  }
+  ~StagedUpload() {
+    for (int i = 0; i < 2; ++i) {
+      if (done_[i]) cudaEventDestroy(done_[i]);
+      if (stage_[i]) cudaFreeHost(stage_[i]);
+    }
+  }
+  // copies [src, src + bytes) to dst (device)
+  bool put(void* dst, const char* src, size_t bytes) {
+    size_t pos = 0;
+    while (ok_ && pos < bytes) {
+      const size_t n = std::min(bytes - pos, kChunk);
+      if (used_[slot_]) ok_ = cuda_ok(cudaEventSynchronize(done_[slot_]), "staging wait");
+      if (!ok_) break;
+      std::memcpy(stage_[slot_], src + pos, n);
+      ok_ = cuda_ok(cudaMemcpyAsync((char*)dst + pos, stage_[slot_], n, cudaMemcpyHostToDevice, st_), "H2D") &&
+            cuda_ok(cudaEventRecord(done_[slot_], st_), "cudaEventRecord");
+      used_[slot_] = true;
+      slot_ ^= 1;
+      pos += n;
+    }
+    return ok_;
+  }
+  bool finish() { return ok_ && cuda_ok(cudaStreamSynchronize(st_), "upload"); }
+
+ private:
+  static constexpr size_t kChunk = 64ull << 20;
+  cudaStream_t st_;
+  void* stage_[2] = {nullptr, nullptr};
+  cudaEvent_t done_[2] = {nullptr, nullptr};
+  bool used_[2] = {false, false};
+  int slot_ = 0;
+  bool ok_ = false;
+};
 }  // namespace
 
-bool circuit_index_opaque::load_file(const char* path, int dev) {
-  device = dev;
+// Maps the file, parses and validates the header and the tensor table, and
+// copies out the child tables; sets D, rank, R, C, N.  No device work.
+bool circuit_index_opaque::parse_file(const char* path, void* tinfo, std::vector<int>* parent,
+                                      std::vector<int>* offsets, std::vector<int>* sizes) {
+  TensorInfo* ti = static_cast<TensorInfo*>(tinfo);
   if (!path) { set_error("null path"); return false; }
   fd = open(path, O_RDONLY);
   if (fd < 0) { set_error(std::string("cannot open ") + path); return false; }
@@ -269,7 +317,6 @@ bool circuit_index_opaque::load_file(const char* path, int dev) {
   const int64_t expect_numel[11] = {(int64_t)R * D, R, (int64_t)R * D * rank, (int64_t)C * rank, (int64_t)C * rank,
                                     C, C, C, C, (int64_t)N * D, N};
   const bool is_int[11] = {false, false, false, false, false, false, true, true, true, false, true};
-  TensorInfo ti[11];
   for (int t = 0; t < 11; ++t) {
     const cb::json::Value* e = tm->get(kTensorNames[t]);
     if (!e || e->kind != cb::json::Value::Object) { set_error(std::string("tensor_meta lacks ") + kTensorNames[t]); return false; }
@@ -300,18 +347,34 @@ bool circuit_index_opaque::load_file(const char* path, int dev) {
       return false;
     }
   }
-  // validate the child tables on the host copy before any device work.  The
-  // file only guarantees 4-byte alignment of tensor data (offsets are 12 mod
-  // 64 with the reference writer), so copy the small int arrays out first.
-  std::vector<int> parent(C), offsets(C), sizes(C);
-  std::memcpy(parent.data(), base + ti[6].offset, 4 * (size_t)C);
-  std::memcpy(offsets.data(), base + ti[7].offset, 4 * (size_t)C);
-  std::memcpy(sizes.data(), base + ti[8].offset, 4 * (size_t)C);
-  {
+  // the file only guarantees 4-byte alignment of tensor data (offsets are 12
+  // mod 64 with the reference writer), so the small int arrays are copied out
+  parent->resize(C);
+  offsets->resize(C);
+  sizes->resize(C);
+  std::memcpy(parent->data(), base + ti[6].offset, 4 * (size_t)C);
+  std::memcpy(offsets->data(), base + ti[7].offset, 4 * (size_t)C);
+  std::memcpy(sizes->data(), base + ti[8].offset, 4 * (size_t)C);
+  return true;
+}
+
+void circuit_index_opaque::unmap_file() {
+  if (map_ptr) munmap(map_ptr, map_size);
+  map_ptr = nullptr;
+  if (fd >= 0) close(fd);
+  fd = -1;
+}
+
+bool circuit_index_opaque::load_file(const char* path, int dev) {
+  device = dev;
+  TensorInfo ti[11];
+  std::vector<int> parent, offsets, sizes;
+  if (!parse_file(path, ti, &parent, &offsets, &sizes)) return false;
+  {  // validate the child tables on the host before any device work
     std::vector<int> p0, l0, r0;
     if (!build_host_tables(parent.data(), offsets.data(), sizes.data(), &p0, &l0, &r0)) return false;
   }
-  // the file is valid: only now touch the device
+  const char* base = static_cast<const char*>(map_ptr);
   if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice")) return false;
   if (!cuda_ok(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate")) return false;
   void* dptr[11];
@@ -319,38 +382,12 @@ bool circuit_index_opaque::load_file(const char* path, int dev) {
     dptr[t] = dev_alloc((size_t)ti[t].nbytes, "cudaMalloc(index tensor)");
     if (!dptr[t]) return false;
   }
-  // upload: pinned double-buffered staging in 64 MiB chunks
-  const size_t CH = 64ull << 20;
-  void* stage[2] = {nullptr, nullptr};
-  cudaEvent_t done[2] = {nullptr, nullptr};
-  bool ok = cuda_ok(cudaMallocHost(&stage[0], CH), "cudaMallocHost(stage)") &&
-            cuda_ok(cudaMallocHost(&stage[1], CH), "cudaMallocHost(stage)") &&
-            cuda_ok(cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming), "cudaEventCreate") &&
-            cuda_ok(cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming), "cudaEventCreate");
-  int slot = 0;
-  bool used[2] = {false, false};
-  for (int t = 0; t < 11 && ok; ++t) {
-    const char* src = base + ti[t].offset;
-    size_t left = (size_t)ti[t].nbytes, pos = 0;
-    while (left > 0 && ok) {
-      const size_t n = std::min(left, CH);
-      if (used[slot]) ok = cuda_ok(cudaEventSynchronize(done[slot]), "staging wait");
-      if (!ok) break;
-      std::memcpy(stage[slot], src + pos, n);
-      ok = cuda_ok(cudaMemcpyAsync((char*)dptr[t] + pos, stage[slot], n, cudaMemcpyHostToDevice, stream), "H2D tensor") &&
-           cuda_ok(cudaEventRecord(done[slot], stream), "cudaEventRecord");
-      used[slot] = true;
-      slot ^= 1;
-      pos += n;
-      left -= n;
-    }
+  {
+    StagedUpload up(stream);
+    for (int t = 0; t < 11; ++t)
+      if (!up.put(dptr[t], base + ti[t].offset, (size_t)ti[t].nbytes)) return false;
+    if (!up.finish()) return false;
   }
-  if (ok) ok = cuda_ok(cudaStreamSynchronize(stream), "upload");
-  for (int i = 0; i < 2; ++i) {
-    if (done[i]) cudaEventDestroy(done[i]);
-    if (stage[i]) cudaFreeHost(stage[i]);
-  }
-  if (!ok) return false;
   view.root_centers = (const float*)dptr[0];
   view.root_radii = (const float*)dptr[1];
   view.bases = (const float*)dptr[2];
@@ -362,12 +399,140 @@ bool circuit_index_opaque::load_file(const char* path, int dev) {
   view.leaf_sizes = (const int*)dptr[8];
   view.leaf = (const float*)dptr[9];
   view.original_ids = (const int*)dptr[10];
-  // the mapping is no longer needed once everything is on the device
-  munmap(map_ptr, map_size);
-  map_ptr = nullptr;
-  close(fd);
-  fd = -1;
+  unmap_file();  // everything is on the device
   return finish_setup(parent.data(), offsets.data(), sizes.data());
+}
+
+// One rank's shard of a .circuit file: the parts of circuit_plan_shard_parts
+// (children of each root in leaf order as atoms) that `rk` of `world` owns.
+// Each part becomes a root of this index (the file root's centre, radius and
+// basis; a contiguous range of its children); only those byte ranges of the
+// file are read.  Original ids stay global.
+bool circuit_index_opaque::load_shard_file(const char* path, int dev, int rk, int world, double max_imbalance) {
+  device = dev;
+  if (world < 1 || rk < 0 || rk >= world || !(max_imbalance >= 1.0)) {
+    set_error("load_shard: need 0 <= rank < world and max_imbalance >= 1");
+    return false;
+  }
+  TensorInfo ti[11];
+  std::vector<int> parent, offsets, sizes;
+  if (!parse_file(path, ti, &parent, &offsets, &sizes)) return false;
+  std::vector<int> ptr, list, rows;
+  if (!build_host_tables(parent.data(), offsets.data(), sizes.data(), &ptr, &list, &rows)) return false;
+  const int R0 = R, C0 = C, N0 = N;
+  (void)C0;
+  (void)N0;
+  // plan over the children of each root (CSR order = leaf order)
+  std::vector<int64_t> atom_rows(list.size()), atom_ptr(R0 + 1);
+  for (size_t i = 0; i < list.size(); ++i) atom_rows[i] = sizes[list[i]];
+  for (int p = 0; p <= R0; ++p) atom_ptr[p] = ptr[p];
+  int cap = R0 + 2 * world + 8, np = 0;
+  std::vector<int> proot, prank;
+  std::vector<int64_t> pa0, pa1;
+  for (int attempt = 0; attempt < 2; ++attempt) {
+    proot.assign(cap, 0); prank.assign(cap, 0); pa0.assign(cap, 0); pa1.assign(cap, 0);
+    const int rc = circuit_plan_shard_parts(atom_rows.data(), atom_ptr.data(), R0, world, max_imbalance, proot.data(),
+                                            pa0.data(), pa1.data(), prank.data(), cap, &np, nullptr);
+    if (rc == CIRCUIT_OK) break;
+    if (np <= cap || attempt == 1) return false;
+    cap = np;
+  }
+  std::vector<int> own;
+  for (int i = 0; i < np; ++i)
+    if (prank[i] == rk) own.push_back(i);
+  if (own.empty()) {
+    set_error("load_shard: this rank owns no rows (more ranks than children)");
+    return false;
+  }
+  const int Rs = (int)own.size();
+  int cpr = 1;
+  int64_t Ns = 0;
+  for (int i : own) {
+    cpr = std::max(cpr, (int)(pa1[i] - pa0[i]));
+    for (int64_t a = pa0[i]; a < pa1[i]; ++a) Ns += atom_rows[a];
+  }
+  const int Cs = Rs * cpr;
+  const char* base = static_cast<const char*>(map_ptr);
+  const float* f_centers = reinterpret_cast<const float*>(base + ti[0].offset);
+  const float* f_radii = reinterpret_cast<const float*>(base + ti[1].offset);
+  const float* f_bases = reinterpret_cast<const float*>(base + ti[2].offset);
+  const float* f_l = reinterpret_cast<const float*>(base + ti[3].offset);
+  const float* f_u = reinterpret_cast<const float*>(base + ti[4].offset);
+  const float* f_crad = reinterpret_cast<const float*>(base + ti[5].offset);
+  // the shard's small arrays on the host (memcpy: file data is only 4-byte aligned)
+  std::vector<float> centers((size_t)Rs * D), radii(Rs), bases((size_t)Rs * D * rank), cl((size_t)Cs * rank, 0.f),
+      cu((size_t)Cs * rank, 0.f), crad(Cs, 0.f);
+  std::vector<int> cpar(Cs), coff(Cs, 0), csz(Cs, 0);
+  struct Span {
+    int64_t src_row, dst_row, n;
+  };
+  std::vector<Span> spans;
+  int64_t cur = 0;
+  for (int j = 0; j < Rs; ++j) {
+    const int i = own[j], p = proot[i];
+    std::memcpy(&centers[(size_t)j * D], f_centers + (size_t)p * D, sizeof(float) * D);
+    std::memcpy(&radii[j], f_radii + p, sizeof(float));
+    std::memcpy(&bases[(size_t)j * D * rank], f_bases + (size_t)p * D * rank, sizeof(float) * (size_t)D * rank);
+    for (int c = 0; c < cpr; ++c) cpar[(size_t)j * cpr + c] = j;
+    for (int64_t a = pa0[i]; a < pa1[i]; ++a) {
+      const int c = list[a], g = j * cpr + (int)(a - pa0[i]);
+      std::memcpy(&cl[(size_t)g * rank], f_l + (size_t)c * rank, sizeof(float) * rank);
+      std::memcpy(&cu[(size_t)g * rank], f_u + (size_t)c * rank, sizeof(float) * rank);
+      std::memcpy(&crad[g], f_crad + c, sizeof(float));
+      coff[g] = (int)cur;
+      csz[g] = sizes[c];
+      if (!spans.empty() && spans.back().src_row + spans.back().n == offsets[c] &&
+          spans.back().dst_row + spans.back().n == cur)
+        spans.back().n += sizes[c];  // adjacent in the file and in the shard: one copy
+      else
+        spans.push_back({offsets[c], cur, sizes[c]});
+      cur += sizes[c];
+    }
+  }
+  R = Rs;
+  C = Cs;
+  N = (int)Ns;
+  if (!check_dims()) return false;
+  if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice")) return false;
+  if (!cuda_ok(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate")) return false;
+  const size_t sz[11] = {centers.size() * 4, radii.size() * 4, bases.size() * 4, cl.size() * 4, cu.size() * 4,
+                         crad.size() * 4, cpar.size() * 4, coff.size() * 4, csz.size() * 4,
+                         (size_t)Ns * D * 4, (size_t)Ns * 4};
+  void* dptr[11];
+  for (int t = 0; t < 11; ++t) {
+    dptr[t] = dev_alloc(sz[t], "cudaMalloc(shard tensor)");
+    if (!dptr[t]) return false;
+  }
+  {
+    StagedUpload up(stream);
+    const void* small[9] = {centers.data(), radii.data(), bases.data(), cl.data(), cu.data(),
+                            crad.data(), cpar.data(), coff.data(), csz.data()};
+    for (int t = 0; t < 9; ++t)
+      if (!up.put(dptr[t], static_cast<const char*>(small[t]), sz[t])) return false;
+    const char* leaf_src = base + ti[9].offset;
+    const char* ids_src = base + ti[10].offset;
+    const size_t rb = (size_t)D * 4;
+    for (const Span& sp : spans) {
+      if (!up.put((char*)dptr[9] + sp.dst_row * rb, leaf_src + sp.src_row * rb, (size_t)sp.n * rb) ||
+          !up.put((char*)dptr[10] + sp.dst_row * 4, ids_src + sp.src_row * 4, (size_t)sp.n * 4))
+        return false;
+    }
+    if (!up.finish()) return false;
+  }
+  view.root_centers = (const float*)dptr[0];
+  view.root_radii = (const float*)dptr[1];
+  view.bases = (const float*)dptr[2];
+  view.child_l = (const float*)dptr[3];
+  view.child_u = (const float*)dptr[4];
+  view.child_radii = (const float*)dptr[5];
+  view.child_parent = (const int*)dptr[6];
+  view.leaf_offsets = (const int*)dptr[7];
+  view.leaf_sizes = (const int*)dptr[8];
+  view.leaf = (const float*)dptr[9];
+  view.original_ids = (const int*)dptr[10];
+  unmap_file();
+  shard_rows_read = Ns;
+  return finish_setup(cpar.data(), coff.data(), csz.data());
 }
 
 bool circuit_index_opaque::wrap_device(int dev, int dim, int rnk, int nr, int nc, int64_t n, const float* const* f,
@@ -764,6 +929,17 @@ circuit_index_t circuit_load_index(const char* filepath, int device_id) {
   auto* idx = new (std::nothrow) circuit_index_opaque();
   if (!idx) { set_error("out of host memory"); return nullptr; }
   if (!idx->load_file(filepath, device_id)) {
+    idx->release();
+    delete idx;
+    return nullptr;
+  }
+  return idx;
+}
+
+circuit_index_t circuit_load_shard(const char* filepath, int rank, int world, int device_id, double max_imbalance) {
+  auto* idx = new (std::nothrow) circuit_index_opaque();
+  if (!idx) { set_error("out of host memory"); return nullptr; }
+  if (!idx->load_shard_file(filepath, device_id, rank, world, max_imbalance)) {
     idx->release();
     delete idx;
     return nullptr;

@@ -70,7 +70,12 @@ struct circuit_index_opaque {
   bool build_host_tables(const int* parent, const int* offsets, const int* sizes, std::vector<int>* ptr,
                          std::vector<int>* list, std::vector<int>* rows);
   bool finish_setup(const int* parent, const int* offsets, const int* sizes);
+  bool parse_file(const char* path, void* tensor_info, std::vector<int>* parent, std::vector<int>* offsets,
+                  std::vector<int>* sizes);
+  void unmap_file();
   bool load_file(const char* path, int dev);
+  bool load_shard_file(const char* path, int dev, int rk, int world, double max_imbalance);
+  int64_t shard_rows_read = 0;
   bool wrap_device(int dev, int dim, int rnk, int nr, int nc, int64_t n, const float* const* f, const int* const* ints);
   int search_async(const float* dq, int k, int64_t min_hier, float* dscores, int* dids, int64_t* drows,
                    cudaStream_t st, cudaEvent_t e0, cudaEvent_t e1);

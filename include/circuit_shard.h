@@ -60,6 +60,19 @@ int circuit_plan_shard_parts(const int64_t* atom_rows, const int64_t* root_atom_
                              double max_imbalance, int* part_root, int64_t* part_atom_begin, int64_t* part_atom_end,
                              int* part_rank, int max_parts, int* num_parts, int64_t* rank_rows);
 
+/* Load rank `rank` of `world`'s shard of a .circuit file onto `device_id`
+ * (NULL on failure, circuit_last_error() says why).  The plan is
+ * circuit_plan_shard_parts over each root's children in leaf order with the
+ * given max_imbalance (e.g. 1.05), identical on every rank; every part the
+ * rank owns becomes a root of the returned index with the file root's centre,
+ * radius and basis and a contiguous range of its children.  Only those parts'
+ * byte ranges of the file are read (mmap + pinned double-buffered staging;
+ * adjacent children are copied as one range); original ids stay global, so
+ * per-shard results merge with circuit_merge_topk.  Search it like any index.
+ * Multi-GPU counterpart of circuit_load_index (reference gpu_index.cpp:50-141
+ * loads the whole file). */
+circuit_index_t circuit_load_shard(const char* filepath, int rank, int world, int device_id, double max_imbalance);
+
 #ifdef __cplusplus
 }
 #endif

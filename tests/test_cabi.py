@@ -98,3 +98,20 @@ def test_loader_rejects_overlapping_children(tmp_path):
     assert not _native.lib().circuit_load_index(str(p).encode(), 0)
     err = _native.last_error()
     assert "overlap" in err or "cover" in err
+
+
+def test_shard_loader_rejects_bad_arguments_before_any_cuda_call(tmp_path):
+    """circuit_load_shard validates rank / world and the file before touching a device."""
+    import ctypes
+
+    from circuit_rag import _native
+
+    L = _native.lib()
+    assert not L.circuit_load_shard(b"/nonexistent.circuit", 0, 2, 0, 1.05)
+    assert "cannot open" in _native.last_error()
+    assert not L.circuit_load_shard(b"/nonexistent.circuit", 2, 2, 0, 1.05)
+    assert "rank" in _native.last_error()
+    p = tmp_path / "bad.circuit"
+    p.write_bytes(b"NOTCIRC1" + b"\0" * 64)
+    assert not L.circuit_load_shard(str(p).encode(), 0, 2, 0, 1.05)
+    assert "magic" in _native.last_error()
