@@ -1,9 +1,10 @@
 """Generate the golden fixtures under tests/golden/ by running the REFERENCE package.
 
 Run from the repository root, in a container where the reference checkout is
-mounted (this script is the only committed file that reads it):
+mounted, with that checkout on PYTHONPATH (this script is the only committed
+file that imports it):
 
-    PYTHONPATH=/root/reference python tests/golden/make_golden.py
+    PYTHONPATH=$CIRCUIT_REF_DIR python tests/golden/make_golden.py
 
 What it pins (all produced by the reference's own code, on CPU):
 
