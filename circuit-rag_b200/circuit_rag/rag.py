@@ -52,21 +52,26 @@ class CircuitRAG:
         nearest root, new child, certificates recomputed) until the appended
         rows exceed REBUILD_FRACTION of the rows of the last full build; then
         the index is rebuilt with the reference's size rule (rag.py:47-55)."""
-        metadatas = metadatas or [{} for _ in texts]
-        if len(metadatas) != len(texts):
+        texts = list(texts)
+        if metadatas is None:
+            metadatas = [{} for _ in range(len(texts))]
+        elif len(metadatas) != len(texts):
             raise ValueError("metadatas must be the same length as texts")
-        vecs = np.asarray(self._embed(list(texts)), dtype=np.float32)
-        first = len(self.texts)
-        self.texts += list(texts)
-        self.metadatas += list(metadatas)
-        self._vectors = vecs if self._vectors is None else np.vstack([self._vectors, vecs])
+        new_vecs = np.asarray(self._embed(texts), dtype=np.float32)
+        start_id = len(self.texts)
+        self.texts.extend(texts)
+        self.metadatas.extend(metadatas)
+        if self._vectors is None:
+            self._vectors = new_vecs
+        else:
+            self._vectors = np.concatenate([self._vectors, new_vecs], axis=0)
         n = len(self._vectors)
         if self.index is not None and (n - self._built_n) <= self.REBUILD_FRACTION * self._built_n:
-            self.index.append(vecs, np.arange(first, n, dtype=np.int32))
+            self.index.append(new_vecs, np.arange(start_id, n, dtype=np.int32))
             self.appended_rows = n - self._built_n
         else:
             self._rebuild()
-        return list(range(first, n))
+        return list(range(start_id, n))
 
     def _rebuild(self):
         n = len(self._vectors)
