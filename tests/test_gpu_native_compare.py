@@ -45,7 +45,8 @@ def test_native_library_against_the_reference_library(tmp_path, name):
     p = subprocess.run([HARNESS, _native.LIB_PATH, REF_SO, path, qpath, str(nq), str(w.dim), str(k), out],
                        capture_output=True, text=True, timeout=600)
     assert p.returncode == 0, p.stderr
-    rows = {json.loads(line)["lib"]: json.loads(line) for line in p.stdout.strip().splitlines()}
+    # the reference library prints its own progress lines to stdout as well
+    rows = {json.loads(line)["lib"]: json.loads(line) for line in p.stdout.splitlines() if line.startswith('{"lib"')}
     res = {}
     for lib in ("ours", "reference"):
         s = np.fromfile(f"{out}.{lib}.scores", np.float32).reshape(nq, k)
