@@ -62,8 +62,10 @@ struct SearchCtrl {
   float qn2;                       // fl(sum q_i^2)
   int best_root;
   int error;                       // cb::ERR_* bits
-  uint32_t pad[8];
+  uint32_t call_seq;               // blocking calls: the call's sequence number (see HostIO)
+  uint32_t pad[7];
 };
+constexpr int CTRL_SEQ_WORD = 8;   // 64-bit word of the header whose low half is call_seq
 constexpr size_t CTRL_RESET_BYTES = 96;
 static_assert(sizeof(SearchCtrl) == CTRL_RESET_BYTES, "ctrl layout");
 
@@ -110,11 +112,19 @@ struct Workspace {
 // out_scores / out_ids, or, with slots, to the device pointers slots[1] /
 // slots[2] (staged in out_indirect by the start kernel), and a copy of the
 // control header to ctrl_out.  No copy-engine operation remains in the graph.
+//
+// Completion: the host writes the call's sequence number to seq_in before the
+// launch; the start kernel copies it into the control header, and the final
+// merge, after its results and the header copy, writes it to done_out (mapped
+// host memory, system-scope fence first).  The blocking call returns once it
+// sees its number there, without waiting for the stream's completion report.
 struct HostIO {
   const float* q_host;               // [D] or null
   void* const* slots;                // {query, scores, ids} device pointers, or null
   void** out_indirect;               // [2]
   SearchCtrl* ctrl_out;              // receives the first CTRL_RESET_BYTES
+  const uint32_t* seq_in;            // mapped host word: this call's sequence number
+  uint32_t* done_out;                // mapped host word: set to it when the results are out
 };
 
 // ---- launchers (search_kernels.cu); all asynchronous on `stream` ----

@@ -189,19 +189,25 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
   // pinned, device-mapped host staging for the blocking search: query, scores,
   // ids, ctrl header, call slots.  Graph replays read the query from it and
   // write the results into it from the kernels themselves.
-  const size_t pin_bytes =
-      sizeof(float) * D + (sizeof(float) + sizeof(int)) * cb::KMAX + sizeof(cb::SearchCtrl) + 4 * sizeof(void*);
+  const size_t pin_bytes = sizeof(float) * D + (sizeof(float) + sizeof(int)) * cb::KMAX + sizeof(cb::SearchCtrl) +
+                           4 * sizeof(void*) + 2 * sizeof(uint32_t);
   if (!cuda_ok(cudaHostAlloc(&h_pinned, pin_bytes, cudaHostAllocMapped), "cudaHostAlloc")) return false;
   h_query = (float*)h_pinned;
   h_scores = h_query + D;
   h_ids = (int*)(h_scores + cb::KMAX);
   h_ctrl = (cb::SearchCtrl*)(h_ids + cb::KMAX);
   h_slots = (void**)(h_ctrl + 1);
+  h_seq = (volatile uint32_t*)(h_slots + 4);
+  h_done = h_seq + 1;
+  *h_seq = 0;
+  *h_done = 0;
   void* d_pinned = nullptr;
   if (!cuda_ok(cudaHostGetDevicePointer(&d_pinned, h_pinned, 0), "cudaHostGetDevicePointer")) return false;
   const auto alias = [&](const void* h) { return (char*)d_pinned + ((const char*)h - (const char*)h_pinned); };
-  io_host = cb::HostIO{(const float*)alias(h_query), nullptr, dev_out_indirect, (cb::SearchCtrl*)alias(h_ctrl)};
-  io_device = cb::HostIO{nullptr, (void* const*)alias(h_slots), dev_out_indirect, (cb::SearchCtrl*)alias(h_ctrl)};
+  io_host = cb::HostIO{(const float*)alias(h_query), nullptr, dev_out_indirect, (cb::SearchCtrl*)alias(h_ctrl),
+                       (const uint32_t*)alias((const void*)h_seq), (uint32_t*)alias((const void*)h_done)};
+  io_device = cb::HostIO{nullptr, (void* const*)alias(h_slots), dev_out_indirect, (cb::SearchCtrl*)alias(h_ctrl),
+                         (const uint32_t*)alias((const void*)h_seq), (uint32_t*)alias((const void*)h_done)};
   map_scores = (float*)alias(h_scores);
   map_ids = (int*)alias(h_ids);
   if (!cuda_ok(cudaStreamSynchronize(stream), "index setup")) return false;
@@ -666,8 +672,9 @@ int circuit_index_opaque::search_blocking(const float* query, bool host_ptrs, in
         h_slots[1] = out_scores;
         h_slots[2] = out_ids;
       }
-      if (!cuda_ok(cudaGraphLaunch(g->second, stream), "graph launch") ||
-          !cuda_ok(cudaStreamSynchronize(stream), "search sync"))
+      const uint32_t seq = ++call_counter;
+      *h_seq = seq;
+      if (!cuda_ok(cudaGraphLaunch(g->second, stream), "graph launch") || !wait_for_results(seq))
         return CIRCUIT_ERR_CUDA;
       last_stream = stream;
       last_path = hier;
@@ -693,6 +700,30 @@ int circuit_index_opaque::search_blocking(const float* query, bool host_ptrs, in
       !cuda_ok(cudaStreamSynchronize(stream), "search sync"))
     return CIRCUIT_ERR_CUDA;
   return finish_blocking(host_ptrs, k, out_scores, out_ids, trace, t0);
+}
+
+// Waits for a graph-replayed blocking search: spins on the completion word the
+// final merge writes into the mapped block (its results are out when it appears),
+// checking the stream's status every few dozen polls; after kSpinLimitUs it falls
+// back to cudaStreamSynchronize, so a long scan does not hold a core for its
+// whole duration.  A stream that ends without the word (an error) is synchronised
+// to report it.
+bool circuit_index_opaque::wait_for_results(uint32_t seq) {
+  constexpr double kSpinLimitUs = 200.0;
+  const auto t0 = std::chrono::steady_clock::now();
+  for (uint32_t polls = 1;; ++polls) {
+    if (*h_done == seq) return true;
+    if ((polls & 63) == 0) {
+      const cudaError_t q = cudaStreamQuery(stream);
+      if (q != cudaErrorNotReady) {
+        if (q != cudaSuccess) return cuda_ok(q, "search");
+        if (*h_done == seq) return true;
+        return cuda_ok(cudaStreamSynchronize(stream), "search sync");
+      }
+      if (std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count() > kSpinLimitUs)
+        return cuda_ok(cudaStreamSynchronize(stream), "search sync");
+    }
+  }
 }
 
 // End of a blocking search once its stream has synchronised: host results leave

@@ -37,6 +37,9 @@ struct circuit_index_opaque {
   int* h_ids = nullptr;
   cb::SearchCtrl* h_ctrl = nullptr;
   void** h_slots = nullptr;         // device-buffer calls: {query, scores, ids}
+  volatile uint32_t* h_seq = nullptr;   // mapped: the blocking call's sequence number
+  volatile uint32_t* h_done = nullptr;  // mapped: written by the final merge when the results are out
+  uint32_t call_counter = 0;
   bool have_host_ctrl = false;
   // device aliases of the mapped staging block (see cb::HostIO)
   void** dev_out_indirect = nullptr;
@@ -81,6 +84,7 @@ struct circuit_index_opaque {
                    cudaStream_t st, cudaEvent_t e0, cudaEvent_t e1);
   int search_blocking(const float* query, bool host_ptrs, int k, float* out_scores, int* out_ids,
                       circuit_trace_t* trace);
+  bool wait_for_results(uint32_t seq);
   int finish_blocking(bool host_ptrs, int k, float* out_scores, int* out_ids, circuit_trace_t* trace,
                       std::chrono::steady_clock::time_point t0);
   void fill_trace(const cb::SearchCtrl& c, circuit_trace_ex_t* t) const;

@@ -64,6 +64,8 @@ struct ScanParams {
   void* const* out_indirect;                  // final: {scores, ids} device pointers replacing out_scores / out_ids
   const unsigned long long* ctrl_hdr;         // final: control header, copied to ctrl_out after the merge
   unsigned long long* ctrl_out;               // (mapped host memory; null = no copy)
+  const uint32_t* call_seq;                   // blocking calls: the call's number in the control header
+  uint32_t* done_out;                         // mapped host word that receives it when the results are out
 };
 
 template <int VPL> struct ScanShape {
@@ -556,6 +558,13 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     block_select_topk<true>(P.cta_lists, M, k, sel, selN, scratch, s_theta);
     for (int i = tid; i < k; i += blockDim.x) emit(i, sel[i]);
   }
+  if (P.done_out) {
+    // every thread's results (and the header copy) reach the system before the
+    // completion word that the blocking caller spins on
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0) *reinterpret_cast<volatile uint32_t*>(P.done_out) = ld_volatile_u32(P.call_seq);
+  }
 }
 
 // ============================================================ search prologue
@@ -567,7 +576,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
 // for the final merge; with neither, only the header is cleared.  The kernels
 // after it are its programmatic dependents.
 __global__ void __launch_bounds__(128) k_search_prologue(const float4* q_host, void* const* slots, float4* dq, int D4,
-                                                         unsigned long long* ctrl_hdr, void** out_indirect) {
+                                                         unsigned long long* ctrl_hdr, void** out_indirect,
+                                                         const uint32_t* seq_in) {
   const int tid = threadIdx.x;
   const float4* src = q_host;
   if (slots) {
@@ -576,7 +586,8 @@ __global__ void __launch_bounds__(128) k_search_prologue(const float4* q_host, v
   }
   if (src)
     for (int i = tid; i < D4; i += blockDim.x) dq[i] = src[i];
-  if (tid < (int)(CTRL_RESET_BYTES / 8)) ctrl_hdr[tid] = 0ull;
+  if (tid < (int)(CTRL_RESET_BYTES / 8))
+    ctrl_hdr[tid] = (tid == CTRL_SEQ_WORD && seq_in) ? (unsigned long long)*seq_in : 0ull;
 }
 
 // ============================================================ root scan (K1)
@@ -1268,7 +1279,7 @@ static cudaError_t search_reset(const IndexView& ix, const Workspace& ws, const 
                                            io ? io->slots : nullptr,
                                            reinterpret_cast<float4*>(const_cast<float*>(q)), ix.D4,
                                            reinterpret_cast<unsigned long long*>(ws.ctrl),
-                                           io ? io->out_indirect : nullptr);
+                                           io ? io->out_indirect : nullptr, io ? io->seq_in : nullptr);
   return cudaGetLastError();
 }
 
@@ -1277,6 +1288,8 @@ static void final_io(ScanParams& M, const Workspace& ws, const HostIO* io) {
   M.out_indirect = io->slots ? io->out_indirect : nullptr;
   M.ctrl_hdr = reinterpret_cast<const unsigned long long*>(ws.ctrl);
   M.ctrl_out = reinterpret_cast<unsigned long long*>(io->ctrl_out);
+  M.call_seq = &ws.ctrl->call_seq;
+  M.done_out = io->done_out;
 }
 
 cudaError_t launch_search_seed(const IndexView& ix, const Workspace& ws, const float* q, int k, float* T_export,

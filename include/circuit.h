@@ -97,12 +97,18 @@ circuit_index_t circuit_load_index(const char* filepath, int device_id);
 /* Host query [dim] -> host out_scores[k] (descending), out_ids[k] (original ids).
  * Blocking.  From the second call with the same k (and path) the search replays a
  * CUDA graph: the kernels read the query from, and write the results into, the
- * handle's mapped pinned staging block (no copy-engine operation).
+ * handle's mapped pinned staging block (no copy-engine operation), and the call
+ * returns as soon as the final kernel has written them -- it polls a completion
+ * word in that block for up to 200 us, then waits on the stream -- so it needs no
+ * spin scheduling flag for low latency.
  * reference: circuit.h:25-32, gpu_index.cpp:242-330 */
 int circuit_search(circuit_index_t index, const float* query, int k, float* out_scores, int* out_ids,
                    circuit_trace_t* trace);
 
-/* Device query -> device outputs.  Blocking (synchronises the handle's stream).
+/* Device query -> device outputs.  Blocking: returns once the results are in the
+ * caller's buffers (the first calls synchronise the handle's stream; graph replays
+ * watch the completion word as above, so the kernel may still be retiring, and later
+ * work on the handle is ordered after it).
  * Graph replay as above when the query is 16-byte aligned, the outputs 4-byte
  * aligned and all three are device (or managed) memory of the index's device:
  * the kernels then read the query from, and write scores / ids to, the caller's
