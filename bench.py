@@ -61,9 +61,9 @@ METRIC = "queries/sec @k=10 on 100M x 384 fp32 (single-query exact search)"
 
 # DRAM bytes (read + write) per algorithmic byte of the main leaf scan, from one
 # ncu capture of that kernel on the 2,000,000-row case of this workload
-# (3.0637 GB read + 4.11 MB written for 3.047 GB of scanned rows); the scan's
+# (3.0702 GB read + 4.19 MB written for 3.070 GB of scanned rows); the scan's
 # traffic grows in proportion to the rows it reads, so a full launch is scaled by rows.
-SCAN_TRAFFIC_PER_ALG_BYTE = 1.007
+SCAN_TRAFFIC_PER_ALG_BYTE = 1.002
 CPU_SAMPLE_ROWS = 12_500_000  # one eighth of the 100M corpus (the per-GPU shard at 8 GPUs)
 TIE_ABS, SCORE_REL = 1e-6, 1e-5  # the parity rule: ids exact except ties within 1e-6, scores within 1e-5 rel
 
