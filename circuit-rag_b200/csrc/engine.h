@@ -39,6 +39,15 @@ class SmemOptIn {
 };
 
 constexpr int KMAX = 256;          // largest k a search accepts
+// Seed sample of a root: blocks of up to SEED_BLOCK consecutive rows starting at
+// evenly spaced positions among the root's rows (the first SEED_SAMPLE_MAX
+// children in leaf order), `want` rows in all: min(rows, max(4k, 128), 1024).
+// For k <= 32 (want = min(rows, 128)) the blocks are precomputed per root at
+// set-up: entry 0 = {blocks, rows sampled, 0, 0}, entries 1.. = {leaf row,
+// length, position in the sample, 0}.
+constexpr int SEED_SAMPLE_MAX = 1024;
+constexpr int SEED_BLOCK = 16;
+constexpr int SEED_TAB_W = 1 + 128 / SEED_BLOCK;
 constexpr int MAX_RANK = 64;       // largest rank r of a parent basis
 constexpr int MAX_DIM = 2048;      // largest vector dimension D (D % 4 == 0)
 constexpr int SCAN_CONSUMER_WARPS = 8;
@@ -86,6 +95,7 @@ struct IndexView {
   const int* root_child_ptr;    // [R+1]  CSR over non-empty children, grouped by parent
   const int* root_child_list;   // [nnz children]
   const int2* root_child_span;  // [nnz] per CSR entry: {leaf offset, first row within its root's rows}
+  const int4* seed_tab;         // [R * SEED_TAB_W] the seed sample of each root for k <= 32 (see below)
   const int* root_rows;         // [R]  leaf rows under each root
   const double* root_cn;        // [R]  upper bound of ||c_r||
   const double* root_defect;    // [R]  upper bound of ||V_r^T V_r - I||_2

@@ -144,20 +144,50 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
     }
   }
   int2* d_span = (int2*)dev_alloc(sizeof(int2) * span.size(), "cudaMalloc(root_child_span)");
+  // the seed sample of every root for k <= 32 (want = min(rows, 128)), with the
+  // same arithmetic as the root scan's on-device computation for larger k
+  std::vector<int4> tab((size_t)R * cb::SEED_TAB_W, make_int4(0, 0, 0, 0));
+  for (int p = 0; p < R; ++p) {
+    const int cb0 = ptr[p], nall = ptr[p + 1] - cb0;
+    const int nch = std::min(nall, cb::SEED_SAMPLE_MAX);
+    if (nch == 0) continue;
+    const int vrows = nall > nch ? span[cb0 + nch].y : rows[p];
+    const int want = std::min(std::min(vrows, 128), cb::SEED_SAMPLE_MAX);
+    const int nb = (want + cb::SEED_BLOCK - 1) / cb::SEED_BLOCK;
+    int pos = 0;
+    for (int b = 0; b < nb; ++b) {
+      const int v = (int)std::floor((double)b * (double)vrows / (double)nb);
+      const int v_next = (b + 1 < nb) ? (int)std::floor((double)(b + 1) * (double)vrows / (double)nb) : vrows;
+      int lo = 0, hi = nch - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (span[cb0 + mid].y <= v) lo = mid; else hi = mid - 1;
+      }
+      const int child_end = (lo + 1 < nch) ? span[cb0 + lo + 1].y : vrows;
+      const int len = std::min(std::min(cb::SEED_BLOCK, v_next - v), child_end - v);
+      tab[(size_t)p * cb::SEED_TAB_W + 1 + b] = make_int4(span[cb0 + lo].x + (v - span[cb0 + lo].y), len, pos, 0);
+      pos += len;
+    }
+    tab[(size_t)p * cb::SEED_TAB_W] = make_int4(nb, pos, 0, 0);
+  }
+  int4* d_tab = (int4*)dev_alloc(sizeof(int4) * tab.size(), "cudaMalloc(seed_tab)");
   double* d_cn = (double*)dev_alloc(sizeof(double) * R, "cudaMalloc(root_cn)");
   double* d_def = (double*)dev_alloc(sizeof(double) * R, "cudaMalloc(root_defect)");
-  if (!d_ptr || !d_list || !d_rows || !d_cn || !d_def || !d_span) return false;
+  if (!d_ptr || !d_list || !d_rows || !d_cn || !d_def || !d_span || !d_tab) return false;
   if (!cuda_ok(cudaMemcpyAsync(d_ptr, ptr.data(), sizeof(int) * ptr.size(), cudaMemcpyHostToDevice, stream), "H2D ptr") ||
       (!list.empty() && !cuda_ok(cudaMemcpyAsync(d_list, list.data(), sizeof(int) * list.size(),
                                                  cudaMemcpyHostToDevice, stream),
                                  "H2D list")) ||
       !cuda_ok(cudaMemcpyAsync(d_rows, rows.data(), sizeof(int) * rows.size(), cudaMemcpyHostToDevice, stream), "H2D rows") ||
       !cuda_ok(cudaMemcpyAsync(d_span, span.data(), sizeof(int2) * span.size(), cudaMemcpyHostToDevice, stream),
-               "H2D spans"))
+               "H2D spans") ||
+      !cuda_ok(cudaMemcpyAsync(d_tab, tab.data(), sizeof(int4) * tab.size(), cudaMemcpyHostToDevice, stream),
+               "H2D seed table"))
     return false;
   view.root_child_ptr = d_ptr;
   view.root_child_list = d_list;
   view.root_child_span = d_span;
+  view.seed_tab = d_tab;
   view.root_rows = d_rows;
   view.root_cn = d_cn;
   view.root_defect = d_def;

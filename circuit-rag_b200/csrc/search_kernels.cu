@@ -601,8 +601,6 @@ __global__ void __launch_bounds__(128) k_search_prologue(const float4* q_host, v
 // FMAs over float4 columns lane, lane + 32, ...; then one xor butterfly), so T
 // equals the main scan's own score of a real row.  The seed root's rows are
 // scanned by the main scan like any surviving root's.
-constexpr int SEED_SAMPLE_MAX = 1024;
-constexpr int SEED_BLOCK = 16;  // consecutive rows per bulk copy of the sample
 constexpr int SEED_RING_BYTES = 192 * 1024;
 
 struct RootScanLayout {
@@ -689,67 +687,86 @@ __global__ void __launch_bounds__(ROOT_SCAN_WARPS * 32) k_root_scan(IndexView ix
   // sample is scored
   int* ch_v = reinterpret_cast<int*>(keys);
   int* ch_off = ch_v + SEED_SAMPLE_MAX;
+  float4* sq4 = reinterpret_cast<float4*>(smem + L.q_off);
   if (warp == 0) {
     const unsigned long long best = ld_volatile_u64(&ctrl->best_packed);
     int pb = 0x3fffffff - (int)(best & 0x3fffffffull);
-    if (pb < 0 || pb >= ix.R) pb = 0;  // only reachable with NaN scores; keeps the CSR reads in bounds
-    const int cb = ix.root_child_ptr[pb];
-    const int nall = ix.root_child_ptr[pb + 1] - cb;
-    const int nch = min(nall, SEED_SAMPLE_MAX);
-    for (int ci = lane; ci < nch; ci += 32) {
-      const int2 sp = __ldg(ix.root_child_span + cb + ci);
-      ch_off[ci] = sp.x;
-      ch_v[ci] = sp.y;
-    }
-    // rows of those children: the whole root, or up to the first child left out
-    const int vrows = nall > nch ? __ldg(ix.root_child_span + cb + nch).y : ix.root_rows[pb];
-    __syncwarp();
-    // blocks of up to SEED_BLOCK consecutive rows starting at evenly spaced
-    // virtual rows, each inside one child (one bulk copy per block); block b
-    // ends before block b + 1 starts, so no row is sampled twice
-    const int want = min(min(vrows, max(4 * k, 128)), SEED_SAMPLE_MAX);
-    const int nb = (want + SEED_BLOCK - 1) / SEED_BLOCK;
-    int pos_base = 0;
-    for (int b0 = 0; b0 < nb; b0 += 32) {
-      const int b = b0 + lane;
-      int row = 0, len = 0;
-      if (b < nb) {
-        // exact in double: vrows < 2^31, nb <= 64
-        const int v = (int)floor((double)b * (double)vrows / (double)nb);
-        const int v_next = (b + 1 < nb) ? (int)floor((double)(b + 1) * (double)vrows / (double)nb) : vrows;
-        int lo = 0, hi = nch - 1;
-        while (lo < hi) {
-          const int mid = (lo + hi + 1) >> 1;
-          if (ch_v[mid] <= v) lo = mid; else hi = mid - 1;
+    if (pb < 0 || pb >= ix.R) pb = 0;  // only reachable with NaN scores; keeps the table reads in bounds
+    if (k <= 32 && ix.seed_tab) {
+      // precomputed blocks of this root: one read per lane
+      const int4 e = lane < SEED_TAB_W ? __ldg(ix.seed_tab + (size_t)pb * SEED_TAB_W + lane) : make_int4(0, 0, 0, 0);
+      const int nb = __shfl_sync(FULL_MASK, e.x, 0), S = __shfl_sync(FULL_MASK, e.y, 0);
+      if (lane >= 1 && lane <= nb) {
+        blk[3 * (lane - 1)] = e.x;
+        blk[3 * (lane - 1) + 1] = e.y;
+        blk[3 * (lane - 1) + 2] = e.z;
+      }
+      if (lane == 0) {
+        s_nblk = nb;
+        s_nsample = S;
+      }
+    } else {
+      const int cb = ix.root_child_ptr[pb];
+      const int nall = ix.root_child_ptr[pb + 1] - cb;
+      const int nch = min(nall, SEED_SAMPLE_MAX);
+      for (int ci = lane; ci < nch; ci += 32) {
+        const int2 sp = __ldg(ix.root_child_span + cb + ci);
+        ch_off[ci] = sp.x;
+        ch_v[ci] = sp.y;
+      }
+      // rows of those children: the whole root, or up to the first child left out
+      const int vrows = nall > nch ? __ldg(ix.root_child_span + cb + nch).y : ix.root_rows[pb];
+      __syncwarp();
+      // blocks of up to SEED_BLOCK consecutive rows starting at evenly spaced
+      // virtual rows, each inside one child (one bulk copy per block); block b
+      // ends before block b + 1 starts, so no row is sampled twice
+      const int want = min(min(vrows, max(4 * k, 128)), SEED_SAMPLE_MAX);
+      const int nb = (want + SEED_BLOCK - 1) / SEED_BLOCK;
+      int pos_base = 0;
+      for (int b0 = 0; b0 < nb; b0 += 32) {
+        const int b = b0 + lane;
+        int row = 0, len = 0;
+        if (b < nb) {
+          // exact in double: vrows < 2^31, nb <= 64
+          const int v = (int)floor((double)b * (double)vrows / (double)nb);
+          const int v_next = (b + 1 < nb) ? (int)floor((double)(b + 1) * (double)vrows / (double)nb) : vrows;
+          int lo = 0, hi = nch - 1;
+          while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (ch_v[mid] <= v) lo = mid; else hi = mid - 1;
+          }
+          const int child_end = (lo + 1 < nch) ? ch_v[lo + 1] : vrows;
+          len = min(min(SEED_BLOCK, v_next - v), child_end - v);
+          row = ch_off[lo] + (v - ch_v[lo]);
         }
-        const int child_end = (lo + 1 < nch) ? ch_v[lo + 1] : vrows;
-        len = min(min(SEED_BLOCK, v_next - v), child_end - v);
-        row = ch_off[lo] + (v - ch_v[lo]);
+        const int incl = warp_incl_scan(len, lane);
+        if (b < nb) {
+          blk[3 * b] = row;
+          blk[3 * b + 1] = len;
+          blk[3 * b + 2] = pos_base + incl - len;
+        }
+        pos_base += __shfl_sync(FULL_MASK, incl, 31);
       }
-      const int incl = warp_incl_scan(len, lane);
-      if (b < nb) {
-        blk[3 * b] = row;
-        blk[3 * b + 1] = len;
-        blk[3 * b + 2] = pos_base + incl - len;
+      if (lane == 0) {
+        s_nblk = nb;
+        s_nsample = pos_base;
       }
-      pos_base += __shfl_sync(FULL_MASK, incl, 31);
     }
     if (lane == 0) {
-      s_nblk = nb;
-      s_nsample = pos_base;
       s_ok = 1;
       ctrl->best_root = pb;
       mbar_init(bar, 1);
       fence_mbar_init();
     }
+  } else {
+    // the other warps stage the query meanwhile
+    for (int c = threadIdx.x - 32; c < ix.D4; c += blockDim.x - 32) sq4[c] = __ldg(q4 + c);
   }
   __syncthreads();
   const int S = s_nsample, nb = s_nblk;
   const int rb = ix.D * 4;
-  // the query in shared memory: this code runs once per search on a cold
-  // instruction cache, so the scoring loop below is kept compact
-  float4* sq4 = reinterpret_cast<float4*>(smem + L.q_off);
-  for (int c = threadIdx.x; c < ix.D4; c += blockDim.x) sq4[c] = __ldg(q4 + c);
+  // (the query is in shared memory: this code runs once per search on a cold
+  // instruction cache, so the scoring loop below is kept compact)
   uint32_t phase = 0;
   for (int r0 = 0; r0 < S; r0 += L.ring_rows) {
     const int nr = min(L.ring_rows, S - r0);
@@ -804,21 +821,38 @@ __global__ void __launch_bounds__(ROOT_SCAN_WARPS * 32) k_root_scan(IndexView ix
   uint32_t T = 0u;
   if (s_ok && S >= k) {
     if (S <= 128) {
-      // warp 0, four keys per lane: the largest t with at least k keys >= t,
-      // decided bit by bit (that t is the k-th largest key)
+      // warp 0, four keys per lane
       if (warp == 0) {
         uint32_t kv[4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) kv[r] = (lane * 4 + r < S) ? cand_key(keys[lane * 4 + r]) : 0u;
-        uint32_t t = 0u;
-        for (int bit = 31; bit >= 0; --bit) {
-          const uint32_t tr = t | (1u << bit);
-          int cnt = 0;
+        if (k <= 32) {
+          // k rounds: the largest key left, one copy of it removed
+          for (int i = 0; i < k; ++i) {
+            const uint32_t m = max(max(kv[0], kv[1]), max(kv[2], kv[3]));
+            const uint32_t wm = __reduce_max_sync(FULL_MASK, m);
+            T = wm;
+            const int lead = __ffs(__ballot_sync(FULL_MASK, m == wm)) - 1;
+            if (lane == lead) {
+              if (kv[0] == wm) kv[0] = 0u;
+              else if (kv[1] == wm) kv[1] = 0u;
+              else if (kv[2] == wm) kv[2] = 0u;
+              else kv[3] = 0u;
+            }
+          }
+        } else {
+          // the largest t with at least k keys >= t, decided bit by bit (that t
+          // is the k-th largest key)
+          uint32_t t = 0u;
+          for (int bit = 31; bit >= 0; --bit) {
+            const uint32_t tr = t | (1u << bit);
+            int cnt = 0;
 #pragma unroll
-          for (int r = 0; r < 4; ++r) cnt += __popc(__ballot_sync(FULL_MASK, kv[r] >= tr));
-          if (cnt >= k) t = tr;
+            for (int r = 0; r < 4; ++r) cnt += __popc(__ballot_sync(FULL_MASK, kv[r] >= tr));
+            if (cnt >= k) t = tr;
+          }
+          T = t;
         }
-        T = t;
       }
     } else {
       int selN = 1;
