@@ -72,9 +72,10 @@ struct SearchCtrl {
   int best_root;
   int error;                       // cb::ERR_* bits
   uint32_t call_seq;               // blocking calls: the call's sequence number (see HostIO)
-  uint32_t pad[7];
+  uint32_t chunk_next;             // the main scan's next chunk to claim (long streams)
+  uint32_t pad[6];
 };
-constexpr int CTRL_SEQ_WORD = 8;   // 64-bit word of the header whose low half is call_seq
+constexpr int CTRL_SEQ_WORD = 8;   // 64-bit word of the header: call_seq (low half), chunk_next (high, zero)
 constexpr size_t CTRL_RESET_BYTES = 96;
 static_assert(sizeof(SearchCtrl) == CTRL_RESET_BYTES, "ctrl layout");
 

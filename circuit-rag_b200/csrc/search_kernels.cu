@@ -57,6 +57,7 @@ struct ScanParams {
   int k;
   int stages;
   int min_rows;                               // rows per CTA below which fewer CTAs take part
+  uint32_t* chunk_counter;                    // long streams: chunks claimed so far (zeroed per search)
   float* out_scores;
   int* out_ids;
   long long* out_rows;
@@ -101,6 +102,11 @@ __host__ __device__ inline ScanLayout scan_layout(int rows_per_stage, int row_by
 
 // Merges whose survivors number at most this many rank them directly.
 constexpr int RANK_CAP = 256;
+// Streams of at least SCAN_DYN_CHUNKS chunks of SCAN_DYN_MIN_STAGES stages per
+// CTA are taken in claimed chunks (about SCAN_DYN_CHUNKS per CTA) instead of
+// equal slices.
+constexpr int SCAN_DYN_CHUNKS = 48;
+constexpr int SCAN_DYN_MIN_STAGES = 8;
 
 template <int VPL, int KCAP>
 __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
@@ -161,20 +167,40 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
 
   if (warp == SCAN_CONSUMER_WARPS) {
     // ------------------------------------------------------------ producer
-    const uint32_t vb = (uint32_t)(((unsigned long long)blockIdx.x * n_rows) / G);
-    const uint32_t ve = (uint32_t)(((unsigned long long)(blockIdx.x + 1) * n_rows) / G);
-    // first range holding virtual row vb: a 32-way search by the whole warp
-    // (ranges[0].x = 0 <= vb, ranges sorted by .x), 3 L2 round trips for 4,096 ranges
+    // Work distribution.  A short stream is split into G equal slices.  A long
+    // one is cut into chunks of chunk_rows virtual rows that the CTAs take from
+    // a counter in the control block, one claim in flight ahead of the chunk
+    // being streamed: SMs do not stream at the same rate (measured at 100M rows,
+    // equal slices finished up to 17 % apart), and with claims the faster ones
+    // take more chunks, so all finish within about one chunk of each other.
+    const bool dyn = P.chunk_counter != nullptr && n_rows >= G * (uint32_t)(SCAN_DYN_CHUNKS * SCAN_DYN_MIN_STAGES * ROWS);
+    uint32_t chunk_rows = 0, next_claim = 0;
+    uint32_t vb, ve;  // the piece of the stream being streamed
+    if (dyn) {
+      const uint32_t per = n_rows / (G * (uint32_t)SCAN_DYN_CHUNKS);
+      chunk_rows = max((uint32_t)(SCAN_DYN_MIN_STAGES * ROWS), (per + ROWS - 1) / ROWS * ROWS);
+      uint32_t c = 0;
+      if (lane == 0) c = atomicAdd(P.chunk_counter, 1u);
+      c = __shfl_sync(FULL_MASK, c, 0);
+      vb = (uint32_t)min((unsigned long long)n_rows, (unsigned long long)c * chunk_rows);
+      ve = min(n_rows, vb + chunk_rows);
+      if (lane == 0) next_claim = atomicAdd(P.chunk_counter, 1u);  // used when this chunk is done
+    } else {
+      vb = (uint32_t)(((unsigned long long)blockIdx.x * n_rows) / G);
+      ve = (uint32_t)(((unsigned long long)(blockIdx.x + 1) * n_rows) / G);
+    }
+    // the range holding virtual row vv, searched from range `lo` (whose entry
+    // is `rg` and starts at or before vv): a 32-way search by the whole warp
+    // (ranges sorted by .x), 3 L2 round trips for 4,096 ranges
     int s = 0;
-    int4 rg = make_int4(0, 0, 0, 0);
-    if (vb < ve && n_ranges > 0) {
-      int lo = 0, hi = (int)n_ranges - 1;
-      rg = s_rg0;
+    int4 rg = s_rg0;  // entry 0 exists whenever ranges do; read beside the count
+    const auto locate = [&](uint32_t vv, int lo) {
+      int hi = (int)n_ranges - 1;
       while (hi > lo) {
         const int step = (hi - lo + 32) >> 5;
         const int pos = lo + lane * step;
         const int4 e = pos <= hi ? __ldcg(&P.ranges[pos]) : make_int4(0x7fffffff, 0, 0, 0);
-        const int j = 31 - __clz(__ballot_sync(FULL_MASK, (uint32_t)e.x <= vb));
+        const int j = 31 - __clz(__ballot_sync(FULL_MASK, (uint32_t)e.x <= vv));
         rg.x = __shfl_sync(FULL_MASK, e.x, j);  // the winner's entry: ranges[new lo]
         rg.y = __shfl_sync(FULL_MASK, e.y, j);
         rg.z = __shfl_sync(FULL_MASK, e.z, j);
@@ -183,7 +209,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
         hi = min(hi, lo + step - 1);
       }
       s = lo;
-    }
+    };
+    if (vb < ve && n_ranges > 0) locate(vb, 0);
     // The whole warp walks the ranges: lane j holds entry base + j of the
     // current 32-entry window and of the next one (loaded a window ahead), so
     // moving from one child's rows to the next is a register shuffle; an L2
@@ -203,7 +230,23 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       return (vb < ve && idx < (int)n_ranges) ? __ldcg(&P.ranges[idx]) : make_int4(0, 0, 0, 0);
     };
     int4 win = load_window(base), win_next = load_window(base + 32);
-    while (v < ve) {
+    bool bad_range = false;
+    for (;;) {
+      if (v >= ve) {
+        if (!dyn || bad_range) break;
+        // the next chunk: claimed a chunk ago; claim the one after it now
+        const uint32_t c = __shfl_sync(FULL_MASK, next_claim, 0);
+        const unsigned long long nvb = (unsigned long long)c * chunk_rows;
+        if (nvb >= n_rows) break;
+        vb = (uint32_t)nvb;
+        ve = min(n_rows, vb + chunk_rows);
+        v = vb;
+        if (lane == 0) next_claim = atomicAdd(P.chunk_counter, 1u);
+        locate(vb, s);  // later chunks lie at higher rows: search forward from the current range
+        base = s & ~31;
+        win = load_window(base);
+        win_next = load_window(base + 32);
+      }
       const int stage = it % STAGES, f = it / STAGES;
       bool free_stage = true;
       if (lane == 0 && f > 0) free_stage = mbar_wait(&empty[stage], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY);
@@ -222,6 +265,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
           if (s >= (int)n_ranges) {
             if (lane == 0) atomicOr(P.err, ERR_BAD_RANGE);
             v = ve;
+            bad_range = true;
             break;
           }
           if (s - base == 32) {
@@ -1297,6 +1341,7 @@ static ScanParams scan_params(const IndexView& ix, const Workspace& ws, const fl
   P.k = k;
   P.stages = stages_for(vpl_bucket(ix.D4), P.row_bytes);
   P.min_rows = SCAN_MIN_ROWS;
+  P.chunk_counter = &ws.ctrl->chunk_next;
   P.out_scores = out_scores;
   P.out_ids = out_ids;
   P.out_rows = out_rows;
@@ -1402,6 +1447,7 @@ cudaError_t launch_flat_scan(const float* leaf, int D, int N, const float* q, in
   F.k = k;
   F.stages = stages_for(vpl, F.row_bytes);
   F.min_rows = SCAN_MIN_ROWS;
+  F.chunk_counter = &ctrl->chunk_next;
   F.out_scores = out_scores;
   F.out_ids = out_ids;
   F.out_rows = nullptr;
