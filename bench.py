@@ -115,7 +115,7 @@ def clock_sampler(device_index):
              "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap",
-             "--format=csv,noheader,nounits", "-lms", "200"],
+             "--format=csv,noheader,nounits", "-lms", "100"],
             stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
     except OSError:
         return None
@@ -397,9 +397,9 @@ class Searcher:
         return merge_topk(self.gs, self.gi, self.k)
 
 
-def single_query(idx, Q, k, warm, steps, world, exchange, dev, clocks=False, local_rank=0):
+def single_query(idx, Q, k, warm, steps, world, exchange, dev):
     """Timed single queries: returns dict(value, p50, p99, scan_ms, main_rows,
-    seed_rows, out_s, out_i, elapsed_ms, clocks)."""
+    seed_rows, out_s, out_i, elapsed_ms)."""
     import torch.distributed as dist
 
     from circuit_rag import _native
@@ -418,7 +418,6 @@ def single_query(idx, Q, k, warm, steps, world, exchange, dev, clocks=False, loc
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    proc = clock_sampler(local_rank) if clocks else None
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     t0.record(stream)
@@ -432,7 +431,6 @@ def single_query(idx, Q, k, warm, steps, world, exchange, dev, clocks=False, loc
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clk = clock_summary(proc)
     elapsed = t0.elapsed_time(t1)
     if world > 1:
         t = torch.tensor([elapsed], device=dev)
@@ -451,7 +449,7 @@ def single_query(idx, Q, k, warm, steps, world, exchange, dev, clocks=False, loc
         main_rows.append(int(raw[2] & 0xFFFFFFFF))
     return {"value": steps / (elapsed / 1000.0), "elapsed_ms": elapsed, "p50_us": pctl(lat, 0.5),
             "p99_us": pctl(lat, 0.99), "scan_ms": scan_ms, "main_rows": main_rows, "seed_rows": seed_rows,
-            "out_s": out_s, "out_i": out_i, "clocks": clk}
+            "out_s": out_s, "out_i": out_i}
 
 
 def phase_split(idx, Q, k, dev, n=20):
@@ -770,7 +768,14 @@ def main():
 
     steps, warm = args.steps, args.warmup
     Q = w.query_batch(steps + warm, device=dev)
-    sq = single_query(idx, Q, k, warm, steps, world, exchange, dev, clocks=(rank == 0), local_rank=local)
+    # clocks: sampled by nvidia-smi every 100 ms from just before the single-query
+    # warm-up to the end of the batched timing (at 8 GPUs the single-query timed
+    # region alone is shorter than one sampling interval)
+    clk_proc = None
+    if rank == 0:
+        clk_proc = clock_sampler(local)
+        time.sleep(0.5)  # nvidia-smi is up and sampling before the first timed launch
+    sq = single_query(idx, Q, k, warm, steps, world, exchange, dev)
     ex_s, ex_i = gather_exact(*exact_topk(idx.leaf_vectors, idx.original_ids, Q[warm:], k), world)
     check = {"checked_queries": steps, "mismatches": count_mismatches(sq["out_s"], sq["out_i"], ex_s, ex_i, k),
              "how": "float64 brute force on the device" + (" per shard, gathered" if world > 1 else "")}
@@ -837,8 +842,16 @@ def main():
     if args.batch > 0:
         Bq, bw, bs = args.batch, max(1, args.batch_warmup), args.batch_steps
         QB = w.query_batch(Bq * (bw + bs), device=dev).view(bw + bs, Bq, D)
-        bat = batched(idx, QB, k, n_local, D, world, dev, bw, bs, args.batch_check, args.tf32_seconds, cpu=cpu_b)
+        bat = batched(idx, QB, k, n_local, D, world, dev, bw, bs, args.batch_check, 0.0, cpu=cpu_b)
         del QB
+    clocks = clock_summary(clk_proc)
+    if clocks:
+        clocks["window"] = "single-query warm-up to the end of the batched timing, 100 ms samples"
+    if bat is not None and args.tf32_seconds > 0:
+        burst, sust = tf32_gemm_in_process(dev, args.tf32_seconds)
+        roof = bat["roofline"]
+        roof["side_in_process_cublas_tf32"] = {"burst": round(burst, 1), "sustained": round(sust, 1),
+                                               "frac_of_sustained": round(roof["achieved"] / sust, 4)}
 
     hbm_peak, _, peak_kind = measured_peaks()
     mean_scan_ms = statistics.mean(sq["scan_ms"])
@@ -889,7 +902,7 @@ def main():
             "pruned_leaf_fraction": round(1.0 - mean_rows / n_local, 5),
             "roofline": roof, "cpu_baseline": ({kk: cpu[kk] for kk in ("value", "unit", "cores", "kind", "sample")}
                                                if cpu else None),
-            "e2e": e2e, "gpu_launches": (4 if world == 1 else 5) * steps, "clocks": sq["clocks"], "build_s": round(build_s, 1),
+            "e2e": e2e, "gpu_launches": (4 if world == 1 else 5) * steps, "clocks": clocks, "build_s": round(build_s, 1),
             "check": check, "threshold_exchange": exchange, "batched": bat,
             "shards": {"rows": rows_all, "max_over_mean": round(max(rows_all) / statistics.mean(rows_all), 4),
                        "parts_total": info["parts_total"], "roots": info["roots"]},
