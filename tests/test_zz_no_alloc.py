@@ -111,3 +111,27 @@ def test_noalloc_small_corpora_match_existing_entry_point(n, k):
         if n < k:
             assert torch.all(torch.isneginf(s_new[n:])) and torch.all(i_new[n:] == -1)
     idx.close()
+
+
+def test_noalloc_long_stream_matches_existing_entry_point():
+    """2,000,000 rows: long enough for the scan to hand out chunks from the
+    counter kept in the fixed scratch (cleared by each call); two calls in a
+    row equal the existing entry point's results."""
+    L = _native.lib()
+    w = WORKLOADS["mixed-100m"]
+    X = w.corpus(0, 2_000_000, device=DEV)
+    Q = w.query_batch(2, device=DEV)
+    idx = _one_child_index(X)
+    h = idx.native_handle()
+    stream = torch.cuda.current_stream()
+    for q in Q:
+        s_new, i_new = _noalloc(L, X, q, 10, stream)
+        s_ref = torch.empty(10, device=DEV)
+        i_ref = torch.empty(10, dtype=torch.int32, device=DEV)
+        assert L.circuit_search_async(h, q.data_ptr(), 10, 1 << 62, s_ref.data_ptr(), i_ref.data_ptr(), None,
+                                      stream.cuda_stream, None, None) == 0, _native.last_error()
+        torch.cuda.synchronize()
+        exact = (X.double() @ q.double()).cpu().numpy()
+        oracle.check_topk(exact, 10, s_new.cpu().numpy(), i_new.cpu().numpy())
+        assert torch.equal(s_new, s_ref) and torch.equal(i_new, i_ref)
+    idx.close()
