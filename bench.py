@@ -397,9 +397,17 @@ class Searcher:
         return merge_topk(self.gs, self.gi, self.k)
 
 
-def single_query(idx, Q, k, warm, steps, world, exchange, dev):
+def single_query(idx, Q, k, warm, steps, world, exchange, dev, scan_events=True):
     """Timed single queries: returns dict(value, p50, p99, scan_ms, main_rows,
-    seed_rows, out_s, out_i, elapsed_ms)."""
+    seed_rows, streamed_rows, scan_rows, out_s, out_i, elapsed_ms).
+
+    scan_events: CUDA events around the main scan inside the timed loop.  An
+    event between the bounds kernel and the main scan makes the scan wait for
+    the bounds (it normally streams beside them), so the latency-bound
+    workloads time the queries without them and time the scan in a separate
+    pass.  main_rows = rows of the children that survive the seed threshold's
+    bounds; streamed_rows = rows the pipelined scan read; scan_rows = rows the
+    scans timed by scan_ms read."""
     import torch.distributed as dist
 
     from circuit_rag import _native
@@ -423,7 +431,7 @@ def single_query(idx, Q, k, warm, steps, world, exchange, dev):
     t0.record(stream)
     for j in range(steps):
         q_ev[j][0].record(stream)
-        rs, ri = se.search(Q[warm + j], *s_ev[j])
+        rs, ri = se.search(Q[warm + j], *(s_ev[j] if scan_events else ()))
         out_s[j].copy_(rs)
         out_i[j].copy_(ri)
         q_ev[j][1].record(stream)
@@ -437,19 +445,27 @@ def single_query(idx, Q, k, warm, steps, world, exchange, dev):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed = float(t.item())
     lat = [a.elapsed_time(b) * 1000.0 for a, b in q_ev]
-    scan_ms = [a.elapsed_time(b) for a, b in s_ev]
-    # rows scanned per query: an untimed replay with trace snapshots
+    scan_ms = [a.elapsed_time(b) for a, b in s_ev] if scan_events else None
+    # rows per query: untimed replays with trace snapshots, with the scan events
+    # (the mode scan_ms is measured in) and without them (the pipelined search)
     snap = torch.empty(_native.TRACE_SNAPSHOT_BYTES, dtype=torch.uint8, device=dev)
-    main_rows, seed_rows = [], []
-    for j in range(steps):
-        se.local(Q[warm + j])
-        se.L.circuit_trace_snapshot_async(se.h, snap.data_ptr(), stream.cuda_stream)
-        raw = snap.cpu().numpy().view(np.uint64)
-        seed_rows.append(int(raw[1] & 0xFFFFFFFF))
-        main_rows.append(int(raw[2] & 0xFFFFFFFF))
+    main_rows, seed_rows, streamed_rows, scan_rows = [], [], [], []
+    for with_events in (True, False):
+        for j in range(steps):
+            se.local(Q[warm + j], *(s_ev[j] if with_events else ()))  # (scan_ms is read already if timed)
+            se.L.circuit_trace_snapshot_async(se.h, snap.data_ptr(), stream.cuda_stream)
+            raw = snap.cpu().numpy().view(np.uint64)
+            if with_events:
+                scan_rows.append(int(raw[9] >> 32))
+            else:
+                seed_rows.append(int(raw[1] & 0xFFFFFFFF))
+                main_rows.append(int(raw[2] & 0xFFFFFFFF))
+                streamed_rows.append(int(raw[9] >> 32))
+    if not scan_events:
+        scan_ms = [a.elapsed_time(b) for a, b in s_ev]
     return {"value": steps / (elapsed / 1000.0), "elapsed_ms": elapsed, "p50_us": pctl(lat, 0.5),
             "p99_us": pctl(lat, 0.99), "scan_ms": scan_ms, "main_rows": main_rows, "seed_rows": seed_rows,
-            "out_s": out_s, "out_i": out_i}
+            "streamed_rows": streamed_rows, "scan_rows": scan_rows, "out_s": out_s, "out_i": out_i}
 
 
 def phase_split(idx, Q, k, dev, n=20):
@@ -676,7 +692,8 @@ def other_workloads(dev, hbm_peak):
     from circuit_rag.synthetic import WORKLOADS
 
     out = {}
-    for name, n_q, flat in (("spread-200k", 300, False), ("clustered-50k", 300, False), ("spread-5k", 300, True)):
+    for name, n_q, flat in (("spread-200k", 300, False), ("clustered-50k", 300, False), ("clustered-4m", 100, False),
+                            ("spread-5k", 300, True)):
         w = WORKLOADS[name]
         X = w.corpus(0, w.n, device=dev)
         idx = build_circuit_index(X, num_roots=w.num_roots, children_per_root=w.children_per_root, rank=w.rank,
@@ -685,18 +702,21 @@ def other_workloads(dev, hbm_peak):
         r = {"N": w.n, "D": w.dim, "k": w.k, "num_roots": w.num_roots, "children_per_root": w.children_per_root,
              "rank": w.rank}
         if not flat:
-            sq = single_query(idx, Q, w.k, 20, n_q, 1, False, dev)
+            sq = single_query(idx, Q, w.k, 20, n_q, 1, False, dev, scan_events=False)
             ex_s, ex_i = exact_topk(idx.leaf_vectors, idx.original_ids, Q[20:20 + n_q], w.k)
             bad = count_mismatches(sq["out_s"], sq["out_i"], ex_s, ex_i, w.k)
             mean_rows = statistics.mean(sq["main_rows"])
             scan = statistics.mean(sq["scan_ms"])
+            scan_rows = statistics.mean(sq["scan_rows"])
             leaf_bytes = mean_rows * w.dim * 4
             R, C, D, rk = idx.num_roots, idx.num_total_children, w.dim, w.rank
             meta_bytes = 4 * R * D + 4 * R * D * rk + 4 * C * (2 * rk + 2) + statistics.mean(sq["seed_rows"]) * D * 4
             r.update({"single_query_qps": round(sq["value"], 1), "p50_us": round(sq["p50_us"], 2),
                       "p99_us": round(sq["p99_us"], 2), "pruned_leaf_fraction": round(1 - mean_rows / w.n, 5),
-                      "main_scan": {"rows": mean_rows, "mean_launch_us": round(scan * 1000, 2),
-                                    "frac_of_hbm": round(leaf_bytes / (scan * 1e-3) / 1e9 / hbm_peak, 4)},
+                      "rows_streamed_fraction": round(statistics.mean(sq["streamed_rows"]) / w.n, 5),
+                      "main_scan": {"rows": scan_rows, "mean_launch_us": round(scan * 1000, 2),
+                                    "frac_of_hbm": round(scan_rows * w.dim * 4 / (scan * 1e-3) / 1e9 / hbm_peak, 4),
+                                    "timed": "alone, after the bounds (events around it)"},
                       "query_roofline": {"bytes": round(leaf_bytes + meta_bytes),
                                          "leaf_bytes": round(leaf_bytes), "bound_metadata_bytes": round(meta_bytes),
                                          "frac_of_hbm_at_p50": round((leaf_bytes + meta_bytes) / (sq["p50_us"] * 1e-6)
@@ -717,7 +737,7 @@ def other_workloads(dev, hbm_peak):
     QB = w.query_batch(1024 * 5, device=dev).view(5, 1024, w.dim)
     b = batched(idx, QB, w.k, w.n, w.dim, 1, dev, 2, 3, 64, 0.0, e2e=False)
     Q1 = w.query_batch(40, device=dev)
-    sq = single_query(idx, Q1, w.k, 5, 30, 1, False, dev)
+    sq = single_query(idx, Q1, w.k, 5, 30, 1, False, dev, scan_events=False)
     ex_s, ex_i = exact_topk(idx.leaf_vectors, idx.original_ids, Q1[5:35], w.k)
     out["zipf-10m"] = {"N": w.n, "D": w.dim, "k": w.k, "num_roots": w.num_roots,
                        "children_per_root": w.children_per_root, "rank": w.rank,
@@ -726,6 +746,8 @@ def other_workloads(dev, hbm_peak):
                        "single_query": {"qps": round(sq["value"], 1), "p50_us": round(sq["p50_us"], 1),
                                         "p99_us": round(sq["p99_us"], 1),
                                         "pruned_leaf_fraction": round(1 - statistics.mean(sq["main_rows"]) / w.n, 5),
+                                        "rows_streamed_fraction": round(statistics.mean(sq["streamed_rows"]) / w.n,
+                                                                        5),
                                         "check": {"checked_queries": 30,
                                                   "mismatches": count_mismatches(sq["out_s"], sq["out_i"], ex_s, ex_i,
                                                                                  w.k)}}}
@@ -855,7 +877,7 @@ def main():
 
     hbm_peak, _, peak_kind = measured_peaks()
     mean_scan_ms = statistics.mean(sq["scan_ms"])
-    mean_rows = statistics.mean(sq["main_rows"])
+    mean_rows = statistics.mean(sq["scan_rows"])  # rows the timed scans read
     alg_bytes = mean_rows * D * 4
     achieved = alg_bytes / (mean_scan_ms * 1e-3) / 1e9
     if world > 1:
@@ -899,7 +921,8 @@ def main():
                        "children_per_root": w.children_per_root, "rank": w.rank, "rows_per_gpu": rows_all,
                        "parallelism": f"root-cluster shards x{world}", "l2": "inputs larger than L2, no flush needed"},
             "p50_us": round(sq["p50_us"], 2), "p99_us": round(sq["p99_us"], 2),
-            "pruned_leaf_fraction": round(1.0 - mean_rows / n_local, 5),
+            "pruned_leaf_fraction": round(1.0 - statistics.mean(sq["main_rows"]) / n_local, 5),
+            "rows_streamed_fraction": round(statistics.mean(sq["streamed_rows"]) / n_local, 5),
             "roofline": roof, "cpu_baseline": ({kk: cpu[kk] for kk in ("value", "unit", "cores", "kind", "sample")}
                                                if cpu else None),
             "e2e": e2e, "gpu_launches": (4 if world == 1 else 5) * steps, "clocks": clocks, "build_s": round(build_s, 1),

@@ -74,6 +74,7 @@ class TraceEx(ctypes.Structure):
         ("seed_threshold", ctypes.c_float),
         ("device_error", ctypes.c_int32),
         ("seed_sample_rows", ctypes.c_int32),
+        ("rows_streamed", ctypes.c_int32),
     ]
 
 

@@ -22,10 +22,17 @@ from circuit_rag.hierarchy.build import CircuitIndex
 
 class SearchTrace:
     """Per-search statistics (reference search.py:12-19 fields plus
-    vectors_scored, surviving_roots, pruned_fraction, best_root)."""
+    vectors_scored, surviving_roots, pruned_fraction, best_root, rows_streamed).
+
+    vectors_scored / pruned_fraction describe the bounds: the rows of the
+    children whose rigorous bound is not below the seed threshold.
+    rows_streamed counts the rows the main scan read; it runs beside the bounds
+    kernel, so it streams children whose bound is not known yet (a small
+    corpus streams whole before the bounds are ready) and skips children whose
+    bound is below the threshold it has raised by then."""
 
     _LAZY = ("seed_threshold", "surviving_children", "surviving_roots", "vectors_scored", "best_root",
-             "total_gpu_time_us", "pruned_fraction")
+             "total_gpu_time_us", "pruned_fraction", "rows_streamed")
 
     def __init__(self):
         self.corpus_size = 0
@@ -33,7 +40,8 @@ class SearchTrace:
         self.total_children = 0
         self._pending = None
         self._values = {"seed_threshold": -1e9, "surviving_children": -1, "surviving_roots": -1,
-                        "vectors_scored": -1, "best_root": -1, "total_gpu_time_us": 0.0, "pruned_fraction": 0.0}
+                        "vectors_scored": -1, "best_root": -1, "total_gpu_time_us": 0.0, "pruned_fraction": 0.0,
+                        "rows_streamed": -1}
 
     def _resolve(self):
         if self._pending is None:
@@ -49,6 +57,7 @@ class SearchTrace:
         v["total_gpu_time_us"] = ev0.elapsed_time(ev1) * 1000.0
         v["vectors_scored"] = int(tx.vectors_scored)
         v["pruned_fraction"] = 1.0 - tx.vectors_scored / max(1, tx.vectors_total)
+        v["rows_streamed"] = int(tx.rows_streamed)
         if path:
             v["seed_threshold"] = float(tx.seed_threshold) if tx.seed_threshold > float("-inf") else -1e9
             v["surviving_children"] = int(tx.surviving_children)

@@ -125,6 +125,8 @@ class Workload:
 
 WORKLOADS = {
     "clustered-50k": Workload("clustered-50k", 50_000, 128, 64, 16, 8, 10, 25, "clustered", 64, 0.05),
+    # the clustered-50k law at 4M rows (2 GB): too large to stream whole while the bounds are computed
+    "clustered-4m": Workload("clustered-4m", 4_000_000, 128, 64, 16, 8, 10, 25, "clustered", 64, 0.05),
     "spread-5k": Workload("spread-5k", 5_183, 384, 64, 16, 8, 10, 300, "spread"),
     "spread-200k": Workload("spread-200k", 200_000, 384, 128, 16, 8, 10, 1000, "spread"),
     "zipf-10m": Workload("zipf-10m", 10_000_000, 384, 256, 32, 16, 100, 1024, "clustered", 4096, 0.08, 1.1),

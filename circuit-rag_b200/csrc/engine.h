@@ -60,22 +60,25 @@ constexpr int ROOT_SCAN_WARPS = 8;
 struct SearchCtrl {
   unsigned long long best_packed;  // argmax root: prio<<62 | key<<30 | (2^30-1-root)
   unsigned long long seed_packed;  // rows scored by the seed sample
-  unsigned long long main_packed;  // main range list: n_ranges<<32 | n_rows (atomicAdd)
+  unsigned long long main_packed;  // children kept by the seed threshold << 32 | their rows (atomicAdd)
   uint32_t k1_done;                // last-CTA tickets
   uint32_t seed_done;
   uint32_t main_done;
   uint32_t theta_key;              // running global threshold key (atomicMax)
   uint32_t seed_T_key;             // k-th best key of the seed rows (0 = none)
   uint32_t n_surv_roots;           // roots whose bound survived (seed root included)
-  uint32_t n_surv_children;        // non-empty children scanned (seed root's included)
+  uint32_t n_surv_children;        // non-empty children kept by the seed threshold
   float qn2;                       // fl(sum q_i^2)
   int best_root;
   int error;                       // cb::ERR_* bits
   uint32_t call_seq;               // blocking calls: the call's sequence number (see HostIO)
-  uint32_t chunk_next;             // the main scan's next chunk to claim (long streams)
-  uint32_t pad[6];
+  uint32_t chunk_next;             // the main scan's next chunk to claim
+  uint32_t epoch;                  // this search's number (tags the bounds it computes; never 0)
+  uint32_t rows_streamed;          // leaf rows the main scan read (atomicAdd per CTA)
+  uint32_t pad[4];
 };
 constexpr int CTRL_SEQ_WORD = 8;   // 64-bit word of the header: call_seq (low half), chunk_next (high, zero)
+constexpr int CTRL_EPOCH_WORD = 9; // epoch (low half), rows_streamed (high, zero)
 constexpr size_t CTRL_RESET_BYTES = 96;
 static_assert(sizeof(SearchCtrl) == CTRL_RESET_BYTES, "ctrl layout");
 
@@ -97,6 +100,8 @@ struct IndexView {
   const int* root_child_list;   // [nnz children]
   const int2* root_child_span;  // [nnz] per CSR entry: {leaf offset, first row within its root's rows}
   const int4* seed_tab;         // [R * SEED_TAB_W] the seed sample of each root for k <= 32 (see below)
+  const int4* all_ranges;       // [nnz] every CSR entry in order: {first virtual row, leaf row begin, end, child}
+  const unsigned long long* all_packed;  // [1] nnz << 32 | N
   const int* root_rows;         // [R]  leaf rows under each root
   const double* root_cn;        // [R]  upper bound of ||c_r||
   const double* root_defect;    // [R]  upper bound of ||V_r^T V_r - I||_2
@@ -106,11 +111,16 @@ struct IndexView {
 // Device workspace owned by one index handle (one in-flight search at a time).
 struct Workspace {
   SearchCtrl* ctrl;
-  int4* main_ranges;                 // [C]
+  uint32_t* epoch_counter;           // [1] the last search's epoch (not cleared between searches)
   int4* flat_range;                  // [1] = {0, 0, N, -1}
   unsigned long long* flat_packed;   // [1] = 1<<32 | N
   float* ub_root;                    // [R] rigorous root bounds (rounded up to float)
   float* ub_child;                   // [C] rigorous child bounds
+  // [nnz] per CSR entry: epoch << 32 | key of min(root bound, child bound);
+  // an entry whose epoch is not the running search's is not known yet
+  unsigned long long* ub_tagged;
+  const int* chunk_first_range;      // [n_chunks] the all_ranges entry holding each chunk's first row
+  int chunk_rows;                    // rows per chunk of the hierarchical main scan
   unsigned long long* cta_lists;     // [scan_grid * KMAX]
   int scan_grid;
 };
@@ -142,10 +152,11 @@ struct HostIO {
 cudaError_t launch_prepare_roots(const IndexView& ix, double* root_cn, double* root_defect, cudaStream_t stream);
 
 // One single-query search.  hierarchical != 0 runs prologue -> root scan (with
-// the seed sample) -> bounds -> main scan; otherwise prologue -> one flat scan
-// over all rows.  Outputs k
-// results sorted by (score desc, row asc).  ev_scan0/1 (may be null) are
-// recorded around the main (dominant) scan kernel.
+// the seed sample) -> bounds -> main scan, the main scan streaming beside the
+// bounds kernel and skipping each child once its bound is known and below the
+// running threshold; otherwise prologue -> one flat scan over all rows.
+// Outputs k results sorted by (score desc, row asc).  ev_scan0/1 (may be null)
+// are recorded around the main (dominant) scan kernel.
 cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float* q, int k, int hierarchical,
                           float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
                           cudaEvent_t ev_scan0, cudaEvent_t ev_scan1, const HostIO* io = nullptr);
@@ -205,6 +216,9 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
                                 cudaEvent_t ev_scan_end);
 
 int scan_smem_bytes(int D);
+// Rows per chunk of the hierarchical main scan over N rows of dimension D on
+// `grid` CTAs: a multiple of the rows of one ring stage, about 48 chunks per CTA.
+int overlap_chunk_rows(int N, int D, int grid);
 // One kernel whose mbarrier wait nothing satisfies, run through the bounded
 // wait every search kernel uses: after the limit it or-s ERR_TIMEOUT_FULL into
 // *err and returns (merge_kernels.cu).

@@ -171,9 +171,24 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
     tab[(size_t)p * cb::SEED_TAB_W] = make_int4(nb, pos, 0, 0);
   }
   int4* d_tab = (int4*)dev_alloc(sizeof(int4) * tab.size(), "cudaMalloc(seed_tab)");
+  // the hierarchical main scan's static range list: every CSR entry in order,
+  // virtual rows numbered along it (children cover all N rows)
+  const size_t nnz = list.size();
+  std::vector<int4> all(std::max<size_t>(nnz, 1), make_int4(0, 0, 0, -1));
+  {
+    int v = 0;
+    for (size_t i = 0; i < nnz; ++i) {
+      const int c = list[i];
+      all[i] = make_int4(v, offsets[c], offsets[c] + sizes[c], c);
+      v += sizes[c];
+    }
+  }
+  const unsigned long long all_packed = ((unsigned long long)nnz << 32) | (unsigned long long)(uint32_t)N;
+  int4* d_all = (int4*)dev_alloc(sizeof(int4) * all.size(), "cudaMalloc(all_ranges)");
+  unsigned long long* d_all_packed = (unsigned long long*)dev_alloc(sizeof(unsigned long long), "cudaMalloc(all_packed)");
   double* d_cn = (double*)dev_alloc(sizeof(double) * R, "cudaMalloc(root_cn)");
   double* d_def = (double*)dev_alloc(sizeof(double) * R, "cudaMalloc(root_defect)");
-  if (!d_ptr || !d_list || !d_rows || !d_cn || !d_def || !d_span || !d_tab) return false;
+  if (!d_ptr || !d_list || !d_rows || !d_cn || !d_def || !d_span || !d_tab || !d_all || !d_all_packed) return false;
   if (!cuda_ok(cudaMemcpyAsync(d_ptr, ptr.data(), sizeof(int) * ptr.size(), cudaMemcpyHostToDevice, stream), "H2D ptr") ||
       (!list.empty() && !cuda_ok(cudaMemcpyAsync(d_list, list.data(), sizeof(int) * list.size(),
                                                  cudaMemcpyHostToDevice, stream),
@@ -182,12 +197,18 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
       !cuda_ok(cudaMemcpyAsync(d_span, span.data(), sizeof(int2) * span.size(), cudaMemcpyHostToDevice, stream),
                "H2D spans") ||
       !cuda_ok(cudaMemcpyAsync(d_tab, tab.data(), sizeof(int4) * tab.size(), cudaMemcpyHostToDevice, stream),
-               "H2D seed table"))
+               "H2D seed table") ||
+      !cuda_ok(cudaMemcpyAsync(d_all, all.data(), sizeof(int4) * all.size(), cudaMemcpyHostToDevice, stream),
+               "H2D range list") ||
+      !cuda_ok(cudaMemcpyAsync(d_all_packed, &all_packed, sizeof(all_packed), cudaMemcpyHostToDevice, stream),
+               "H2D range count"))
     return false;
   view.root_child_ptr = d_ptr;
   view.root_child_list = d_list;
   view.root_child_span = d_span;
   view.seed_tab = d_tab;
+  view.all_ranges = d_all;
+  view.all_packed = d_all_packed;
   view.root_rows = d_rows;
   view.root_cn = d_cn;
   view.root_defect = d_def;
@@ -196,7 +217,22 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
   // workspace
   ws.scan_grid = cb::sm_count(device);
   ws.ctrl = (cb::SearchCtrl*)dev_alloc(sizeof(cb::SearchCtrl), "cudaMalloc(ctrl)");
-  ws.main_ranges = (int4*)dev_alloc(sizeof(int4) * std::max(C, 1), "cudaMalloc(main_ranges)");
+  ws.epoch_counter = (uint32_t*)dev_alloc(sizeof(uint32_t), "cudaMalloc(epoch)");
+  ws.ub_tagged = (unsigned long long*)dev_alloc(sizeof(unsigned long long) * std::max<size_t>(nnz, 1),
+                                                "cudaMalloc(ub_tagged)");
+  // chunks of the hierarchical main scan: the range holding each chunk's first row
+  ws.chunk_rows = cb::overlap_chunk_rows(N, D, ws.scan_grid);
+  std::vector<int> first((size_t)(((int64_t)N + ws.chunk_rows - 1) / ws.chunk_rows), 0);
+  {
+    size_t i = 0;
+    for (size_t c = 0; c < first.size(); ++c) {
+      const int64_t v = (int64_t)c * ws.chunk_rows;
+      while (i + 1 < nnz && all[i + 1].x <= v) ++i;
+      first[c] = (int)i;
+    }
+  }
+  int* d_first = (int*)dev_alloc(sizeof(int) * std::max<size_t>(first.size(), 1), "cudaMalloc(chunk table)");
+  ws.chunk_first_range = d_first;
   ws.flat_range = (int4*)dev_alloc(sizeof(int4), "cudaMalloc(flat_range)");
   ws.flat_packed = (unsigned long long*)dev_alloc(sizeof(unsigned long long), "cudaMalloc(flat_packed)");
   ws.ub_root = (float*)dev_alloc(sizeof(float) * R, "cudaMalloc(ub_root)");
@@ -207,14 +243,21 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
   dev_scores = (float*)dev_alloc(sizeof(float) * cb::KMAX, "cudaMalloc(scores)");
   dev_ids = (int*)dev_alloc(sizeof(int) * cb::KMAX, "cudaMalloc(ids)");
   dev_out_indirect = (void**)dev_alloc(2 * sizeof(void*), "cudaMalloc(out pointers)");
-  if (!ws.ctrl || !ws.main_ranges || !ws.flat_range || !ws.flat_packed || !ws.ub_root || !ws.ub_child ||
+  if (!ws.ctrl || !ws.epoch_counter || !ws.ub_tagged || !d_first || !ws.flat_range || !ws.flat_packed ||
+      !ws.ub_root || !ws.ub_child ||
       !ws.cta_lists || !dev_query || !dev_scores || !dev_ids || !dev_out_indirect)
     return false;
   const int4 fr = make_int4(0, 0, N, -1);
   const unsigned long long fp = (1ull << 32) | (unsigned long long)(uint32_t)N;
   if (!cuda_ok(cudaMemcpyAsync(ws.flat_range, &fr, sizeof(fr), cudaMemcpyHostToDevice, stream), "H2D flat range") ||
       !cuda_ok(cudaMemcpyAsync(ws.flat_packed, &fp, sizeof(fp), cudaMemcpyHostToDevice, stream), "H2D flat packed") ||
-      !cuda_ok(cudaMemsetAsync(ws.ctrl, 0, sizeof(cb::SearchCtrl), stream), "memset ctrl"))
+      !cuda_ok(cudaMemsetAsync(ws.ctrl, 0, sizeof(cb::SearchCtrl), stream), "memset ctrl") ||
+      !cuda_ok(cudaMemsetAsync(ws.epoch_counter, 0, sizeof(uint32_t), stream), "memset epoch") ||
+      !cuda_ok(cudaMemsetAsync(ws.ub_tagged, 0, sizeof(unsigned long long) * std::max<size_t>(nnz, 1), stream),
+               "memset bounds") ||
+      (!first.empty() && !cuda_ok(cudaMemcpyAsync(d_first, first.data(), sizeof(int) * first.size(),
+                                                  cudaMemcpyHostToDevice, stream),
+                                  "H2D chunk table")))
     return false;
   // pinned, device-mapped host staging for the blocking search: query, scores,
   // ids, ctrl header, call slots.  Graph replays read the query from it and
@@ -636,8 +679,10 @@ void circuit_index_opaque::fill_trace(const cb::SearchCtrl& c, circuit_trace_ex_
     t->best_root = c.best_root;
     t->seed_threshold = c.seed_T_key ? key_to_float(c.seed_T_key) : -std::numeric_limits<float>::infinity();
     t->seed_sample_rows = (int32_t)(uint32_t)c.seed_packed;
+    t->rows_streamed = (int32_t)c.rows_streamed;
   } else {
     t->vectors_scored = N;
+    t->rows_streamed = N;
     t->surviving_roots = R;
     t->surviving_children = -1;
     t->best_root = -1;

@@ -1,8 +1,9 @@
 // Single-query exact top-k search kernels for B200 (sm_100a).
 //
 // Pipeline for one query (all on one stream, no host synchronisation):
-//   memset(ctrl header)   (graph-replayed blocking calls: k_search_prologue,
-//                          which also stages the query)
+//   k_search_prologue  clears the control header and numbers the search (its
+//                 epoch); in graph-replayed blocking calls it also stages the
+//                 query
 //   k_root_scan   warp per root: q.c_r for every root, ||q||^2, argmax root
 //                 (the seed root); its last CTA scores an evenly spaced
 //                 sample of the seed root's rows (bulk copies into shared
@@ -12,15 +13,20 @@
 //                                                 root_bounds.cu:31-54)
 //   k_bounds      warp per root: rigorous root bound, rank-r projection of q
 //                 (basis staged in shared memory by TMA), rigorous child box
-//                 bounds, compaction of surviving children into leaf ranges.
+//                 bounds, published per child tagged with the search's epoch;
+//                 then (after the seed) the survivor counts of the trace.
 //                                               (reference: parent_projection.cu:125-178,
 //                                                 child_bounds.cu:11-83)
-//   k_scan<final> streams the surviving leaves (TMA bulk copies into a
+//   k_scan<final> streams the leaves child by child (TMA bulk copies into a
 //                 3..8-stage shared-memory ring, one producer warp, eight
 //                 consumer warps), fused top-k; its last CTA merges all lists
-//                 and writes scores / original ids.
+//                 and writes scores / original ids.  It runs BESIDE the bounds
+//                 kernel: a child whose bound is already published and below
+//                 the running threshold is skipped, any other child is
+//                 streamed, so the scan never waits for the bounds (the
+//                 reference scores only the survivors, after host syncs).
 //                                               (reference: dense_score.cu:116-164,
-//                                                 topk.cu:56-170, search.py:77-84)
+//                                                 topk.cu:56-170, search.py:63-84)
 // The flat path (small corpora) is the final scan over one range [0, N).
 #include <cmath>
 #include <cstdio>
@@ -67,6 +73,14 @@ struct ScanParams {
   unsigned long long* ctrl_out;               // (mapped host memory; null = no copy)
   const uint32_t* call_seq;                   // blocking calls: the call's number in the control header
   uint32_t* done_out;                         // mapped host word that receives it when the results are out
+  // hierarchical scans (all null / 0 for a flat scan)
+  const unsigned long long* ub_tagged;        // per range: epoch << 32 | bound key (see Workspace)
+  const uint32_t* epoch;                      // this search's epoch (control header)
+  const int* chunk_first_range;               // per chunk: the range holding its first row
+  uint32_t chunk_rows;                        // rows per chunk, with chunk_first_range
+  const float* T_ext;                         // a threshold from outside the index (or null)
+  uint32_t* rows_streamed;                    // rows read, summed over CTAs (or null)
+  int overlapped;                             // launched beside the bounds kernel (no wait before streaming)
 };
 
 template <int VPL> struct ScanShape {
@@ -133,8 +147,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
   const int theta_word = (int)(((uintptr_t)P.theta_key & 15u) >> 2);
   __shared__ int s_is_last, s_err;
   __shared__ unsigned long long s_pc;
-  __shared__ int4 s_rg0;
-  __shared__ uint32_t s_theta, s_rank_count, s_fin_count;
+  __shared__ uint32_t s_theta, s_rank_count, s_fin_count, s_text, s_epoch;
   __shared__ uint32_t s_warp_theta[SCAN_CONSUMER_WARPS];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -142,15 +155,26 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
   const int k = P.k;
 
   for (int i = tid; i < SCAN_CONSUMER_WARPS * SORTN; i += blockDim.x) topk_all[i] = 0ull;
-  // launched as a programmatic dependent of the kernel that writes its ranges
-  // (bounds) or clears its control words (search prologue): everything above
-  // overlaps that kernel, everything below reads its results
-  griddep_wait();
+  // A flat scan is a programmatic dependent of the search prologue, which
+  // clears its control words: it waits here.  A hierarchical scan is one of the
+  // bounds kernel, and everything it reads before its last CTA (the static
+  // range list, the query, the control words) was written by kernels that had
+  // completed before the bounds kernel was launched (the root scan waits for
+  // the prologue before it lets the bounds kernel start); the bounds it reads
+  // while they are being written carry the epoch, so it does not wait.
+  if (!P.overlapped) griddep_wait();
   if (tid == 0) {
     s_err = 0;
     s_fin_count = 0;
+    uint32_t tx = 0u;
+    if (P.T_ext) {
+      const float te = __ldcg(P.T_ext);
+      if (te > -INFINITY) tx = f2key(te);
+    }
+    s_text = tx;
+    if (tx && blockIdx.x == 0) atomicMax(P.theta_key, tx);
+    s_epoch = P.epoch ? ld_volatile_u32(P.epoch) : 0u;
     s_pc = ld_volatile_u64(P.packed_counts);
-    s_rg0 = __ldcg(P.ranges);  // entry 0 exists whenever ranges do; read beside the count
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], SCAN_CONSUMER_WARPS);
@@ -167,33 +191,37 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
 
   if (warp == SCAN_CONSUMER_WARPS) {
     // ------------------------------------------------------------ producer
-    // Work distribution.  A short stream is split into G equal slices.  A long
-    // one is cut into chunks of chunk_rows virtual rows that the CTAs take from
-    // a counter in the control block, one claim in flight ahead of the chunk
-    // being streamed: SMs do not stream at the same rate (measured at 100M rows,
-    // equal slices finished up to 17 % apart), and with claims the faster ones
-    // take more chunks, so all finish within about one chunk of each other.
-    const bool dyn = P.chunk_counter != nullptr && n_rows >= G * (uint32_t)(SCAN_DYN_CHUNKS * SCAN_DYN_MIN_STAGES * ROWS);
-    uint32_t chunk_rows = 0, next_claim = 0;
-    uint32_t vb, ve;  // the piece of the stream being streamed
+    // Work distribution.  A short flat stream is split into G equal slices.  A
+    // long one, and every hierarchical one, is cut into chunks of chunk_rows
+    // virtual rows that the CTAs take from a counter in the control block, one
+    // claim in flight ahead of the chunk being streamed: SMs do not stream at
+    // the same rate (measured at 100M rows, equal slices finished up to 17 %
+    // apart), and a hierarchical scan's CTAs start at different times (an SM
+    // running a root-scan or bounds CTA takes its scan CTA later), so the CTAs
+    // that stream more take more chunks and all finish within about a chunk of
+    // each other.
+    const bool table = P.chunk_first_range != nullptr;
+    const bool dyn = P.chunk_counter != nullptr &&
+                     (table || n_rows >= G * (uint32_t)(SCAN_DYN_CHUNKS * SCAN_DYN_MIN_STAGES * ROWS));
+    uint32_t chunk_rows = 0, n_chunks = 0, next_claim = 0;
+    uint32_t vb = 0, ve = 0;  // the piece of the stream being streamed
+    int next_s = -1;          // table: the range holding the claimed chunk's first row (-1 = not read yet)
     if (dyn) {
-      const uint32_t per = n_rows / (G * (uint32_t)SCAN_DYN_CHUNKS);
-      chunk_rows = max((uint32_t)(SCAN_DYN_MIN_STAGES * ROWS), (per + ROWS - 1) / ROWS * ROWS);
-      uint32_t c = 0;
-      if (lane == 0) c = atomicAdd(P.chunk_counter, 1u);
-      c = __shfl_sync(FULL_MASK, c, 0);
-      vb = (uint32_t)min((unsigned long long)n_rows, (unsigned long long)c * chunk_rows);
-      ve = min(n_rows, vb + chunk_rows);
-      if (lane == 0) next_claim = atomicAdd(P.chunk_counter, 1u);  // used when this chunk is done
+      if (table) {
+        chunk_rows = P.chunk_rows;
+      } else {
+        const uint32_t per = n_rows / (G * (uint32_t)SCAN_DYN_CHUNKS);
+        chunk_rows = max((uint32_t)(SCAN_DYN_MIN_STAGES * ROWS), (per + ROWS - 1) / ROWS * ROWS);
+      }
+      n_chunks = (n_rows + chunk_rows - 1) / chunk_rows;
     } else {
       vb = (uint32_t)(((unsigned long long)blockIdx.x * n_rows) / G);
       ve = (uint32_t)(((unsigned long long)(blockIdx.x + 1) * n_rows) / G);
     }
-    // the range holding virtual row vv, searched from range `lo` (whose entry
-    // is `rg` and starts at or before vv): a 32-way search by the whole warp
-    // (ranges sorted by .x), 3 L2 round trips for 4,096 ranges
+    // the range holding virtual row vv, searched from range `lo` (which starts
+    // at or before vv): a 32-way search by the whole warp (ranges sorted by
+    // .x), 3 L2 round trips for 4,096 ranges
     int s = 0;
-    int4 rg = s_rg0;  // entry 0 exists whenever ranges do; read beside the count
     const auto locate = [&](uint32_t vv, int lo) {
       int hi = (int)n_ranges - 1;
       while (hi > lo) {
@@ -201,51 +229,97 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
         const int pos = lo + lane * step;
         const int4 e = pos <= hi ? __ldcg(&P.ranges[pos]) : make_int4(0x7fffffff, 0, 0, 0);
         const int j = 31 - __clz(__ballot_sync(FULL_MASK, (uint32_t)e.x <= vv));
-        rg.x = __shfl_sync(FULL_MASK, e.x, j);  // the winner's entry: ranges[new lo]
-        rg.y = __shfl_sync(FULL_MASK, e.y, j);
-        rg.z = __shfl_sync(FULL_MASK, e.z, j);
-        rg.w = __shfl_sync(FULL_MASK, e.w, j);
         lo += j * step;
         hi = min(hi, lo + step - 1);
       }
       s = lo;
     };
-    if (vb < ve && n_ranges > 0) locate(vb, 0);
     // The whole warp walks the ranges: lane j holds entry base + j of the
     // current 32-entry window and of the next one (loaded a window ahead), so
     // moving from one child's rows to the next is a register shuffle; an L2
     // round trip happens once per 32 ranges and overlaps the stages in flight.
-    // Short children (a few rows each) no longer stall the stream.  Lane j
+    // Short children (a few rows each) do not stall the stream.  Lane j
     // records and issues the stage's run j, so up to 32 bulk copies per stage
     // go out in parallel.
+    // Pruning (hierarchical): each window lane also holds its range's bound key
+    // when the bounds kernel has published it for this search (the epoch in the
+    // same 64-bit word says so), else 0xffffffff.  A range is skipped when that
+    // key is below pkey = max(external threshold, the running threshold read at
+    // the start of the piece): every row of the child then scores below a value
+    // that never exceeds the final k-th best.
+    const bool prune = P.ub_tagged != nullptr;
+    const uint32_t epoch = s_epoch;
     const uint64_t policy = policy_evict_first();
     const void* theta_line = reinterpret_cast<const void*>((uintptr_t)P.theta_key & ~(uintptr_t)15);
     const char* leaf_bytes = reinterpret_cast<const char*>(P.leaf);
-    uint32_t v = vb;
+    const auto load_window = [&](int b, uint32_t& key) {
+      const int idx = b + lane;
+      const bool in = idx < (int)n_ranges;
+      key = 0xffffffffu;
+      if (prune && in) {
+        const unsigned long long t = __ldcg(&P.ub_tagged[idx]);
+        if ((uint32_t)(t >> 32) == epoch) key = (uint32_t)t;
+      }
+      return in ? __ldcg(&P.ranges[idx]) : make_int4(0, 0, 0, 0);
+    };
+    int base = 0;
+    int4 win = make_int4(0, 0, 0, 0), win_next = win, rg = win;
+    uint32_t ubk = 0xffffffffu, ubk_next = 0xffffffffu, rkey = 0xffffffffu, pkey = 0u;
+    bool bad_range = false;
+    const auto fail_range = [&]() {
+      if (lane == 0) atomicOr(P.err, ERR_BAD_RANGE);
+      bad_range = true;
+    };
+    // windows around range s for the piece starting at virtual row vb
+    const auto begin_piece = [&]() {
+      if (s < 0 || s >= (int)n_ranges) {
+        fail_range();
+        return;
+      }
+      base = s & ~31;
+      win = load_window(base, ubk);
+      win_next = load_window(base + 32, ubk_next);
+      if (prune) pkey = max(s_text, ld_volatile_u32(P.theta_key));
+      rg.x = __shfl_sync(FULL_MASK, win.x, s - base);
+      rg.y = __shfl_sync(FULL_MASK, win.y, s - base);
+      rg.z = __shfl_sync(FULL_MASK, win.z, s - base);
+      rg.w = __shfl_sync(FULL_MASK, win.w, s - base);
+      rkey = __shfl_sync(FULL_MASK, ubk, s - base);
+      if ((uint32_t)rg.x > vb) fail_range();  // the range must start at or before the piece
+    };
+    // takes the next claimed chunk (claimed one chunk ago) and claims the one
+    // after it; false when none is left
+    const auto next_chunk = [&](int from) {
+      const uint32_t c = __shfl_sync(FULL_MASK, next_claim, 0);
+      if (c >= n_chunks) return false;
+      vb = c * chunk_rows;  // < n_rows
+      ve = min(n_rows, vb + chunk_rows);
+      if (lane == 0) next_claim = atomicAdd(P.chunk_counter, 1u);
+      if (table) {
+        s = next_s >= 0 ? next_s : __ldcg(&P.chunk_first_range[c]);
+        next_s = -1;
+      } else {
+        locate(vb, from);  // later chunks lie at higher rows: search forward
+      }
+      begin_piece();
+      return true;
+    };
+    if (dyn) {
+      if (lane == 0) next_claim = atomicAdd(P.chunk_counter, 1u);
+      if (!next_chunk(0)) vb = ve = 0;
+    } else if (vb < ve && n_ranges > 0) {
+      locate(vb, 0);
+      begin_piece();
+    }
+    if (bad_range) ve = vb;
+    uint32_t v = vb, streamed = 0;
     int it = 0;
     bool ok = true;
-    int base = s & ~31;
-    const auto load_window = [&](int b) {
-      const int idx = b + lane;
-      return (vb < ve && idx < (int)n_ranges) ? __ldcg(&P.ranges[idx]) : make_int4(0, 0, 0, 0);
-    };
-    int4 win = load_window(base), win_next = load_window(base + 32);
-    bool bad_range = false;
     for (;;) {
       if (v >= ve) {
-        if (!dyn || bad_range) break;
-        // the next chunk: claimed a chunk ago; claim the one after it now
-        const uint32_t c = __shfl_sync(FULL_MASK, next_claim, 0);
-        const unsigned long long nvb = (unsigned long long)c * chunk_rows;
-        if (nvb >= n_rows) break;
-        vb = (uint32_t)nvb;
-        ve = min(n_rows, vb + chunk_rows);
+        if (!dyn || bad_range || !next_chunk(s)) break;
+        if (bad_range) break;
         v = vb;
-        if (lane == 0) next_claim = atomicAdd(P.chunk_counter, 1u);
-        locate(vb, s);  // later chunks lie at higher rows: search forward from the current range
-        base = s & ~31;
-        win = load_window(base);
-        win_next = load_window(base + 32);
       }
       const int stage = it % STAGES, f = it / STAGES;
       bool free_stage = true;
@@ -263,20 +337,25 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
         if (v >= (uint32_t)rg.x + rlen) {
           ++s;
           if (s >= (int)n_ranges) {
-            if (lane == 0) atomicOr(P.err, ERR_BAD_RANGE);
+            fail_range();
             v = ve;
-            bad_range = true;
             break;
           }
           if (s - base == 32) {
             base += 32;
             win = win_next;
-            win_next = load_window(base + 32);
+            ubk = ubk_next;
+            win_next = load_window(base + 32, ubk_next);
           }
           rg.x = __shfl_sync(FULL_MASK, win.x, s - base);
           rg.y = __shfl_sync(FULL_MASK, win.y, s - base);
           rg.z = __shfl_sync(FULL_MASK, win.z, s - base);
           rg.w = __shfl_sync(FULL_MASK, win.w, s - base);
+          rkey = __shfl_sync(FULL_MASK, ubk, s - base);
+          continue;
+        }
+        if (rkey < pkey) {  // the rest of this child is below the threshold
+          v = min(ve, (uint32_t)rg.x + rlen);
           continue;
         }
         const uint32_t row = (uint32_t)rg.y + (v - (uint32_t)rg.x);
@@ -292,6 +371,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
         n += (int)take;
         v += take;
       }
+      if (n == 0) continue;  // every child left in the piece was skipped: no stage
+      streamed += (uint32_t)n;
       // run j covers slots [start_j, start_{j+1}) (the last one up to n)
       const int next_slot = __shfl_down_sync(FULL_MASK, my_slot, 1);
       const int slot_end = (lane + 1 < nr) ? next_slot : n;
@@ -312,8 +393,16 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
                            (uint32_t)(slot_end - my_slot) * (uint32_t)P.row_bytes, &full[stage], policy);
       }
       ++it;
+      // with the stage's copies out: the range of the chunk claimed at the start
+      // of this one (its claim is back by now), so the next chunk starts without
+      // that round trip
+      if (table && next_s < 0) {
+        const uint32_t c2 = __shfl_sync(FULL_MASK, next_claim, 0);
+        if (c2 < n_chunks) next_s = __ldcg(&P.chunk_first_range[c2]);
+      }
     }
     if (lane == 0) {
+      if (P.rows_streamed && streamed) atomicAdd(P.rows_streamed, streamed);
       const int stage = it % STAGES, f = it / STAGES;
       if (ok && f > 0 && !mbar_wait(&empty[stage], (f - 1) & 1, P.err, ERR_TIMEOUT_EMPTY)) s_err = 1;
       stage_n[stage] = -1;
@@ -330,7 +419,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     }
     unsigned long long* tk = topk_all + warp * SORTN;
     uint32_t theta_w = 0;                                 // this warp's k-th best key
-    uint32_t theta = ld_volatile_u32(P.theta_key);        // filter key (max of both)
+    uint32_t theta = max(ld_volatile_u32(P.theta_key), s_text);  // filter key (max of both)
     int cnt = 0;                                          // buffered candidates
     uint32_t published = 0;
 
@@ -529,6 +618,10 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     __syncthreads();
   }
   if (!s_is_last) return;
+  // an overlapped scan does not finish before the bounds kernel (nor, through
+  // it, the root scan): later work on the stream and the control-header copy
+  // below see both complete
+  if (P.overlapped) griddep_wait();
   __threadfence();
 
   // ---------------------------------------------------------- grid merge (last CTA)
@@ -621,7 +714,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
 // after it are its programmatic dependents.
 __global__ void __launch_bounds__(128) k_search_prologue(const float4* q_host, void* const* slots, float4* dq, int D4,
                                                          unsigned long long* ctrl_hdr, void** out_indirect,
-                                                         const uint32_t* seq_in) {
+                                                         const uint32_t* seq_in, uint32_t* epoch_counter) {
   const int tid = threadIdx.x;
   const float4* src = q_host;
   if (slots) {
@@ -630,8 +723,19 @@ __global__ void __launch_bounds__(128) k_search_prologue(const float4* q_host, v
   }
   if (src)
     for (int i = tid; i < D4; i += blockDim.x) dq[i] = src[i];
-  if (tid < (int)(CTRL_RESET_BYTES / 8))
-    ctrl_hdr[tid] = (tid == CTRL_SEQ_WORD && seq_in) ? (unsigned long long)*seq_in : 0ull;
+  if (tid < (int)(CTRL_RESET_BYTES / 8)) {
+    unsigned long long w = 0ull;
+    if (tid == CTRL_SEQ_WORD && seq_in) w = *seq_in;
+    if (tid == CTRL_EPOCH_WORD && epoch_counter) {
+      // searches on one workspace run one after another: a plain increment;
+      // 0 is skipped, so a never-written bound entry (epoch 0) is never current
+      uint32_t e = *epoch_counter + 1u;
+      if (e == 0u) e = 1u;
+      *epoch_counter = e;
+      w = e;
+    }
+    ctrl_hdr[tid] = w;
+  }
 }
 
 // ============================================================ root scan (K1)
@@ -907,7 +1011,7 @@ __global__ void __launch_bounds__(ROOT_SCAN_WARPS * 32) k_root_scan(IndexView ix
   if (threadIdx.x == 0) {
     ctrl->seed_T_key = T;
     ctrl->seed_packed = (unsigned long long)(uint32_t)S;  // rows scored by the sample
-    if (T > ctrl->theta_key) ctrl->theta_key = T;
+    if (T) atomicMax(&ctrl->theta_key, T);  // the main scan may be raising it already
     if (T_export) *T_export = T ? key2f(T) : -INFINITY;
   }
 }
@@ -934,16 +1038,20 @@ __host__ __device__ inline BoundsLayout bounds_layout(int D, int rank, int chunk
 //     rigorous root bound, the projection a = V^T q with the basis staged by
 //     TMA, and every child's rigorous bound; all rounded up to float and kept
 //     in ub_root[R] / ub_child[C].  None of this depends on the threshold.
-//  2. after griddep_wait(): T = max(seed threshold, T_ext) is known; roots and
-//     children whose bound is below T are skipped, the survivors are compacted
-//     into leaf ranges (one packed 64-bit atomic per 32 children).
+//     Each child's min(root bound, child bound) is also published for the main
+//     scan, which runs beside this kernel: ub_tagged[CSR entry] = epoch << 32 |
+//     key, one 64-bit store, so the scan sees either this search's bound or a
+//     stale epoch (and then streams the child).
+//  2. after griddep_wait(): T = max(seed threshold, T_ext) is known; the roots,
+//     children and rows whose bound is not below T are counted for the trace
+//     (what a scan of the survivors alone would read).
 // T_ext (optional): a threshold from outside this index (the max of all shards'
-// seed thresholds); the bounds and the main scan use max(own seed, T_ext).
+// seed thresholds); the main scan prunes with it too.
 __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, const float* __restrict__ q,
                                                                SearchCtrl* ctrl, float* __restrict__ ub_root,
                                                                float* __restrict__ ub_child,
-                                                               int4* __restrict__ main_ranges, int chunk_rows,
-                                                               const float* __restrict__ T_ext) {
+                                                               unsigned long long* __restrict__ ub_tagged,
+                                                               int chunk_rows, const float* __restrict__ T_ext) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_abort;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -961,6 +1069,7 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
   // the query was complete before the kernel this one depends on was launched
   // (an earlier kernel of the search, or the caller's own work): read through L2
   for (int i = threadIdx.x; i < D; i += blockDim.x) sq[i] = __ldcg(q + i);
+  const unsigned long long tag = (unsigned long long)ld_volatile_u32(&ctrl->epoch) << 32;
   if (threadIdx.x == 0) s_abort = 0;
   if (lane == 0) {
     mbar_init(&bars[0], 1);
@@ -1004,7 +1113,8 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
     const double e_leaf = gD * QN * (cn + rad);   // |fl(q.x) - q.x| for ||x|| <= ||c|| + rad
     double ub_r = dot + e_dot + QN * rad + e_leaf;
     ub_r += 1e-12 * (fabs(dot) + QN * rad + e_dot + e_leaf);
-    if (lane == 0) ub_root[p] = __double2float_ru(ub_r);
+    const float ub_rf = __double2float_ru(ub_r);  // the same in every lane (butterfly sums)
+    if (lane == 0) ub_root[p] = ub_rf;
     // the children's boxes and radii are read after the projection: start
     // bringing them into L2 while the basis copies are in flight
     const int cb = ix.root_child_ptr[p], ce = ix.root_child_ptr[p + 1];
@@ -1126,7 +1236,11 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
       const double rho = (double)ix.child_radii[c];
       double ub = dot + e_dot + box + ebox + an * E * sqrt(wn2) * (1.0 + 1e-15) + perp * rho + e_leaf;
       ub += 1e-12 * (fabs(dot) + fabs(box) + perp * rho + e_dot + e_leaf + ebox);
-      ub_child[c] = __double2float_ru(ub);
+      const float ub_cf = __double2float_ru(ub);
+      ub_child[c] = ub_cf;
+      // a NaN bound (NaN query) is never published: the child is streamed
+      const float m = fminf(ub_cf, ub_rf);
+      if (!isnan(ub_cf) && !isnan(ub_rf)) ub_tagged[ci] = tag | f2key(m);
     }
     __syncwarp();  // sa / ss are rewritten for the next root
   }
@@ -1144,13 +1258,11 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
     if (te > -INFINITY) {
       const uint32_t ek = f2key(te);
       if (ek > Tkey) Tkey = ek;
-      // the main scan starts from the raised threshold (it runs after this kernel)
-      if (blockIdx.x == 0 && threadIdx.x == 0) atomicMax(&ctrl->theta_key, ek);
     }
   }
   const float T = Tkey ? key2f(Tkey) : -INFINITY;
   const bool keep_all = s_abort != 0;
-  uint32_t surv_roots = 0, surv_children = 0;
+  uint32_t surv_roots = 0, surv_children = 0, surv_rows = 0;
   for (int p = blockIdx.x * BOUNDS_WARPS + warp; p < ix.R; p += gridDim.x * BOUNDS_WARPS) {
     if (ix.root_rows[p] == 0) continue;
     if (!keep_all && __ldcg(ub_root + p) < T) continue;
@@ -1159,33 +1271,22 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
     for (int c0 = cb; c0 < ce; c0 += 32) {
       const int ci = c0 + lane;
       bool surv = false;
-      int c = -1, off = 0, size = 0;
+      int size = 0;
       if (ci < ce) {
-        c = ix.root_child_list[ci];
-        off = ix.leaf_offsets[c];
-        size = ix.leaf_sizes[c];
+        const int c = ix.root_child_list[ci];
         surv = keep_all || !(__ldcg(ub_child + c) < T);
+        size = surv ? ix.leaf_sizes[c] : 0;
       }
-      const uint32_t bal = __ballot_sync(FULL_MASK, surv);
-      const int rows_l = surv ? size : 0;
-      const int incl = warp_incl_scan(rows_l, lane);
-      const int total = __shfl_sync(FULL_MASK, incl, 31);
-      const int nsurv = __popc(bal);
-      unsigned long long old = 0ull;
-      if (lane == 0 && nsurv)
-        old = atomicAdd(&ctrl->main_packed, ((unsigned long long)nsurv << 32) | (unsigned long long)(uint32_t)total);
-      old = __shfl_sync(FULL_MASK, old, 0);
-      if (surv) {
-        const uint32_t slot = (uint32_t)(old >> 32) + __popc(bal & lanemask_lt());
-        const uint32_t vbegin = (uint32_t)old + (uint32_t)(incl - size);
-        main_ranges[slot] = make_int4((int)vbegin, off, off + size, c);
-      }
-      surv_children += (uint32_t)nsurv;
+      surv_children += (uint32_t)__popc(__ballot_sync(FULL_MASK, surv));
+      surv_rows += (uint32_t)__shfl_sync(FULL_MASK, warp_incl_scan(size, lane), 31);
     }
   }
   if (lane == 0) {
     if (surv_roots) atomicAdd(&ctrl->n_surv_roots, surv_roots);
-    if (surv_children) atomicAdd(&ctrl->n_surv_children, surv_children);
+    if (surv_children) {
+      atomicAdd(&ctrl->n_surv_children, surv_children);
+      atomicAdd(&ctrl->main_packed, ((unsigned long long)surv_children << 32) | (unsigned long long)surv_rows);
+    }
   }
 }
 
@@ -1252,6 +1353,14 @@ static int stages_for(int vpl, int row_bytes) {
   const size_t sb = align_up((size_t)rows_per_stage(vpl) * row_bytes, 128);
   int s = (int)(147456 / sb);
   return s < 2 ? 2 : (s > MAX_STAGES ? MAX_STAGES : s);
+}
+
+int overlap_chunk_rows(int N, int D, int grid) {
+  const long long rows = rows_per_stage(vpl_bucket(D / 4));
+  const long long parts = (long long)(grid > 0 ? grid : 1) * SCAN_DYN_CHUNKS;
+  const long long per = ((long long)N + parts - 1) / parts;
+  const long long c = (per + rows - 1) / rows * rows;
+  return (int)(c > 2 * rows ? c : 2 * rows);
 }
 
 int scan_smem_bytes(int D) {
@@ -1358,7 +1467,8 @@ static cudaError_t search_reset(const IndexView& ix, const Workspace& ws, const 
                                            io ? io->slots : nullptr,
                                            reinterpret_cast<float4*>(const_cast<float*>(q)), ix.D4,
                                            reinterpret_cast<unsigned long long*>(ws.ctrl),
-                                           io ? io->out_indirect : nullptr, io ? io->seq_in : nullptr);
+                                           io ? io->out_indirect : nullptr, io ? io->seq_in : nullptr,
+                                           ws.epoch_counter);
   return cudaGetLastError();
 }
 
@@ -1394,12 +1504,19 @@ cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const
   int grid_b = (ix.R + BOUNDS_WARPS - 1) / BOUNDS_WARPS;
   if (grid_b > 2 * ws.scan_grid) grid_b = 2 * ws.scan_grid;
   if ((e = launch_dependent(k_bounds, grid_b, BOUNDS_WARPS * 32, BL.total, stream, ix, q, ws.ctrl, ws.ub_root,
-                            ws.ub_child, ws.main_ranges, chunk_rows, T_ext)) != cudaSuccess)
+                            ws.ub_child, ws.ub_tagged, chunk_rows, T_ext)) != cudaSuccess)
     return e;
   ScanParams M = scan_params(ix, ws, q, k, out_scores, out_ids, out_rows);
-  M.ranges = ws.main_ranges;
-  M.packed_counts = &ws.ctrl->main_packed;
+  M.ranges = ix.all_ranges;
+  M.packed_counts = ix.all_packed;
   M.done = &ws.ctrl->main_done;
+  M.ub_tagged = ws.ub_tagged;
+  M.epoch = &ws.ctrl->epoch;
+  M.chunk_first_range = ws.chunk_first_range;
+  M.chunk_rows = (uint32_t)ws.chunk_rows;
+  M.T_ext = T_ext;
+  M.rows_streamed = &ws.ctrl->rows_streamed;
+  M.overlapped = 1;
   final_io(M, ws, io);
   if (ev_scan0) cudaEventRecord(ev_scan0, stream);
   e = launch_scan(M, ws.scan_grid, stream);

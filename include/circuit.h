@@ -22,8 +22,10 @@
  *     prunes with rigorously inflated bounds; the reference native path runs
  *     with threshold -1e9 (gpu_index.cpp:279) and never prunes.  Results are
  *     identical to brute force in both.
- *   - circuit_trace_t.vectors_scored counts the leaf rows actually scored
- *     (reference always reports N, gpu_index.cpp:326).
+ *   - circuit_trace_t.vectors_scored counts the rows of the children that
+ *     survive the seed threshold's bounds (reference always reports N,
+ *     gpu_index.cpp:326); circuit_trace_ex_t.rows_streamed counts the rows the
+ *     scan actually read.
  *   - errors return a negative CIRCUIT_ERR_* code (reference returns 0 even
  *     when CUDA calls fail); circuit_last_error() describes the last one.
  *
@@ -75,7 +77,8 @@ typedef struct {
 typedef struct {
   float latency_us;            /* host wall time of the call (0 for async calls) */
   int32_t path;                /* 0 = flat scan, 1 = hierarchical */
-  int64_t vectors_scored;      /* leaf rows scanned for the result (rows of surviving children) */
+  int64_t vectors_scored;      /* rows of the children whose bound is not below the seed threshold:
+                                  what a scan of the survivors alone reads (flat path: N) */
   int64_t vectors_total;       /* N */
   int32_t surviving_roots;     /* roots not pruned (seed root included) */
   int32_t surviving_children;  /* non-empty children scanned */
@@ -86,6 +89,12 @@ typedef struct {
   int32_t seed_sample_rows;    /* rows of the seed root scored beforehand for the threshold (not in
                                   vectors_scored; scanned again when their children survive);
                                   ABI version 2 */
+  int32_t rows_streamed;       /* leaf rows the main scan read.  The hierarchical scan runs beside the
+                                  bounds kernel and streams every child whose bound is not known yet,
+                                  then skips the children whose bound is below the running threshold
+                                  (which rises above the seed's): more rows than vectors_scored on
+                                  small corpora, which stream whole before the bounds are ready, and
+                                  at most as many once the bounds lead the scan.  ABI version 2 */
 } circuit_trace_ex_t;
 
 /* ------------------------------------------------------------------ reference ABI */
