@@ -61,8 +61,8 @@ struct SearchCtrl {
   unsigned long long best_packed;  // argmax root: prio<<62 | key<<30 | (2^30-1-root)
   unsigned long long seed_packed;  // rows scored by the seed sample
   unsigned long long main_packed;  // children kept by the seed threshold << 32 | their rows (atomicAdd)
-  uint32_t k1_done;                // last-CTA tickets
-  uint32_t seed_done;
+  uint32_t k1_done;                // last-CTA tickets (root scan, main scan)
+  uint32_t pad0;
   uint32_t main_done;
   uint32_t theta_key;              // running global threshold key (atomicMax)
   uint32_t seed_T_key;             // k-th best key of the seed rows (0 = none)
@@ -72,7 +72,7 @@ struct SearchCtrl {
   int best_root;
   int error;                       // cb::ERR_* bits
   uint32_t call_seq;               // blocking calls: the call's sequence number (see HostIO)
-  uint32_t chunk_next;             // the main scan's next chunk to claim
+  uint32_t chunk_next;             // a long flat scan's next chunk to claim
   uint32_t epoch;                  // this search's number (tags the bounds it computes; never 0)
   uint32_t rows_streamed;          // leaf rows the main scan read (atomicAdd per CTA)
   uint32_t pad[4];
@@ -81,6 +81,22 @@ constexpr int CTRL_SEQ_WORD = 8;   // 64-bit word of the header: call_seq (low h
 constexpr int CTRL_EPOCH_WORD = 9; // epoch (low half), rows_streamed (high, zero)
 constexpr size_t CTRL_RESET_BYTES = 96;
 static_assert(sizeof(SearchCtrl) == CTRL_RESET_BYTES, "ctrl layout");
+
+// Per-search words of the hierarchical main scan and the bounds kernel that
+// take many atomics while both run, each group on its own 128-byte line, away
+// from the control header (whose running threshold every consumer warp
+// raises); cleared by the search prologue.
+struct alignas(128) ScanSync {
+  // chunks claimed in order (low half); the bounds kernel adds 1 to the high
+  // half once its live-chunk list is complete
+  unsigned long long chunk_claims;
+  uint32_t list_next;              // the next live-list entry to claim
+  uint32_t pad_a[29];
+  uint32_t n_live;                 // chunks in the live list
+  uint32_t bounds_done;            // the bounds kernel's last-CTA ticket
+  uint32_t pad_b[30];
+};
+static_assert(sizeof(ScanSync) == 256, "sync layout");
 
 // Read-only device view of one index (all pointers are device pointers).
 struct IndexView {
@@ -102,6 +118,7 @@ struct IndexView {
   const int4* seed_tab;         // [R * SEED_TAB_W] the seed sample of each root for k <= 32 (see below)
   const int4* all_ranges;       // [nnz] every CSR entry in order: {first virtual row, leaf row begin, end, child}
   const unsigned long long* all_packed;  // [1] nnz << 32 | N
+  int all_nnz;                  // entries of all_ranges
   const int* root_rows;         // [R]  leaf rows under each root
   const double* root_cn;        // [R]  upper bound of ||c_r||
   const double* root_defect;    // [R]  upper bound of ||V_r^T V_r - I||_2
@@ -111,6 +128,7 @@ struct IndexView {
 // Device workspace owned by one index handle (one in-flight search at a time).
 struct Workspace {
   SearchCtrl* ctrl;
+  ScanSync* sync;
   uint32_t* epoch_counter;           // [1] the last search's epoch (not cleared between searches)
   int4* flat_range;                  // [1] = {0, 0, N, -1}
   unsigned long long* flat_packed;   // [1] = 1<<32 | N
@@ -121,6 +139,10 @@ struct Workspace {
   unsigned long long* ub_tagged;
   const int* chunk_first_range;      // [n_chunks] the all_ranges entry holding each chunk's first row
   int chunk_rows;                    // rows per chunk of the hierarchical main scan
+  int n_chunks;
+  uint32_t* chunk_mark;              // [n_chunks] epoch of the last search that listed the chunk as live
+  int* live_list;                    // [n_chunks] the live chunks of this search (ctrl->n_live of them)
+  uint32_t* chunk_taken;             // [n_chunks] epoch of the last search that streamed the chunk
   unsigned long long* cta_lists;     // [scan_grid * KMAX]
   int scan_grid;
 };
@@ -217,7 +239,8 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
 
 int scan_smem_bytes(int D);
 // Rows per chunk of the hierarchical main scan over N rows of dimension D on
-// `grid` CTAs: a multiple of the rows of one ring stage, about 48 chunks per CTA.
+// `grid` CTAs: a multiple of the rows of one ring stage (at least 4 stages),
+// about 48 chunks per CTA.
 int overlap_chunk_rows(int N, int D, int grid);
 // One kernel whose mbarrier wait nothing satisfies, run through the bounded
 // wait every search kernel uses: after the limit it or-s ERR_TIMEOUT_FULL into

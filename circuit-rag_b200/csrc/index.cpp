@@ -209,6 +209,7 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
   view.seed_tab = d_tab;
   view.all_ranges = d_all;
   view.all_packed = d_all_packed;
+  view.all_nnz = (int)nnz;
   view.root_rows = d_rows;
   view.root_cn = d_cn;
   view.root_defect = d_def;
@@ -218,6 +219,7 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
   ws.scan_grid = cb::sm_count(device);
   ws.ctrl = (cb::SearchCtrl*)dev_alloc(sizeof(cb::SearchCtrl), "cudaMalloc(ctrl)");
   ws.epoch_counter = (uint32_t*)dev_alloc(sizeof(uint32_t), "cudaMalloc(epoch)");
+  ws.sync = (cb::ScanSync*)dev_alloc(sizeof(cb::ScanSync), "cudaMalloc(scan sync)");
   ws.ub_tagged = (unsigned long long*)dev_alloc(sizeof(unsigned long long) * std::max<size_t>(nnz, 1),
                                                 "cudaMalloc(ub_tagged)");
   // chunks of the hierarchical main scan: the range holding each chunk's first row
@@ -233,6 +235,10 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
   }
   int* d_first = (int*)dev_alloc(sizeof(int) * std::max<size_t>(first.size(), 1), "cudaMalloc(chunk table)");
   ws.chunk_first_range = d_first;
+  ws.n_chunks = (int)first.size();
+  ws.chunk_mark = (uint32_t*)dev_alloc(sizeof(uint32_t) * std::max<size_t>(first.size(), 1), "cudaMalloc(chunk marks)");
+  ws.live_list = (int*)dev_alloc(sizeof(int) * std::max<size_t>(first.size(), 1), "cudaMalloc(live list)");
+  ws.chunk_taken = (uint32_t*)dev_alloc(sizeof(uint32_t) * std::max<size_t>(first.size(), 1), "cudaMalloc(taken)");
   ws.flat_range = (int4*)dev_alloc(sizeof(int4), "cudaMalloc(flat_range)");
   ws.flat_packed = (unsigned long long*)dev_alloc(sizeof(unsigned long long), "cudaMalloc(flat_packed)");
   ws.ub_root = (float*)dev_alloc(sizeof(float) * R, "cudaMalloc(ub_root)");
@@ -243,7 +249,9 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
   dev_scores = (float*)dev_alloc(sizeof(float) * cb::KMAX, "cudaMalloc(scores)");
   dev_ids = (int*)dev_alloc(sizeof(int) * cb::KMAX, "cudaMalloc(ids)");
   dev_out_indirect = (void**)dev_alloc(2 * sizeof(void*), "cudaMalloc(out pointers)");
-  if (!ws.ctrl || !ws.epoch_counter || !ws.ub_tagged || !d_first || !ws.flat_range || !ws.flat_packed ||
+  if (!ws.ctrl || !ws.sync || !ws.epoch_counter || !ws.ub_tagged || !d_first || !ws.chunk_mark || !ws.live_list ||
+      !ws.chunk_taken ||
+      !ws.flat_range || !ws.flat_packed ||
       !ws.ub_root || !ws.ub_child ||
       !ws.cta_lists || !dev_query || !dev_scores || !dev_ids || !dev_out_indirect)
     return false;
@@ -253,6 +261,11 @@ bool circuit_index_opaque::finish_setup(const int* parent, const int* offsets, c
       !cuda_ok(cudaMemcpyAsync(ws.flat_packed, &fp, sizeof(fp), cudaMemcpyHostToDevice, stream), "H2D flat packed") ||
       !cuda_ok(cudaMemsetAsync(ws.ctrl, 0, sizeof(cb::SearchCtrl), stream), "memset ctrl") ||
       !cuda_ok(cudaMemsetAsync(ws.epoch_counter, 0, sizeof(uint32_t), stream), "memset epoch") ||
+      !cuda_ok(cudaMemsetAsync(ws.sync, 0, sizeof(cb::ScanSync), stream), "memset scan sync") ||
+      !cuda_ok(cudaMemsetAsync(ws.chunk_mark, 0, sizeof(uint32_t) * std::max<size_t>(first.size(), 1), stream),
+               "memset chunk marks") ||
+      !cuda_ok(cudaMemsetAsync(ws.chunk_taken, 0, sizeof(uint32_t) * std::max<size_t>(first.size(), 1), stream),
+               "memset taken") ||
       !cuda_ok(cudaMemsetAsync(ws.ub_tagged, 0, sizeof(unsigned long long) * std::max<size_t>(nnz, 1), stream),
                "memset bounds") ||
       (!first.empty() && !cuda_ok(cudaMemcpyAsync(d_first, first.data(), sizeof(int) * first.size(),

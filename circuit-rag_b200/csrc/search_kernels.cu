@@ -53,7 +53,8 @@ struct ScanParams {
   const float* leaf;                          // [N, D]
   const float* q;                             // [D]
   const int4* ranges;                         // {vbegin, row_begin, row_end, child}
-  const unsigned long long* packed_counts;    // n_ranges << 32 | n_rows
+  const unsigned long long* packed_counts;    // n_ranges << 32 | n_rows (read when packed_value is 0)
+  unsigned long long packed_value;            // the same, when the host knows it
   uint32_t* theta_key;                        // running global threshold (atomicMax)
   unsigned long long* cta_lists;              // [(gridDim.x + 1) * k]
   uint32_t* done;                             // last-CTA ticket
@@ -78,6 +79,11 @@ struct ScanParams {
   const uint32_t* epoch;                      // this search's epoch (control header)
   const int* chunk_first_range;               // per chunk: the range holding its first row
   uint32_t chunk_rows;                        // rows per chunk, with chunk_first_range
+  unsigned long long* chunk_claims;           // in-order claims; high half set once the live list is complete
+  const int* live_list;                       // chunks listed by the bounds kernel
+  const uint32_t* n_live;
+  uint32_t* list_next;
+  uint32_t* chunk_taken;                      // per chunk: epoch of the search that streams it
   const float* T_ext;                         // a threshold from outside the index (or null)
   uint32_t* rows_streamed;                    // rows read, summed over CTAs (or null)
   int overlapped;                             // launched beside the bounds kernel (no wait before streaming)
@@ -163,18 +169,24 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
   // the prologue before it lets the bounds kernel start); the bounds it reads
   // while they are being written carry the epoch, so it does not wait.
   if (!P.overlapped) griddep_wait();
+  // the producer's first chunk is chunk blockIdx.x (see below): its table entry
+  // is requested before the shared-memory set-up
+  int first_range = -1;
+  if (warp == SCAN_CONSUMER_WARPS && P.chunk_first_range && P.packed_value &&
+      blockIdx.x < ((uint32_t)P.packed_value + P.chunk_rows - 1) / P.chunk_rows)
+    first_range = __ldcg(P.chunk_first_range + blockIdx.x);
   if (tid == 0) {
+    // (independent loads, in flight together)
+    const float te = P.T_ext ? __ldcg(P.T_ext) : -INFINITY;
+    const uint32_t ep = P.epoch ? __ldcg(P.epoch) : 0u;
+    const unsigned long long pc = P.packed_value ? P.packed_value : __ldcg(P.packed_counts);
     s_err = 0;
     s_fin_count = 0;
-    uint32_t tx = 0u;
-    if (P.T_ext) {
-      const float te = __ldcg(P.T_ext);
-      if (te > -INFINITY) tx = f2key(te);
-    }
+    const uint32_t tx = te > -INFINITY ? f2key(te) : 0u;
     s_text = tx;
     if (tx && blockIdx.x == 0) atomicMax(P.theta_key, tx);
-    s_epoch = P.epoch ? ld_volatile_u32(P.epoch) : 0u;
-    s_pc = ld_volatile_u64(P.packed_counts);
+    s_epoch = ep;
+    s_pc = pc;
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], SCAN_CONSUMER_WARPS);
@@ -193,19 +205,27 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     // ------------------------------------------------------------ producer
     // Work distribution.  A short flat stream is split into G equal slices.  A
     // long one, and every hierarchical one, is cut into chunks of chunk_rows
-    // virtual rows that the CTAs take from a counter in the control block, one
-    // claim in flight ahead of the chunk being streamed: SMs do not stream at
-    // the same rate (measured at 100M rows, equal slices finished up to 17 %
-    // apart), and a hierarchical scan's CTAs start at different times (an SM
-    // running a root-scan or bounds CTA takes its scan CTA later), so the CTAs
-    // that stream more take more chunks and all finish within about a chunk of
-    // each other.
+    // virtual rows that the CTAs claim from a counter in the control block:
+    // SMs do not stream at the same rate (measured at 100M rows, equal slices
+    // finished up to 17 % apart), and a hierarchical scan's CTAs start at
+    // different times (an SM running a root-scan or bounds CTA takes its scan
+    // CTA later), so the CTAs that stream more take more chunks and all finish
+    // within about a chunk of each other.
+    // CTA b starts with chunk b; claim c stands for chunk G + c.
+    // Hierarchical scans claim chunks in order while the bounds are being
+    // computed.  The bounds kernel marks the chunks that hold a child whose
+    // bound is not below the seed threshold, lists the marked chunks not taken
+    // yet and then adds 1 to the high half of the claim word: a CTA whose claim
+    // returns a non-zero high half takes its chunks from the list from then on,
+    // so dead chunks cost nothing.  A chunk
+    // can reach one CTA in order and another from the list: whoever swaps this
+    // search's epoch into its taken word first streams it, so each chunk is
+    // streamed once, and every listed chunk is streamed.
     const bool table = P.chunk_first_range != nullptr;
-    const bool dyn = P.chunk_counter != nullptr &&
-                     (table || n_rows >= G * (uint32_t)(SCAN_DYN_CHUNKS * SCAN_DYN_MIN_STAGES * ROWS));
-    uint32_t chunk_rows = 0, n_chunks = 0, next_claim = 0;
+    const bool dyn = table || (P.chunk_counter != nullptr &&
+                               n_rows >= G * (uint32_t)(SCAN_DYN_CHUNKS * SCAN_DYN_MIN_STAGES * ROWS));
+    uint32_t chunk_rows = 0, n_chunks = 0;
     uint32_t vb = 0, ve = 0;  // the piece of the stream being streamed
-    int next_s = -1;          // table: the range holding the claimed chunk's first row (-1 = not read yet)
     if (dyn) {
       if (table) {
         chunk_rows = P.chunk_rows;
@@ -221,7 +241,6 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     // the range holding virtual row vv, searched from range `lo` (which starts
     // at or before vv): a 32-way search by the whole warp (ranges sorted by
     // .x), 3 L2 round trips for 4,096 ranges
-    int s = 0;
     const auto locate = [&](uint32_t vv, int lo) {
       int hi = (int)n_ranges - 1;
       while (hi > lo) {
@@ -232,7 +251,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
         lo += j * step;
         hi = min(hi, lo + step - 1);
       }
-      s = lo;
+      return lo;
     };
     // The whole warp walks the ranges: lane j holds entry base + j of the
     // current 32-entry window and of the next one (loaded a window ahead), so
@@ -244,82 +263,170 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     // Pruning (hierarchical): each window lane also holds its range's bound key
     // when the bounds kernel has published it for this search (the epoch in the
     // same 64-bit word says so), else 0xffffffff.  A range is skipped when that
-    // key is below pkey = max(external threshold, the running threshold read at
-    // the start of the piece): every row of the child then scores below a value
-    // that never exceeds the final k-th best.
+    // key is below pkey = max(external threshold, the running threshold read
+    // before the piece): every row of the child then scores below a value that
+    // never exceeds the final k-th best.
     const bool prune = P.ub_tagged != nullptr;
     const uint32_t epoch = s_epoch;
     const uint64_t policy = policy_evict_first();
     const void* theta_line = reinterpret_cast<const void*>((uintptr_t)P.theta_key & ~(uintptr_t)15);
     const char* leaf_bytes = reinterpret_cast<const char*>(P.leaf);
-    const auto load_window = [&](int b, uint32_t& key) {
+    // a window: lane j's range entry and its raw tagged bound (decoded only
+    // when the window becomes current, so that loading it never stalls)
+    const auto load_window = [&](int b, unsigned long long& tag) {
       const int idx = b + lane;
       const bool in = idx < (int)n_ranges;
-      key = 0xffffffffu;
-      if (prune && in) {
-        const unsigned long long t = __ldcg(&P.ub_tagged[idx]);
-        if ((uint32_t)(t >> 32) == epoch) key = (uint32_t)t;
-      }
+      tag = (prune && in) ? __ldcg(&P.ub_tagged[idx]) : 0ull;
       return in ? __ldcg(&P.ranges[idx]) : make_int4(0, 0, 0, 0);
     };
-    int base = 0;
+    const auto decode = [&](unsigned long long t) {
+      return (prune && (uint32_t)(t >> 32) == epoch) ? (uint32_t)t : 0xffffffffu;
+    };
+    int s = 0, base = 0;
     int4 win = make_int4(0, 0, 0, 0), win_next = win, rg = win;
-    uint32_t ubk = 0xffffffffu, ubk_next = 0xffffffffu, rkey = 0xffffffffu, pkey = 0u;
+    unsigned long long tag_cur = 0ull, tag_next = 0ull;
+    uint32_t ubk = 0xffffffffu, rkey = 0xffffffffu, pkey = 0u;
     bool bad_range = false;
     const auto fail_range = [&]() {
       if (lane == 0) atomicOr(P.err, ERR_BAD_RANGE);
       bad_range = true;
     };
-    // windows around range s for the piece starting at virtual row vb
-    const auto begin_piece = [&]() {
-      if (s < 0 || s >= (int)n_ranges) {
-        fail_range();
-        return;
-      }
-      base = s & ~31;
-      win = load_window(base, ubk);
-      win_next = load_window(base + 32, ubk_next);
-      if (prune) pkey = max(s_text, ld_volatile_u32(P.theta_key));
+    const auto set_range = [&]() {  // rg / rkey from the windows
       rg.x = __shfl_sync(FULL_MASK, win.x, s - base);
       rg.y = __shfl_sync(FULL_MASK, win.y, s - base);
       rg.z = __shfl_sync(FULL_MASK, win.z, s - base);
       rg.w = __shfl_sync(FULL_MASK, win.w, s - base);
       rkey = __shfl_sync(FULL_MASK, ubk, s - base);
-      if ((uint32_t)rg.x > vb) fail_range();  // the range must start at or before the piece
     };
-    // takes the next claimed chunk (claimed one chunk ago) and claims the one
-    // after it; false when none is left
-    const auto next_chunk = [&](int from) {
-      const uint32_t c = __shfl_sync(FULL_MASK, next_claim, 0);
-      if (c >= n_chunks) return false;
-      vb = c * chunk_rows;  // < n_rows
-      ve = min(n_rows, vb + chunk_rows);
-      if (lane == 0) next_claim = atomicAdd(P.chunk_counter, 1u);
-      if (table) {
-        s = next_s >= 0 ? next_s : __ldcg(&P.chunk_first_range[c]);
-        next_s = -1;
-      } else {
-        locate(vb, from);  // later chunks lie at higher rows: search forward
+
+    // ---- chunk claims: one claim in flight (lane 0), resolved a chunk ahead
+    unsigned long long pend = 0ull;
+    bool list_mode = false;
+    uint32_t n_live = 0;
+    const auto claim = [&]() {
+      if (lane == 0) {
+        if (!table) pend = atomicAdd(P.chunk_counter, 1u);
+        else if (!list_mode) pend = atomicAdd(P.chunk_claims, 1ull);
+        else pend = atomicAdd(P.list_next, 1u);
       }
-      begin_piece();
-      return true;
+    };
+    // the chunk that the claim in flight gives (claiming again where it gives
+    // none), with the following claim issued; -1 = none left.  The chunk still
+    // has to be won through its taken word (hierarchical scans).
+    const auto resolve = [&]() -> int {
+      for (uint32_t guard = 0; guard <= 2 * n_chunks + 2; ++guard) {
+        const unsigned long long r = __shfl_sync(FULL_MASK, pend, 0);
+        if (!list_mode) {
+          if ((r >> 32) == 0ull) {
+            const uint32_t lo = (uint32_t)r + G;
+            if (lo >= n_chunks) return -1;
+            claim();
+            return (int)lo;
+          }
+          // the list is complete (the bounds kernel fenced it before the add)
+          __threadfence();
+          n_live = ld_volatile_u32(P.n_live);
+          list_mode = true;
+          claim();
+          continue;
+        }
+        const uint32_t i = (uint32_t)r;
+        if (i >= n_live) return -1;
+        const uint32_t j = (uint32_t)__ldcg(P.live_list + i);
+        claim();
+        if (j < n_chunks) return (int)j;
+      }
+      return -1;
+    };
+    // the next chunk, prepared one step per issued stage: 0 = nothing yet,
+    // 1 = chunk known, its taken word swapped and its first range requested,
+    // 2 = its windows and the threshold requested, 3 = no chunk left; the swap
+    // is checked when the chunk is taken (a lost chunk is dropped then)
+    int pf = 0, nj = -1, ns = -1, pbase = 0;
+    uint32_t taken_old = 0u;
+    int4 pw = make_int4(0, 0, 0, 0), pw2 = pw;
+    unsigned long long pt = 0ull, pt2 = 0ull;
+    uint32_t ppkey = 0u;
+    const auto prefetch = [&]() {
+      if (pf == 0) {
+        nj = resolve();
+        if (nj < 0) {
+          pf = 3;
+          return;
+        }
+        if (table) {
+          if (lane == 0) taken_old = atomicExch(P.chunk_taken + nj, epoch);
+          ns = __ldcg(P.chunk_first_range + nj);
+        } else {
+          ns = locate((uint32_t)nj * chunk_rows, s);
+        }
+        pf = 1;
+      } else if (pf == 1) {
+        pbase = ns & ~31;
+        if (ns >= 0 && ns < (int)n_ranges) {
+          pw = load_window(pbase, pt);
+          pw2 = load_window(pbase + 32, pt2);
+        }
+        ppkey = prune ? max(s_text, ld_volatile_u32(P.theta_key)) : 0u;
+        pf = 2;
+      }
     };
     if (dyn) {
-      if (lane == 0) next_claim = atomicAdd(P.chunk_counter, 1u);
-      if (!next_chunk(0)) vb = ve = 0;
+      claim();
+      if (blockIdx.x < n_chunks) {  // the first chunk needs no claim
+        nj = (int)blockIdx.x;
+        if (table) {
+          if (lane == 0) taken_old = atomicExch(P.chunk_taken + nj, epoch);
+          ns = first_range >= 0 ? first_range : __ldcg(P.chunk_first_range + nj);
+        } else {
+          ns = locate((uint32_t)nj * chunk_rows, 0);
+        }
+        pf = 1;
+      }
     } else if (vb < ve && n_ranges > 0) {
-      locate(vb, 0);
-      begin_piece();
+      s = locate(vb, 0);
+      base = s & ~31;
+      win = load_window(base, tag_cur);
+      win_next = load_window(base + 32, tag_next);
+      ubk = decode(tag_cur);
+      set_range();
+      if ((uint32_t)rg.x > vb) {
+        fail_range();
+        ve = vb;
+      }
     }
-    if (bad_range) ve = vb;
     uint32_t v = vb, streamed = 0;
     int it = 0;
     bool ok = true;
     for (;;) {
       if (v >= ve) {
-        if (!dyn || bad_range || !next_chunk(s)) break;
-        if (bad_range) break;
+        if (!dyn || bad_range) break;
+        for (;;) {
+          while (pf < 2) prefetch();  // what the stages of the last chunk did not prepare
+          if (pf == 3 || !table || __shfl_sync(FULL_MASK, taken_old, 0) != epoch) break;
+          pf = 0;  // another CTA streams it
+        }
+        if (pf == 3) break;
+        vb = (uint32_t)nj * chunk_rows;  // < n_rows
+        ve = min(n_rows, vb + chunk_rows);
         v = vb;
+        s = ns;
+        pf = 0;
+        if (s < 0 || s >= (int)n_ranges) {
+          fail_range();
+          break;
+        }
+        base = pbase;
+        win = pw;
+        win_next = pw2;
+        ubk = decode(pt);
+        tag_next = pt2;
+        pkey = ppkey;
+        set_range();
+        if ((uint32_t)rg.x > vb) {  // the range must start at or before the chunk
+          fail_range();
+          break;
+        }
       }
       const int stage = it % STAGES, f = it / STAGES;
       bool free_stage = true;
@@ -344,14 +451,10 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
           if (s - base == 32) {
             base += 32;
             win = win_next;
-            ubk = ubk_next;
-            win_next = load_window(base + 32, ubk_next);
+            ubk = decode(tag_next);
+            win_next = load_window(base + 32, tag_next);
           }
-          rg.x = __shfl_sync(FULL_MASK, win.x, s - base);
-          rg.y = __shfl_sync(FULL_MASK, win.y, s - base);
-          rg.z = __shfl_sync(FULL_MASK, win.z, s - base);
-          rg.w = __shfl_sync(FULL_MASK, win.w, s - base);
-          rkey = __shfl_sync(FULL_MASK, ubk, s - base);
+          set_range();
           continue;
         }
         if (rkey < pkey) {  // the rest of this child is below the threshold
@@ -393,13 +496,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
                            (uint32_t)(slot_end - my_slot) * (uint32_t)P.row_bytes, &full[stage], policy);
       }
       ++it;
-      // with the stage's copies out: the range of the chunk claimed at the start
-      // of this one (its claim is back by now), so the next chunk starts without
-      // that round trip
-      if (table && next_s < 0) {
-        const uint32_t c2 = __shfl_sync(FULL_MASK, next_claim, 0);
-        if (c2 < n_chunks) next_s = __ldcg(&P.chunk_first_range[c2]);
-      }
+      if (dyn && pf < 2) prefetch();  // with the stage's copies out
     }
     if (lane == 0) {
       if (P.rows_streamed && streamed) atomicAdd(P.rows_streamed, streamed);
@@ -714,7 +811,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
 // after it are its programmatic dependents.
 __global__ void __launch_bounds__(128) k_search_prologue(const float4* q_host, void* const* slots, float4* dq, int D4,
                                                          unsigned long long* ctrl_hdr, void** out_indirect,
-                                                         const uint32_t* seq_in, uint32_t* epoch_counter) {
+                                                         const uint32_t* seq_in, uint32_t* epoch_counter,
+                                                         unsigned long long* sync_words) {
   const int tid = threadIdx.x;
   const float4* src = q_host;
   if (slots) {
@@ -736,6 +834,7 @@ __global__ void __launch_bounds__(128) k_search_prologue(const float4* q_host, v
     }
     ctrl_hdr[tid] = w;
   }
+  if (sync_words && tid < (int)(sizeof(ScanSync) / 8)) sync_words[tid] = 0ull;
 }
 
 // ============================================================ root scan (K1)
@@ -1044,16 +1143,26 @@ __host__ __device__ inline BoundsLayout bounds_layout(int D, int rank, int chunk
 //     stale epoch (and then streams the child).
 //  2. after griddep_wait(): T = max(seed threshold, T_ext) is known; the roots,
 //     children and rows whose bound is not below T are counted for the trace
-//     (what a scan of the survivors alone would read).
+//     (what a scan of the survivors alone would read), and every main-scan
+//     chunk that holds such a child is marked with the epoch.  The last CTA
+//     lists the marked chunks that no scan CTA has taken yet, then adds 1 to
+//     the high half of the main scan's claim word: the scan's CTAs take the
+//     listed chunks from then on.
 // T_ext (optional): a threshold from outside this index (the max of all shards'
 // seed thresholds); the main scan prunes with it too.
 __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, const float* __restrict__ q,
                                                                SearchCtrl* ctrl, float* __restrict__ ub_root,
                                                                float* __restrict__ ub_child,
                                                                unsigned long long* __restrict__ ub_tagged,
-                                                               int chunk_rows, const float* __restrict__ T_ext) {
+                                                               int chunk_rows, const float* __restrict__ T_ext,
+                                                               uint32_t scan_chunk_rows, uint32_t n_scan_chunks,
+                                                               uint32_t* __restrict__ chunk_mark,
+                                                               const uint32_t* __restrict__ chunk_taken,
+                                                               int* __restrict__ live_list, uint32_t scan_ctas,
+                                                               ScanSync* __restrict__ sync) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_abort;
+  griddep_launch();  // the main scan may start as soon as every CTA of this kernel runs
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int D = ix.D, r = ix.rank;
   const BoundsLayout L = bounds_layout(D, r, chunk_rows);
@@ -1069,7 +1178,8 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
   // the query was complete before the kernel this one depends on was launched
   // (an earlier kernel of the search, or the caller's own work): read through L2
   for (int i = threadIdx.x; i < D; i += blockDim.x) sq[i] = __ldcg(q + i);
-  const unsigned long long tag = (unsigned long long)ld_volatile_u32(&ctrl->epoch) << 32;
+  const uint32_t epoch = ld_volatile_u32(&ctrl->epoch);
+  const unsigned long long tag = (unsigned long long)epoch << 32;
   if (threadIdx.x == 0) s_abort = 0;
   if (lane == 0) {
     mbar_init(&bars[0], 1);
@@ -1077,7 +1187,6 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
     fence_mbar_init();
   }
   __syncthreads();
-  griddep_launch();
 
   const double gD = gamma_n(D);
   // QN >= ||q||: fl(sum q_i^2) errs by at most gamma_D sum q_i^2 in any order
@@ -1123,6 +1232,8 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
       prefetch_l2(ix.child_l + (size_t)c * r);
       prefetch_l2(ix.child_u + (size_t)c * r);
       prefetch_l2(ix.child_radii + c);
+      prefetch_l2(ix.leaf_sizes + c);  // read by phase 2, while the main scan may be saturating HBM
+      prefetch_l2(ix.all_ranges + ci);
     }
 
     // ---- projection a = V^T q (and s = |V|^T |q|)
@@ -1277,6 +1388,12 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
         surv = keep_all || !(__ldcg(ub_child + c) < T);
         size = surv ? ix.leaf_sizes[c] : 0;
       }
+      if (size > 0 && chunk_mark) {
+        // mark the main-scan chunks holding this surviving child's virtual rows
+        const uint32_t x = (uint32_t)__ldg(&ix.all_ranges[ci].x);
+        const uint32_t j1 = min((x + (uint32_t)size - 1u) / scan_chunk_rows, n_scan_chunks - 1u);
+        for (uint32_t j = x / scan_chunk_rows; j <= j1; ++j) chunk_mark[j] = epoch;
+      }
       surv_children += (uint32_t)__popc(__ballot_sync(FULL_MASK, surv));
       surv_rows += (uint32_t)__shfl_sync(FULL_MASK, warp_incl_scan(size, lane), 31);
     }
@@ -1288,6 +1405,46 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
       atomicAdd(&ctrl->main_packed, ((unsigned long long)surv_children << 32) | (unsigned long long)surv_rows);
     }
   }
+  if (!chunk_mark) return;
+  __threadfence();  // each thread's marks reach the GPU before the CTA's ticket
+  __syncthreads();
+  if (threadIdx.x == 0) s_abort = (atomicAdd(&sync->bounds_done, 1u) == gridDim.x - 1);  // (flag reused)
+  __syncthreads();
+  if (!s_abort) return;
+  __threadfence();
+  // last CTA: the live chunks that no scan CTA has taken yet, then the signal.
+  // Chunks below the in-order claims handed out so far (each CTA's first chunk
+  // and the claimed ones) are streamed by the CTAs that hold them: not listed.
+  // (read once for the whole CTA: every thread's loop must cover the same chunks)
+  __shared__ uint32_t s_from;
+  if (threadIdx.x == 0) s_from = (uint32_t)ld_volatile_u64(&sync->chunk_claims) + scan_ctas;
+  __syncthreads();
+  for (uint32_t j0 = min(s_from, n_scan_chunks); j0 < n_scan_chunks; j0 += 16 * blockDim.x) {
+    bool live[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const uint32_t j = j0 + u * blockDim.x + threadIdx.x;
+      live[u] = j < n_scan_chunks && __ldcg(chunk_mark + j) == epoch && __ldcg(chunk_taken + j) != epoch;
+    }
+    // one append per warp and pass
+    uint32_t bal[16], total = 0u;
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      bal[u] = __ballot_sync(FULL_MASK, live[u]);
+      total += (uint32_t)__popc(bal[u]);
+    }
+    uint32_t at = 0u;
+    if (lane == 0 && total) at = atomicAdd(&sync->n_live, total);
+    at = __shfl_sync(FULL_MASK, at, 0);
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      if (live[u]) live_list[at + __popc(bal[u] & lanemask_lt())] = (int)(j0 + u * blockDim.x + threadIdx.x);
+      at += (uint32_t)__popc(bal[u]);
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) atomicAdd(&sync->chunk_claims, 1ull << 32);
 }
 
 // ============================================================ index preparation
@@ -1360,7 +1517,7 @@ int overlap_chunk_rows(int N, int D, int grid) {
   const long long parts = (long long)(grid > 0 ? grid : 1) * SCAN_DYN_CHUNKS;
   const long long per = ((long long)N + parts - 1) / parts;
   const long long c = (per + rows - 1) / rows * rows;
-  return (int)(c > 2 * rows ? c : 2 * rows);
+  return (int)(c > 4 * rows ? c : 4 * rows);
 }
 
 int scan_smem_bytes(int D) {
@@ -1437,6 +1594,12 @@ cudaError_t launch_prepare_roots(const IndexView& ix, double* root_cn, double* r
   return cudaGetLastError();
 }
 
+// CTAs that take part in a scan of n rows on `grid` CTAs (the kernel's G)
+static int scan_ctas(int n, int grid) {
+  const int g = (n + SCAN_MIN_ROWS - 1) / SCAN_MIN_ROWS;
+  return g < 1 ? 1 : (g < grid ? g : grid);
+}
+
 static ScanParams scan_params(const IndexView& ix, const Workspace& ws, const float* q, int k, float* out_scores,
                               int* out_ids, long long* out_rows) {
   ScanParams P{};
@@ -1468,7 +1631,7 @@ static cudaError_t search_reset(const IndexView& ix, const Workspace& ws, const 
                                            reinterpret_cast<float4*>(const_cast<float*>(q)), ix.D4,
                                            reinterpret_cast<unsigned long long*>(ws.ctrl),
                                            io ? io->out_indirect : nullptr, io ? io->seq_in : nullptr,
-                                           ws.epoch_counter);
+                                           ws.epoch_counter, reinterpret_cast<unsigned long long*>(ws.sync));
   return cudaGetLastError();
 }
 
@@ -1504,16 +1667,24 @@ cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const
   int grid_b = (ix.R + BOUNDS_WARPS - 1) / BOUNDS_WARPS;
   if (grid_b > 2 * ws.scan_grid) grid_b = 2 * ws.scan_grid;
   if ((e = launch_dependent(k_bounds, grid_b, BOUNDS_WARPS * 32, BL.total, stream, ix, q, ws.ctrl, ws.ub_root,
-                            ws.ub_child, ws.ub_tagged, chunk_rows, T_ext)) != cudaSuccess)
+                            ws.ub_child, ws.ub_tagged, chunk_rows, T_ext, (uint32_t)ws.chunk_rows,
+                            (uint32_t)ws.n_chunks, ws.chunk_mark, ws.chunk_taken, ws.live_list,
+                            (uint32_t)scan_ctas(ix.N, ws.scan_grid), ws.sync)) != cudaSuccess)
     return e;
   ScanParams M = scan_params(ix, ws, q, k, out_scores, out_ids, out_rows);
   M.ranges = ix.all_ranges;
   M.packed_counts = ix.all_packed;
+  M.packed_value = ((unsigned long long)ix.all_nnz << 32) | (unsigned long long)(uint32_t)ix.N;
   M.done = &ws.ctrl->main_done;
   M.ub_tagged = ws.ub_tagged;
   M.epoch = &ws.ctrl->epoch;
   M.chunk_first_range = ws.chunk_first_range;
   M.chunk_rows = (uint32_t)ws.chunk_rows;
+  M.chunk_claims = &ws.sync->chunk_claims;
+  M.live_list = ws.live_list;
+  M.n_live = &ws.sync->n_live;
+  M.list_next = &ws.sync->list_next;
+  M.chunk_taken = ws.chunk_taken;
   M.T_ext = T_ext;
   M.rows_streamed = &ws.ctrl->rows_streamed;
   M.overlapped = 1;
@@ -1538,6 +1709,7 @@ cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float*
   ScanParams F = scan_params(ix, ws, q, k, out_scores, out_ids, out_rows);
   F.ranges = ws.flat_range;
   F.packed_counts = ws.flat_packed;
+  F.packed_value = (1ull << 32) | (unsigned long long)(uint32_t)ix.N;
   F.done = &ws.ctrl->main_done;
   final_io(F, ws, io);
   if (ev_scan0) cudaEventRecord(ev_scan0, stream);
