@@ -29,6 +29,10 @@ class SmemOptIn {
     std::lock_guard<std::mutex> lock(mu_);
     if (set_[dev].load(std::memory_order_relaxed) >= bytes) return cudaSuccess;
     e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    // all of the unified L1 as shared memory: kernels of one search alternate on
+    // the SMs, and a different split would have to be set up between them
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (e == cudaSuccess) set_[dev].store(bytes, std::memory_order_release);
     return e;
   }

@@ -122,6 +122,8 @@ __host__ __device__ inline ScanLayout scan_layout(int rows_per_stage, int row_by
 
 // Merges whose survivors number at most this many rank them directly.
 constexpr int RANK_CAP = 256;
+// The final merge ranks up to this many candidates directly.
+constexpr int FINAL_RANK_CAP = 512;
 // Streams of at least SCAN_DYN_CHUNKS chunks of SCAN_DYN_MIN_STAGES stages per
 // CTA are taken in claimed chunks (about SCAN_DYN_CHUNKS per CTA) instead of
 // equal slices.
@@ -753,7 +755,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
   uint32_t th = 0u;
   if (lane == 0) th = ld_volatile_u32(P.theta_key);
   th = max(__shfl_sync(FULL_MASK, th, 0), s_theta);  // per warp; any of these bounds is valid
-  unsigned long long* tmp = ring;                       // idle now; holds RANK_CAP entries
+  unsigned long long* tmp = ring;                       // idle now; holds FINAL_RANK_CAP entries
   for (int b0 = 0; b0 < M; b0 += 8 * SCAN_THREADS) {
     unsigned long long v[8];
 #pragma unroll
@@ -768,12 +770,12 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       uint32_t pos = 0;
       if (lane == 0 && bal) pos = atomicAdd(&s_fin_count, (uint32_t)__popc(bal));
       pos = __shfl_sync(FULL_MASK, pos, 0) + __popc(bal & lanemask_lt());
-      if (pass && pos < (uint32_t)RANK_CAP) tmp[pos] = v[u];
+      if (pass && pos < (uint32_t)FINAL_RANK_CAP) tmp[pos] = v[u];
     }
   }
   __syncthreads();
   const int n = (int)s_fin_count;
-  if (n <= RANK_CAP) {
+  if (n <= FINAL_RANK_CAP) {
     // rank = number of larger kept entries (entries are unique); for every
     // entry of the true top-k all larger entries were kept, whatever bound
     // each warp used, so these ranks are the global ranks
@@ -1144,10 +1146,10 @@ __host__ __device__ inline BoundsLayout bounds_layout(int D, int rank, int chunk
 //  2. after griddep_wait(): T = max(seed threshold, T_ext) is known; the roots,
 //     children and rows whose bound is not below T are counted for the trace
 //     (what a scan of the survivors alone would read), and every main-scan
-//     chunk that holds such a child is marked with the epoch.  The last CTA
-//     lists the marked chunks that no scan CTA has taken yet, then adds 1 to
-//     the high half of the main scan's claim word: the scan's CTAs take the
-//     listed chunks from then on.
+//     chunk that holds such a child and that no scan CTA holds yet is listed
+//     once (an epoch swap per chunk).  The last CTA then adds 1 to the high half
+//     of the main scan's claim word: the scan's CTAs take the listed chunks from
+//     then on.
 // T_ext (optional): a threshold from outside this index (the max of all shards'
 // seed thresholds); the main scan prunes with it too.
 __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, const float* __restrict__ q,
@@ -1157,7 +1159,6 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
                                                                int chunk_rows, const float* __restrict__ T_ext,
                                                                uint32_t scan_chunk_rows, uint32_t n_scan_chunks,
                                                                uint32_t* __restrict__ chunk_mark,
-                                                               const uint32_t* __restrict__ chunk_taken,
                                                                int* __restrict__ live_list, uint32_t scan_ctas,
                                                                ScanSync* __restrict__ sync) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -1373,6 +1374,9 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
   }
   const float T = Tkey ? key2f(Tkey) : -INFINITY;
   const bool keep_all = s_abort != 0;
+  // chunks [0, frontier) are held by scan CTAs already (each CTA's first chunk
+  // and every in-order claim so far)
+  const uint32_t frontier = chunk_mark ? (uint32_t)ld_volatile_u64(&sync->chunk_claims) + scan_ctas : 0u;
   uint32_t surv_roots = 0, surv_children = 0, surv_rows = 0;
   for (int p = blockIdx.x * BOUNDS_WARPS + warp; p < ix.R; p += gridDim.x * BOUNDS_WARPS) {
     if (ix.root_rows[p] == 0) continue;
@@ -1388,11 +1392,39 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
         surv = keep_all || !(__ldcg(ub_child + c) < T);
         size = surv ? ix.leaf_sizes[c] : 0;
       }
-      if (size > 0 && chunk_mark) {
-        // mark the main-scan chunks holding this surviving child's virtual rows
-        const uint32_t x = (uint32_t)__ldg(&ix.all_ranges[ci].x);
-        const uint32_t j1 = min((x + (uint32_t)size - 1u) / scan_chunk_rows, n_scan_chunks - 1u);
-        for (uint32_t j = x / scan_chunk_rows; j <= j1; ++j) chunk_mark[j] = epoch;
+      if (chunk_mark) {
+        // list the main-scan chunks of this surviving child that no scan CTA
+        // holds yet (every chunk below the in-order frontier is held): an epoch
+        // swap per chunk keeps each listed once, up to 8 per lane in flight,
+        // one list append per warp and batch
+        uint32_t j0 = 1u, j1 = 0u;
+        if (size > 0) {
+          const uint32_t x = (uint32_t)__ldg(&ix.all_ranges[ci].x);
+          j0 = max(x / scan_chunk_rows, frontier);
+          j1 = min((x + (uint32_t)size - 1u) / scan_chunk_rows, n_scan_chunks - 1u);
+        }
+        const uint32_t cnt = j1 >= j0 ? j1 - j0 + 1u : 0u;
+        const uint32_t steps = __reduce_max_sync(FULL_MASK, cnt);
+        for (uint32_t t0 = 0; t0 < steps; t0 += 8) {
+          bool fresh[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            fresh[u] = t0 + u < cnt && atomicExch(chunk_mark + j0 + t0 + u, epoch) != epoch;
+          uint32_t bal[8], total = 0u;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            bal[u] = __ballot_sync(FULL_MASK, fresh[u]);
+            total += (uint32_t)__popc(bal[u]);
+          }
+          uint32_t at = 0u;
+          if (lane == 0 && total) at = atomicAdd(&sync->n_live, total);
+          at = __shfl_sync(FULL_MASK, at, 0);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            if (fresh[u]) live_list[at + __popc(bal[u] & lanemask_lt())] = (int)(j0 + t0 + u);
+            at += (uint32_t)__popc(bal[u]);
+          }
+        }
       }
       surv_children += (uint32_t)__popc(__ballot_sync(FULL_MASK, surv));
       surv_rows += (uint32_t)__shfl_sync(FULL_MASK, warp_incl_scan(size, lane), 31);
@@ -1406,46 +1438,14 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
     }
   }
   if (!chunk_mark) return;
-  __threadfence();  // each thread's marks reach the GPU before the CTA's ticket
+  __threadfence();  // each thread's list entries reach the GPU before the CTA's ticket
   __syncthreads();
-  if (threadIdx.x == 0) s_abort = (atomicAdd(&sync->bounds_done, 1u) == gridDim.x - 1);  // (flag reused)
-  __syncthreads();
-  if (!s_abort) return;
-  __threadfence();
-  // last CTA: the live chunks that no scan CTA has taken yet, then the signal.
-  // Chunks below the in-order claims handed out so far (each CTA's first chunk
-  // and the claimed ones) are streamed by the CTAs that hold them: not listed.
-  // (read once for the whole CTA: every thread's loop must cover the same chunks)
-  __shared__ uint32_t s_from;
-  if (threadIdx.x == 0) s_from = (uint32_t)ld_volatile_u64(&sync->chunk_claims) + scan_ctas;
-  __syncthreads();
-  for (uint32_t j0 = min(s_from, n_scan_chunks); j0 < n_scan_chunks; j0 += 16 * blockDim.x) {
-    bool live[16];
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const uint32_t j = j0 + u * blockDim.x + threadIdx.x;
-      live[u] = j < n_scan_chunks && __ldcg(chunk_mark + j) == epoch && __ldcg(chunk_taken + j) != epoch;
-    }
-    // one append per warp and pass
-    uint32_t bal[16], total = 0u;
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      bal[u] = __ballot_sync(FULL_MASK, live[u]);
-      total += (uint32_t)__popc(bal[u]);
-    }
-    uint32_t at = 0u;
-    if (lane == 0 && total) at = atomicAdd(&sync->n_live, total);
-    at = __shfl_sync(FULL_MASK, at, 0);
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      if (live[u]) live_list[at + __popc(bal[u] & lanemask_lt())] = (int)(j0 + u * blockDim.x + threadIdx.x);
-      at += (uint32_t)__popc(bal[u]);
-    }
+  if (threadIdx.x == 0 && atomicAdd(&sync->bounds_done, 1u) == gridDim.x - 1) {
+    __threadfence();  // every CTA's entries (fenced before its ticket) before the signal
+    atomicAdd(&sync->chunk_claims, 1ull << 32);
   }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) atomicAdd(&sync->chunk_claims, 1ull << 32);
 }
+
 
 // ============================================================ index preparation
 // Per root: an upper bound of ||c_r|| and of ||V_r^T V_r - I||_2 (Frobenius norm
@@ -1668,7 +1668,7 @@ cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const
   if (grid_b > 2 * ws.scan_grid) grid_b = 2 * ws.scan_grid;
   if ((e = launch_dependent(k_bounds, grid_b, BOUNDS_WARPS * 32, BL.total, stream, ix, q, ws.ctrl, ws.ub_root,
                             ws.ub_child, ws.ub_tagged, chunk_rows, T_ext, (uint32_t)ws.chunk_rows,
-                            (uint32_t)ws.n_chunks, ws.chunk_mark, ws.chunk_taken, ws.live_list,
+                            (uint32_t)ws.n_chunks, ws.chunk_mark, ws.live_list,
                             (uint32_t)scan_ctas(ix.N, ws.scan_grid), ws.sync)) != cudaSuccess)
     return e;
   ScanParams M = scan_params(ix, ws, q, k, out_scores, out_ids, out_rows);
