@@ -1377,12 +1377,33 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
   // chunks [0, frontier) are held by scan CTAs already (each CTA's first chunk
   // and every in-order claim so far)
   const uint32_t frontier = chunk_mark ? (uint32_t)ld_volatile_u64(&sync->chunk_claims) + scan_ctas : 0u;
+  // Live-chunk list.  Inside a root, a chunk is listed by the first surviving
+  // child that covers it (a max-scan over the warp's lanes, carried across the
+  // root's 32-child groups); only a chunk that reaches past the root's rows can
+  // also be listed by a neighbouring root, and only for those an epoch swap on
+  // its mark keeps it listed once.  Entries gather in shared memory (one list
+  // append per CTA); a CTA that lists more than LIST_SMEM appends the rest per
+  // warp.
+  constexpr uint32_t LIST_SMEM = 1024;
+  __shared__ int s_list[LIST_SMEM];
+  __shared__ uint32_t s_nlist, s_roots, s_children, s_rows, s_base;
+  if (threadIdx.x == 0) s_nlist = s_roots = s_children = s_rows = 0u;
+  __syncthreads();
+  const uint32_t cr = scan_chunk_rows;
   uint32_t surv_roots = 0, surv_children = 0, surv_rows = 0;
   for (int p = blockIdx.x * BOUNDS_WARPS + warp; p < ix.R; p += gridDim.x * BOUNDS_WARPS) {
     if (ix.root_rows[p] == 0) continue;
     if (!keep_all && __ldcg(ub_root + p) < T) continue;
     ++surv_roots;
     const int cb = ix.root_child_ptr[p], ce = ix.root_child_ptr[p + 1];
+    // the root's virtual rows [r_lo, r_hi)
+    uint32_t r_lo = 0u, r_hi = 0u;
+    if (chunk_mark && ce > cb) {
+      const int4 e0 = __ldg(&ix.all_ranges[cb]), e1 = __ldg(&ix.all_ranges[ce - 1]);
+      r_lo = (uint32_t)e0.x;
+      r_hi = (uint32_t)e1.x + (uint32_t)(e1.z - e1.y);
+    }
+    int carry = -1;  // the last chunk listed by this root's children so far
     for (int c0 = cb; c0 < ce; c0 += 32) {
       const int ci = c0 + lane;
       bool surv = false;
@@ -1393,35 +1414,54 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
         size = surv ? ix.leaf_sizes[c] : 0;
       }
       if (chunk_mark) {
-        // list the main-scan chunks of this surviving child that no scan CTA
-        // holds yet (every chunk below the in-order frontier is held): an epoch
-        // swap per chunk keeps each listed once, up to 8 per lane in flight,
-        // one list append per warp and batch
-        uint32_t j0 = 1u, j1 = 0u;
+        int jlo = 0, jhi = -1;
         if (size > 0) {
           const uint32_t x = (uint32_t)__ldg(&ix.all_ranges[ci].x);
-          j0 = max(x / scan_chunk_rows, frontier);
-          j1 = min((x + (uint32_t)size - 1u) / scan_chunk_rows, n_scan_chunks - 1u);
+          jlo = (int)(x / cr);
+          jhi = (int)min((x + (uint32_t)size - 1u) / cr, n_scan_chunks - 1u);
         }
-        const uint32_t cnt = j1 >= j0 ? j1 - j0 + 1u : 0u;
-        const uint32_t steps = __reduce_max_sync(FULL_MASK, cnt);
-        for (uint32_t t0 = 0; t0 < steps; t0 += 8) {
+        // the last chunk covered by this root's surviving children before this lane
+        int m = jhi;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int t = __shfl_up_sync(FULL_MASK, m, o);
+          if (lane >= o) m = max(m, t);
+        }
+        int before = __shfl_up_sync(FULL_MASK, m, 1);
+        before = max(lane == 0 ? -1 : before, carry);
+        carry = max(carry, __shfl_sync(FULL_MASK, m, 31));
+        if (size > 0) jlo = max(max(jlo, before + 1), (int)frontier);  // chunks below the frontier are held
+        const int cnt = jhi >= jlo ? jhi - jlo + 1 : 0;
+        const int steps = __reduce_max_sync(FULL_MASK, cnt);
+        for (int t0 = 0; t0 < steps; t0 += 8) {
           bool fresh[8];
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            fresh[u] = t0 + u < cnt && atomicExch(chunk_mark + j0 + t0 + u, epoch) != epoch;
+          for (int u = 0; u < 8; ++u) {
+            const uint32_t j = (uint32_t)(jlo + t0 + u);
+            bool ok = t0 + u < cnt;
+            if (ok && (j * cr < r_lo || (j + 1u) * cr > r_hi)) ok = atomicExch(chunk_mark + j, epoch) != epoch;
+            fresh[u] = ok;
+          }
           uint32_t bal[8], total = 0u;
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             bal[u] = __ballot_sync(FULL_MASK, fresh[u]);
             total += (uint32_t)__popc(bal[u]);
           }
+          if (total == 0u) continue;
           uint32_t at = 0u;
-          if (lane == 0 && total) at = atomicAdd(&sync->n_live, total);
+          if (lane == 0) at = atomicAdd(&s_nlist, total);
           at = __shfl_sync(FULL_MASK, at, 0);
+          int* dst = s_list;
+          if (at + total > LIST_SMEM) {  // shared staging full: straight to the list
+            for (uint32_t i = at + lane; i < LIST_SMEM; i += 32) s_list[i] = -1;  // (reserved, unused)
+            if (lane == 0) at = atomicAdd(&sync->n_live, total);
+            at = __shfl_sync(FULL_MASK, at, 0);
+            dst = live_list;
+          }
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            if (fresh[u]) live_list[at + __popc(bal[u] & lanemask_lt())] = (int)(j0 + t0 + u);
+            if (fresh[u]) dst[at + __popc(bal[u] & lanemask_lt())] = jlo + t0 + u;
             at += (uint32_t)__popc(bal[u]);
           }
         }
@@ -1431,13 +1471,23 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
     }
   }
   if (lane == 0) {
-    if (surv_roots) atomicAdd(&ctrl->n_surv_roots, surv_roots);
-    if (surv_children) {
-      atomicAdd(&ctrl->n_surv_children, surv_children);
-      atomicAdd(&ctrl->main_packed, ((unsigned long long)surv_children << 32) | (unsigned long long)surv_rows);
+    if (surv_roots) atomicAdd(&s_roots, surv_roots);
+    if (surv_children) atomicAdd(&s_children, surv_children);
+    if (surv_rows) atomicAdd(&s_rows, surv_rows);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {  // one update of each trace counter and one list append per CTA
+    if (s_roots) atomicAdd(&ctrl->n_surv_roots, s_roots);
+    if (s_children) {
+      atomicAdd(&ctrl->n_surv_children, s_children);
+      atomicAdd(&ctrl->main_packed, ((unsigned long long)s_children << 32) | (unsigned long long)s_rows);
     }
+    const uint32_t n = min(s_nlist, LIST_SMEM);
+    s_base = (chunk_mark && n) ? atomicAdd(&sync->n_live, n) : 0u;
   }
   if (!chunk_mark) return;
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < min(s_nlist, LIST_SMEM); i += blockDim.x) live_list[s_base + i] = s_list[i];
   __threadfence();  // each thread's list entries reach the GPU before the CTA's ticket
   __syncthreads();
   if (threadIdx.x == 0 && atomicAdd(&sync->bounds_done, 1u) == gridDim.x - 1) {
