@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
   const int theta_word = (int)(((uintptr_t)P.theta_key & 15u) >> 2);
   __shared__ int s_is_last, s_err;
   __shared__ unsigned long long s_pc;
-  __shared__ uint32_t s_theta, s_rank_count, s_fin_count, s_text, s_epoch;
+  __shared__ uint32_t s_theta, s_rank_count, s_fin_count, s_text, s_epoch, s_theta0;
   __shared__ uint32_t s_warp_theta[SCAN_CONSUMER_WARPS];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -172,15 +172,31 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
   // while they are being written carry the epoch, so it does not wait.
   if (!P.overlapped) griddep_wait();
   // the producer's first chunk is chunk blockIdx.x (see below): its table entry
-  // is requested before the shared-memory set-up
+  // and its range windows are requested before the shared-memory set-up (the
+  // windows' bounds are decoded once the epoch is known)
   int first_range = -1;
+  int4 fw0 = make_int4(0, 0, 0, 0), fw1 = fw0;
+  unsigned long long ft0 = 0ull, ft1 = 0ull;
   if (warp == SCAN_CONSUMER_WARPS && P.chunk_first_range && P.packed_value &&
-      blockIdx.x < ((uint32_t)P.packed_value + P.chunk_rows - 1) / P.chunk_rows)
+      blockIdx.x < ((uint32_t)P.packed_value + P.chunk_rows - 1) / P.chunk_rows) {
     first_range = __ldcg(P.chunk_first_range + blockIdx.x);
+    const int nr = (int)(P.packed_value >> 32), b0 = (first_range & ~31) + lane, b1 = b0 + 32;
+    if (first_range >= 0 && first_range < nr) {
+      if (b0 < nr) {
+        fw0 = __ldcg(&P.ranges[b0]);
+        if (P.ub_tagged) ft0 = __ldcg(&P.ub_tagged[b0]);
+      }
+      if (b1 < nr) {
+        fw1 = __ldcg(&P.ranges[b1]);
+        if (P.ub_tagged) ft1 = __ldcg(&P.ub_tagged[b1]);
+      }
+    }
+  }
   if (tid == 0) {
     // (independent loads, in flight together)
     const float te = P.T_ext ? __ldcg(P.T_ext) : -INFINITY;
     const uint32_t ep = P.epoch ? __ldcg(P.epoch) : 0u;
+    const uint32_t th0 = P.ub_tagged ? __ldcg(P.theta_key) : 0u;  // the running threshold so far
     const unsigned long long pc = P.packed_value ? P.packed_value : __ldcg(P.packed_counts);
     s_err = 0;
     s_fin_count = 0;
@@ -188,6 +204,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     s_text = tx;
     if (tx && blockIdx.x == 0) atomicMax(P.theta_key, tx);
     s_epoch = ep;
+    s_theta0 = max(th0, tx);
     s_pc = pc;
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -313,8 +330,10 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       }
     };
     // the chunk that the claim in flight gives (claiming again where it gives
-    // none), with the following claim issued; -1 = none left.  The chunk still
-    // has to be won through its taken word (hierarchical scans).
+    // none), with the following claim issued: >= 0 = that chunk (it still has to
+    // be won through its taken word), -1 = none left, -2 = a live-list entry
+    // requested (list_entry, read a step later)
+    uint32_t list_entry = 0u;
     const auto resolve = [&]() -> int {
       for (uint32_t guard = 0; guard <= 2 * n_chunks + 2; ++guard) {
         const unsigned long long r = __shfl_sync(FULL_MASK, pend, 0);
@@ -334,43 +353,52 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
         }
         const uint32_t i = (uint32_t)r;
         if (i >= n_live) return -1;
-        const uint32_t j = (uint32_t)__ldcg(P.live_list + i);
+        list_entry = (uint32_t)__ldcg(P.live_list + i);
         claim();
-        if (j < n_chunks) return (int)j;
+        return -2;
       }
       return -1;
     };
     // the next chunk, prepared one step per issued stage: 0 = nothing yet,
-    // 1 = chunk known, its taken word swapped and its first range requested,
-    // 2 = its windows and the threshold requested, 3 = no chunk left; the swap
-    // is checked when the chunk is taken (a lost chunk is dropped then)
+    // 1 = a live-list entry requested, 2 = chunk known, its taken word swapped
+    // and its first range requested, 3 = its windows and the threshold
+    // requested, 4 = no chunk left; the swap is checked when the chunk is taken
+    // (a lost chunk is dropped then)
     int pf = 0, nj = -1, ns = -1, pbase = 0;
     uint32_t taken_old = 0u;
     int4 pw = make_int4(0, 0, 0, 0), pw2 = pw;
     unsigned long long pt = 0ull, pt2 = 0ull;
     uint32_t ppkey = 0u;
+    const auto start_chunk = [&]() {
+      if (table) {
+        if (lane == 0) taken_old = atomicExch(P.chunk_taken + nj, epoch);
+        ns = __ldcg(P.chunk_first_range + nj);
+      } else {
+        ns = locate((uint32_t)nj * chunk_rows, s);
+      }
+      pf = 2;
+    };
     const auto prefetch = [&]() {
       if (pf == 0) {
         nj = resolve();
-        if (nj < 0) {
-          pf = 3;
-          return;
-        }
-        if (table) {
-          if (lane == 0) taken_old = atomicExch(P.chunk_taken + nj, epoch);
-          ns = __ldcg(P.chunk_first_range + nj);
-        } else {
-          ns = locate((uint32_t)nj * chunk_rows, s);
-        }
-        pf = 1;
+        if (nj == -1) pf = 4;
+        else if (nj == -2) pf = 1;
+        else start_chunk();
       } else if (pf == 1) {
+        if (list_entry < n_chunks) {
+          nj = (int)list_entry;
+          start_chunk();
+        } else {
+          pf = 0;
+        }
+      } else if (pf == 2) {
         pbase = ns & ~31;
         if (ns >= 0 && ns < (int)n_ranges) {
           pw = load_window(pbase, pt);
           pw2 = load_window(pbase + 32, pt2);
         }
         ppkey = prune ? max(s_text, ld_volatile_u32(P.theta_key)) : 0u;
-        pf = 2;
+        pf = 3;
       }
     };
     if (dyn) {
@@ -383,7 +411,16 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
         } else {
           ns = locate((uint32_t)nj * chunk_rows, 0);
         }
-        pf = 1;
+        pf = 2;
+        if (first_range >= 0) {  // its windows are in flight already
+          pbase = first_range & ~31;
+          pw = fw0;
+          pw2 = fw1;
+          pt = ft0;
+          pt2 = ft1;
+          ppkey = s_theta0;
+          pf = 3;
+        }
       }
     } else if (vb < ve && n_ranges > 0) {
       s = locate(vb, 0);
@@ -404,11 +441,11 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       if (v >= ve) {
         if (!dyn || bad_range) break;
         for (;;) {
-          while (pf < 2) prefetch();  // what the stages of the last chunk did not prepare
-          if (pf == 3 || !table || __shfl_sync(FULL_MASK, taken_old, 0) != epoch) break;
+          while (pf < 3) prefetch();  // what the stages of the last chunk did not prepare
+          if (pf == 4 || !table || __shfl_sync(FULL_MASK, taken_old, 0) != epoch) break;
           pf = 0;  // another CTA streams it
         }
-        if (pf == 3) break;
+        if (pf == 4) break;
         vb = (uint32_t)nj * chunk_rows;  // < n_rows
         ve = min(n_rows, vb + chunk_rows);
         v = vb;
@@ -498,7 +535,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
                            (uint32_t)(slot_end - my_slot) * (uint32_t)P.row_bytes, &full[stage], policy);
       }
       ++it;
-      if (dyn && pf < 2) prefetch();  // with the stage's copies out
+      if (dyn && pf < 3) prefetch();  // with the stage's copies out
     }
     if (lane == 0) {
       if (P.rows_streamed && streamed) atomicAdd(P.rows_streamed, streamed);
