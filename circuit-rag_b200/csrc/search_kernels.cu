@@ -1590,9 +1590,9 @@ static int vpl_bucket(int D4) {
 static int kcap_bucket(int k) { return k <= 32 ? 32 : (k <= 128 ? 128 : 256); }
 static int rows_per_stage(int vpl) { return vpl <= 4 ? 32 : (vpl <= 8 ? 16 : 8); }
 static int sortn_for(int kcap) { return kcap + 64 <= 128 ? 128 : (kcap + 64 <= 256 ? 256 : 512); }
-// Rows per CTA below which a scan uses fewer CTAs: 32 (one to four stages),
+// Rows per CTA below which a scan uses fewer CTAs: 64 (one to eight stages),
 // so that every CTA's k-th best (k <= 32) is a useful threshold.
-constexpr int SCAN_MIN_ROWS = 32;
+constexpr int SCAN_MIN_ROWS = 64;
 static int stages_for(int vpl, int row_bytes) {
   const size_t sb = align_up((size_t)rows_per_stage(vpl) * row_bytes, 128);
   int s = (int)(147456 / sb);

@@ -127,3 +127,38 @@ def test_trace_counts_small_corpus():
         assert tr2.path == "flat" and tr2.rows_streamed == w.n
         assert torch.equal(i, i2)
     idx.close()
+
+
+@pytest.mark.parametrize("law,n,roots,cpr", [
+    ("clustered-50k", 200, 1, 4),       # fewer rows than one chunk, one root
+    ("clustered-50k", 20_000, 400, 2),  # many roots of ~50 rows: most chunks span several roots
+    ("clustered-50k", 60_000, 16, 64),  # small children, chunks inside roots
+    ("spread-200k", 200_000, 1, 64),    # one root holding ~1,500 live chunks (more than one CTA stages)
+])
+def test_chunk_and_list_shapes(law, n, roots, cpr):
+    """Index shapes that exercise the claim/list edge cases: a single chunk, a single
+    root, chunks shared by several roots, a CTA listing more chunks than it stages in
+    shared memory; k = 1, 10, 256; the pipelined search and the one that starts the
+    scan after the bounds (scan events) must both be exact and agree."""
+    w = dataclasses.replace(WORKLOADS[law], name="shape", n=n)
+    X = w.corpus(device=DEV)
+    idx = build_circuit_index(X, num_roots=roots, children_per_root=cpr, rank=8, device=DEV)
+    L = _native.lib()
+    h = idx.native_handle()
+    st = torch.cuda.current_stream().cuda_stream
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for e in (ev0, ev1):
+        e.record()
+    for q in w.query_batch(4, device=DEV):
+        for k in (1, 10, 256):
+            kk = min(k, n)
+            s, i, tr = circuit_search(q, idx, k=kk, min_hierarchy_n=0)
+            assert tr.path == "hierarchical"
+            _check(X, q, kk, s, i)
+            s2 = torch.empty(kk, device=DEV)
+            i2 = torch.empty(kk, dtype=torch.int32, device=DEV)
+            assert L.circuit_search_async(h, q.data_ptr(), kk, 0, s2.data_ptr(), i2.data_ptr(), None, st,
+                                          ev0.cuda_event, ev1.cuda_event) == 0
+            _check(X, q, kk, s2, i2)
+            assert torch.equal(i, i2) and torch.equal(s, s2)
+    idx.close()
