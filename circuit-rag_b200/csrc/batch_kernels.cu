@@ -136,15 +136,20 @@ __device__ __forceinline__ void epi_pass_topk(const uint32_t (&sc0)[32], const u
   }
   theta = fmaxf(theta, theta_local);
   if (P.seed_only) return;
+  // the candidates: one reservation in the query's list for all of them
   const float lim2 = theta - band;
+  uint64_t keep = 0ull;
   for (uint64_t m = mask; m; m &= m - 1ull) {
     const int i = __ffsll((long long)m) - 1;
-    const float sv = stash[i * BQ + threadIdx.x];
-    if (sv >= lim2) {
-      const int slot = atomicAdd(P.cand_count + q, 1);
-      if (slot < P.cap)
-        P.cand[(size_t)q * P.cap + slot] = ((unsigned long long)f2key(sv) << 32) | (uint32_t)(row_base + i);
-    }
+    if (stash[i * BQ + threadIdx.x] >= lim2) keep |= 1ull << i;
+  }
+  if (!keep) return;
+  int slot = atomicAdd(P.cand_count + q, __popcll(keep));
+  for (uint64_t m = keep; m; m &= m - 1ull, ++slot) {
+    const int i = __ffsll((long long)m) - 1;
+    if (slot < P.cap)
+      P.cand[(size_t)q * P.cap + slot] =
+          ((unsigned long long)f2key(stash[i * BQ + threadIdx.x]) << 32) | (uint32_t)(row_base + i);
   }
 }
 
@@ -155,10 +160,26 @@ __device__ __forceinline__ void epi_pass_topk(const uint32_t (&sc0)[32], const u
 // yet filled).  A row always maps to the same slot, so rows seen twice (the
 // threshold pass samples rows that the main pass scans again) cannot count
 // twice.  No per-thread top-k list is needed, for any k.
+// The slots are read through L2 (other threads raise them with atomicMax; a
+// stale value is still one real row's score, so the minimum stays valid), 16
+// bytes at a time with the loads issued together: k = 100 slots take a few L2
+// round trips, not one per slot.
 __device__ __forceinline__ uint32_t slot_min(const uint32_t* sl, int k) {
-  uint32_t mn = 0xffffffffu;
-  for (int i = 0; i < k; ++i) mn = min(mn, ld_volatile_u32(sl + i));
-  return mn;
+  uint32_t m0 = 0xffffffffu, m1 = m0, m2 = m0, m3 = m0;
+  int i = 0;
+  for (; i < k && (reinterpret_cast<uintptr_t>(sl + i) & 15u); ++i) m0 = min(m0, __ldcg(sl + i));
+  const uint4* v4 = reinterpret_cast<const uint4*>(sl + i);
+  const int n4 = (k - i) >> 2;
+#pragma unroll 8
+  for (int j = 0; j < n4; ++j) {
+    const uint4 v = __ldcg(v4 + j);
+    m0 = min(m0, v.x);
+    m1 = min(m1, v.y);
+    m2 = min(m2, v.z);
+    m3 = min(m3, v.w);
+  }
+  for (i += 4 * n4; i < k; ++i) m1 = min(m1, __ldcg(sl + i));
+  return min(min(m0, m1), min(m2, m3));
 }
 
 // One epilogue pass over 64 accumulator columns (rows row_base + i of the scan's
@@ -184,6 +205,8 @@ __device__ __forceinline__ bool epi_pass(const uint32_t (&sc0)[32], const uint32
   }
   uint32_t* sl = P.slots + (size_t)q * P.k;
   bool raised = false;
+  // every row of the mask is a candidate: one reservation in the query's list
+  int slot = P.seed_only ? 0 : atomicAdd(P.cand_count + q, __popcll(mask));
   for (uint64_t m = mask; m; m &= m - 1ull) {
     const int i = __ffsll((long long)m) - 1;
     const float sv = stash[i * BQ + threadIdx.x];
@@ -194,8 +217,8 @@ __device__ __forceinline__ bool epi_pass(const uint32_t (&sc0)[32], const uint32
       raised = true;
     }
     if (!P.seed_only) {
-      const int slot = atomicAdd(P.cand_count + q, 1);
       if (slot < P.cap) P.cand[(size_t)q * P.cap + slot] = ((unsigned long long)key << 32) | (uint32_t)(row_base + i);
+      ++slot;
     }
   }
   return raised;
