@@ -88,6 +88,9 @@ def parse():
     ap.add_argument("--no-extra", action="store_true", help="skip the other workloads")
     ap.add_argument("--no-threshold-exchange", action="store_true",
                     help="N > 1: prune each shard with its own seed threshold only")
+    ap.add_argument("--shared-threshold", action="store_true",
+                    help="N > 1: also share the running threshold between the shards while their scans run "
+                         "(circuit_search_finish_shared_async over CUDA IPC)")
     return ap.parse_args()
 
 
@@ -355,9 +358,16 @@ class Searcher:
     """One rank's single-query search (+ threshold exchange and all-gather
     merge at N > 1) on preallocated buffers."""
 
+    _shared = None  # one SharedThreshold per process (its set-up is collective)
+
     def __init__(self, idx, k, world, exchange, dev):
         from circuit_rag import _native
 
+        if exchange == "shared" and Searcher._shared is None:
+            from circuit_rag.shard import SharedThreshold
+
+            Searcher._shared = SharedThreshold(torch.device(dev), None)
+        self.shared = Searcher._shared if exchange == "shared" else None
         self.L = _native.lib()
         self.h = idx.native_handle()
         self.k, self.world, self.exchange = k, world, exchange
@@ -379,6 +389,14 @@ class Searcher:
         assert self.L.circuit_search_seed_async(self.h, q.data_ptr(), self.k, self.T.data_ptr(),
                                                 self.stream.cuda_stream) == 0
         dist.all_reduce(self.T, op=dist.ReduceOp.MAX)
+        if self.shared is not None:
+            sh = self.shared
+            sh.tag = ((sh.tag + 1) & 0xFFFFFFFF) or 1
+            assert self.L.circuit_search_finish_shared_async(
+                self.h, q.data_ptr(), self.k, self.T.data_ptr(), sh.word.data_ptr(), sh.peers.data_ptr(), sh.n_peers,
+                sh.tag, self.s.data_ptr(), self.i.data_ptr(), None, self.stream.cuda_stream,
+                e0.cuda_event if e0 is not None else None, e1.cuda_event if e1 is not None else None) == 0
+            return
         assert self.L.circuit_search_finish_async(self.h, q.data_ptr(), self.k, self.T.data_ptr(), self.s.data_ptr(),
                                                   self.i.data_ptr(), None, self.stream.cuda_stream,
                                                   e0.cuda_event if e0 is not None else None,
@@ -787,6 +805,8 @@ def main():
     info = idx.shard_info
     n_local = idx.N
     exchange = world > 1 and not args.no_threshold_exchange
+    if exchange and args.shared_threshold:
+        exchange = "shared"
 
     steps, warm = args.steps, args.warmup
     Q = w.query_batch(steps + warm, device=dev)

@@ -52,6 +52,10 @@ EXPORTED_SYMBOLS = (
     "circuit_batch_overflow",
     "circuit_search_batch",
     "circuit_search_batch_device",
+    "circuit_search_finish_shared_async",
+    "circuit_ipc_export",
+    "circuit_ipc_import",
+    "circuit_ipc_close",
 )
 
 
@@ -126,6 +130,11 @@ def _declare(lib):
         "circuit_batch_overflow": (_I, [_P, _P]),
         "circuit_search_batch": (_I, [_P, _P, _I, _I, _P, _P]),
         "circuit_search_batch_device": (_I, [_P, _P, _I, _I, _P, _P]),
+        "circuit_search_finish_shared_async": (_I, [_P, _P, _I, _P, _P, _P, _I, ctypes.c_uint32, _P, _P, _P, _P, _P,
+                                                    _P]),
+        "circuit_ipc_export": (_I, [_P, _P, _P]),
+        "circuit_ipc_import": (_I, [_P, _I, _P]),
+        "circuit_ipc_close": (_I, [_P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -201,6 +201,61 @@ def merge_topk_host(scores: torch.Tensor, ids: torch.Tensor, k: int) -> Tuple[to
     return out_s, out_i
 
 
+class SharedThreshold:
+    """The running threshold shared by the ranks of a process group that search
+    the same query on their shards (circuit_search_finish_shared_async): every
+    rank owns one 64-bit word on its GPU; the words' CUDA IPC handles are
+    all-gathered and every rank opens the others', so each rank's main scan
+    raises every word with the k-th best scores it finds and prunes with the
+    largest one carrying the query's tag.  The tag is a counter advanced by
+    finish(), identical on every rank as long as every rank searches the same
+    queries in the same order.  Construction is collective."""
+
+    def __init__(self, device: torch.device, group=None):
+        import torch.distributed as dist
+
+        self.dist, self.group = dist, group
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        lib = _native.lib()
+        self.word = torch.zeros(1, dtype=torch.int64, device=device)
+        handle = (ctypes.c_ubyte * 64)()
+        offset = ctypes.c_int64()
+        _native.check(lib.circuit_ipc_export(self.word.data_ptr(), handle, ctypes.byref(offset)), "ipc export")
+        mine = torch.tensor(list(bytes(handle)) + list(int(offset.value).to_bytes(8, "little", signed=True)),
+                            dtype=torch.uint8, device=device)
+        every = torch.empty(world * 72, dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        every = every.cpu().numpy().reshape(world, 72)
+        self.imported, peers = [], []
+        for r in range(world):
+            if r == rank:
+                continue
+            ptr = ctypes.c_void_p()
+            _native.check(lib.circuit_ipc_import(every[r, :64].tobytes(), device.index, ctypes.byref(ptr)),
+                          "ipc import")
+            self.imported.append(ptr.value)
+            peers.append(ptr.value + int.from_bytes(every[r, 64:].tobytes(), "little", signed=True))
+        self.peers = torch.tensor(peers or [0], dtype=torch.int64, device=device)
+        self.n_peers = len(peers)
+        self.tag = 0
+        dist.barrier(group=group)  # every rank's peers are open before any scan writes to them
+
+    def finish(self, index, query, k, T, scores, ids, stream):
+        """circuit_search_finish_shared_async for the next query (advances the tag)."""
+        self.tag = ((self.tag + 1) & 0xFFFFFFFF) or 1
+        rc = _native.lib().circuit_search_finish_shared_async(
+            index.native_handle(), _aligned(query).data_ptr(), int(k), T.data_ptr() if T is not None else None,
+            self.word.data_ptr(), self.peers.data_ptr(), self.n_peers, self.tag, scores.data_ptr(), ids.data_ptr(),
+            None, stream, None, None)
+        _native.check(rc, "circuit_search_finish_shared_async")
+
+    def close(self):
+        self.dist.barrier(group=self.group)
+        for p in self.imported:
+            _native.lib().circuit_ipc_close(p)
+        self.imported = []
+
+
 class ShardedSearcher:
     """Exact top-k over a corpus sharded across the ranks of a process group."""
 
@@ -215,6 +270,19 @@ class ShardedSearcher:
         self.index = index
         self._local = local_search or self._native_local
         self._merge = merge or merge_topk
+        self._shared = None  # SharedThreshold (enable_shared_threshold)
+
+    def enable_shared_threshold(self):
+        """Share the running threshold of a search between the ranks while their
+        scans run (circuit_search_finish_shared_async; see SharedThreshold).
+        Collective; used by search(..., exchange_threshold=True)."""
+        self._shared = SharedThreshold(self.index.leaf_vectors.device, self.group)
+
+    def close_shared_threshold(self):
+        """Collective: no rank may still be searching."""
+        if self._shared is not None:
+            self._shared.close()
+            self._shared = None
 
     def _native_local(self, query: torch.Tensor, k: int, min_hierarchy_n: int):
         from circuit_rag.search import circuit_search
@@ -254,9 +322,12 @@ class ShardedSearcher:
     def _native_finish(self, query: torch.Tensor, k: int, T: torch.Tensor):
         s = torch.empty(k, dtype=torch.float32, device=query.device)
         i = torch.empty(k, dtype=torch.int32, device=query.device)
+        st = torch.cuda.current_stream(query.device).cuda_stream
+        if self._shared is not None:
+            self._shared.finish(self.index, query, k, T, s, i, st)
+            return s, i
         rc = _native.lib().circuit_search_finish_async(self.index.native_handle(), _aligned(query).data_ptr(), int(k),
-                                                       T.data_ptr(), s.data_ptr(), i.data_ptr(), None,
-                                                       torch.cuda.current_stream(query.device).cuda_stream, None,
+                                                       T.data_ptr(), s.data_ptr(), i.data_ptr(), None, st, None,
                                                        None)
         _native.check(rc, "circuit_search_finish_async")
         return s, i

@@ -192,9 +192,20 @@ cudaError_t launch_search(const IndexView& ix, const Workspace& ws, const float*
 // sampled); finish = bounds + main scan with threshold max(own seed, *T_ext).
 cudaError_t launch_search_seed(const IndexView& ix, const Workspace& ws, const float* q, int k, float* T_export,
                                cudaStream_t stream, const HostIO* io = nullptr);
+// A running threshold shared by the shards searching one query: this shard's
+// 64-bit word and a device array of the peers' words (in their GPUs' memory),
+// each holding tag << 32 | threshold key; the main scan raises them all and
+// prunes with the largest key carrying this query's tag.
+struct SharedThreshold {
+  unsigned long long* local;
+  unsigned long long* const* peers;
+  int n_peers;
+  uint32_t tag;
+};
 cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const float* q, int k, const float* T_ext,
                                  float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
-                                 cudaEvent_t ev_scan0, cudaEvent_t ev_scan1, const HostIO* io = nullptr);
+                                 cudaEvent_t ev_scan0, cudaEvent_t ev_scan1, const HostIO* io = nullptr,
+                                 const SharedThreshold* shared = nullptr);
 
 // Flat exact top-k of leaf[0..N) . q with caller-provided scratch: ctrl (its
 // first CTRL_RESET_BYTES zeroed by the caller), range = {0, 0, N, -1},

@@ -23,6 +23,9 @@
 #include <string>
 #include <vector>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "../../include/circuit.h"
 #include "../../include/circuit_shard.h"
 #include "engine.h"
@@ -1145,6 +1148,82 @@ int circuit_search_finish_async(circuit_index_t index, const float* dev_query, i
   index->last_stream = st;
   if (e != cudaSuccess) { set_error(std::string("finish launch: ") + cudaGetErrorString(e)); return CIRCUIT_ERR_CUDA; }
   return CIRCUIT_OK;
+}
+
+int circuit_search_finish_shared_async(circuit_index_t index, const float* dev_query, int k,
+                                       const float* dev_threshold_in, unsigned long long* dev_shared_word,
+                                       unsigned long long* const* dev_peer_words, int num_peers, uint32_t query_tag,
+                                       float* dev_out_scores, int* dev_out_ids, int64_t* dev_out_rows, void* stream,
+                                       void* ev_scan_begin, void* ev_scan_end) {
+  if (!index) return CIRCUIT_ERR_NULL;
+  if (k < 1 || k > cb::KMAX) { set_error("k must be in [1, " + std::to_string(cb::KMAX) + "]"); return CIRCUIT_ERR_ARG; }
+  if (!dev_query || !dev_out_scores || ((uintptr_t)dev_query & 15)) {
+    set_error("null or misaligned pointer");
+    return CIRCUIT_ERR_ARG;
+  }
+  if (!dev_shared_word || ((uintptr_t)dev_shared_word & 7) || num_peers < 0 || num_peers > 1024 ||
+      (num_peers > 0 && (!dev_peer_words || ((uintptr_t)dev_peer_words & 7)))) {
+    set_error("shared threshold: null or misaligned word, or a bad peer list");
+    return CIRCUIT_ERR_ARG;
+  }
+  if (k != index->last_k || index->last_path != 1) {
+    set_error("circuit_search_finish_shared_async must follow circuit_search_seed_async with the same k");
+    return CIRCUIT_ERR_ARG;
+  }
+  if (!cuda_ok(cudaSetDevice(index->device), "cudaSetDevice")) return CIRCUIT_ERR_CUDA;
+  cudaStream_t st = (cudaStream_t)stream;
+  const cb::SharedThreshold sh{dev_shared_word, dev_peer_words, num_peers, query_tag};
+  cudaError_t e = cb::launch_search_finish(index->view, index->ws, dev_query, k, dev_threshold_in, dev_out_scores,
+                                           dev_out_ids, (long long*)dev_out_rows, st, (cudaEvent_t)ev_scan_begin,
+                                           (cudaEvent_t)ev_scan_end, nullptr, &sh);
+  index->last_stream = st;
+  if (e != cudaSuccess) { set_error(std::string("finish launch: ") + cudaGetErrorString(e)); return CIRCUIT_ERR_CUDA; }
+  return CIRCUIT_OK;
+}
+
+int circuit_ipc_export(const void* dev_ptr, void* handle_out, int64_t* offset_out) {
+  if (!dev_ptr || !handle_out) { set_error("null pointer"); return CIRCUIT_ERR_ARG; }
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  // the allocation holding dev_ptr (an IPC handle names an allocation's start)
+  static PFN_cuMemGetAddressRange_v3020 range_fn = nullptr;
+  if (!range_fn) {
+    void* fp = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fp, cudaEnableDefault, &qr) != cudaSuccess ||
+        qr != cudaDriverEntryPointSuccess || !fp) {
+      set_error("circuit_ipc_export: cuMemGetAddressRange unavailable");
+      return CIRCUIT_ERR_CUDA;
+    }
+    range_fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fp);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, (CUdeviceptr)dev_ptr) != CUDA_SUCCESS) {
+    set_error("circuit_ipc_export: not device memory");
+    return CIRCUIT_ERR_ARG;
+  }
+  cudaIpcMemHandle_t h;
+  if (!cuda_ok(cudaIpcGetMemHandle(&h, (void*)base), "cudaIpcGetMemHandle")) return CIRCUIT_ERR_CUDA;
+  std::memcpy(handle_out, &h, sizeof(h));
+  if (offset_out) *offset_out = (int64_t)((CUdeviceptr)dev_ptr - base);
+  return CIRCUIT_OK;
+}
+
+int circuit_ipc_import(const void* handle, int device_id, void** dev_ptr_out) {
+  if (!handle || !dev_ptr_out) { set_error("null pointer"); return CIRCUIT_ERR_ARG; }
+  if (!cuda_ok(cudaSetDevice(device_id), "cudaSetDevice")) return CIRCUIT_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (!cuda_ok(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle"))
+    return CIRCUIT_ERR_CUDA;
+  *dev_ptr_out = p;
+  return CIRCUIT_OK;
+}
+
+int circuit_ipc_close(void* dev_ptr) {
+  if (!dev_ptr) { set_error("null pointer"); return CIRCUIT_ERR_ARG; }
+  return cuda_ok(cudaIpcCloseMemHandle(dev_ptr), "cudaIpcCloseMemHandle") ? CIRCUIT_OK : CIRCUIT_ERR_CUDA;
 }
 
 int circuit_search_async(circuit_index_t index, const float* dev_query, int k, int64_t min_hierarchy_n,

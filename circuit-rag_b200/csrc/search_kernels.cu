@@ -84,6 +84,13 @@ struct ScanParams {
   const uint32_t* n_live;
   uint32_t* list_next;
   uint32_t* chunk_taken;                      // per chunk: epoch of the search that streams it
+  // sharded search: a running threshold shared by the shards searching the same
+  // query, as words tag << 32 | key (key of a k-th best score of k real rows of
+  // some shard); this shard reads xth_local and raises it and every peer's word
+  unsigned long long* xth_local;              // (null: not shared)
+  unsigned long long* const* xth_peers;       // device array of n_peers pointers (peer GPUs' memory)
+  int n_peers;
+  uint32_t xth_tag;                           // the query's number, the same on every shard
   const float* T_ext;                         // a threshold from outside the index (or null)
   uint32_t* rows_streamed;                    // rows read, summed over CTAs (or null)
   int overlapped;                             // launched beside the bounds kernel (no wait before streaming)
@@ -129,6 +136,15 @@ constexpr int FINAL_RANK_CAP = 512;
 // equal slices.
 constexpr int SCAN_DYN_CHUNKS = 48;
 constexpr int SCAN_DYN_MIN_STAGES = 8;
+
+// A new running threshold key of this shard, for the other shards searching the
+// same query (fire-and-forget atomics, over NVLink for a peer's word).
+__device__ __forceinline__ void share_threshold(const ScanParams& P, uint32_t key) {
+  if (!P.xth_local) return;
+  const unsigned long long w = ((unsigned long long)P.xth_tag << 32) | key;
+  atomicMax(P.xth_local, w);
+  for (int i = 0; i < P.n_peers; ++i) atomicMax(P.xth_peers[i], w);
+}
 
 template <int VPL, int KCAP>
 __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
@@ -368,7 +384,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     uint32_t taken_old = 0u;
     int4 pw = make_int4(0, 0, 0, 0), pw2 = pw;
     unsigned long long pt = 0ull, pt2 = 0ull;
-    uint32_t ppkey = 0u;
+    uint32_t pth = 0u;               // (the running threshold as read for the next chunk)
+    unsigned long long pxw = 0ull;   // (the shared word as read for the next chunk)
     const auto start_chunk = [&]() {
       if (table) {
         if (lane == 0) taken_old = atomicExch(P.chunk_taken + nj, epoch);
@@ -397,7 +414,11 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
           pw = load_window(pbase, pt);
           pw2 = load_window(pbase + 32, pt2);
         }
-        ppkey = prune ? max(s_text, ld_volatile_u32(P.theta_key)) : 0u;
+        // raw reads, combined when the chunk is taken (no stall here)
+        if (prune) {
+          pth = ld_volatile_u32(P.theta_key);
+          if (P.xth_local) pxw = ld_volatile_u64(P.xth_local);
+        }
         pf = 3;
       }
     };
@@ -418,7 +439,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
           pw2 = fw1;
           pt = ft0;
           pt2 = ft1;
-          ppkey = s_theta0;
+          pth = s_theta0;
           pf = 3;
         }
       }
@@ -460,7 +481,13 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
         win_next = pw2;
         ubk = decode(pt);
         tag_next = pt2;
-        pkey = ppkey;
+        pkey = max(s_text, pth);
+        if (P.xth_local && (uint32_t)(pxw >> 32) == P.xth_tag && (uint32_t)pxw > pkey) {
+          // another shard's k-th best is higher: it becomes this shard's running
+          // threshold too (the consumers read it from the threshold line)
+          pkey = (uint32_t)pxw;
+          if (lane == 0) atomicMax(P.theta_key, pkey);
+        }
         set_range();
         if ((uint32_t)rg.x > vb) {  // the range must start at or before the chunk
           fail_range();
@@ -593,7 +620,10 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       if (kth > theta_w) {
         theta_w = kth;
         if (kth > published) {
-          if (lane == 0) atomicMax(P.theta_key, kth);
+          if (lane == 0) {
+            atomicMax(P.theta_key, kth);
+            share_threshold(P, kth);
+          }
           published = kth;
         }
       }
@@ -727,7 +757,10 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
       const unsigned long long kth = __shfl_sync(FULL_MASK, m, k - 1);
       if (lane < k) {
         P.cta_lists[(size_t)blockIdx.x * k + lane] = m;
-        if (lane == 0 && kth != 0ull && cand_key(kth) > s_theta) atomicMax(P.theta_key, cand_key(kth));
+        if (lane == 0 && kth != 0ull && cand_key(kth) > s_theta) {
+          atomicMax(P.theta_key, cand_key(kth));
+          share_threshold(P, cand_key(kth));
+        }
         __threadfence();
       }
       __syncwarp();
@@ -741,7 +774,10 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
     if (tid < k) {
       const unsigned long long c = sel[tid];
       P.cta_lists[(size_t)blockIdx.x * k + tid] = c;
-      if (tid == k - 1 && c != 0ull && cand_key(c) > s_theta) atomicMax(P.theta_key, cand_key(c));
+      if (tid == k - 1 && c != 0ull && cand_key(c) > s_theta) {
+        atomicMax(P.theta_key, cand_key(c));
+        share_threshold(P, cand_key(c));
+      }
       __threadfence();
     }
   }
@@ -1745,7 +1781,8 @@ cudaError_t launch_search_seed(const IndexView& ix, const Workspace& ws, const f
 
 cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const float* q, int k, const float* T_ext,
                                  float* out_scores, int* out_ids, long long* out_rows, cudaStream_t stream,
-                                 cudaEvent_t ev_scan0, cudaEvent_t ev_scan1, const HostIO* io) {
+                                 cudaEvent_t ev_scan0, cudaEvent_t ev_scan1, const HostIO* io,
+                                 const SharedThreshold* shared) {
   cudaError_t e;
   const int chunk_rows = bounds_chunk_rows(ix.D, ix.rank);
   const BoundsLayout BL = bounds_layout(ix.D, ix.rank, chunk_rows);
@@ -1772,6 +1809,12 @@ cudaError_t launch_search_finish(const IndexView& ix, const Workspace& ws, const
   M.n_live = &ws.sync->n_live;
   M.list_next = &ws.sync->list_next;
   M.chunk_taken = ws.chunk_taken;
+  if (shared && shared->local) {
+    M.xth_local = shared->local;
+    M.xth_peers = shared->peers;
+    M.n_peers = shared->peers ? shared->n_peers : 0;
+    M.xth_tag = shared->tag;
+  }
   M.T_ext = T_ext;
   M.rows_streamed = &ws.ctrl->rows_streamed;
   M.overlapped = 1;

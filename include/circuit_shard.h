@@ -73,6 +73,39 @@ int circuit_plan_shard_parts(const int64_t* atom_rows, const int64_t* root_atom_
  * loads the whole file). */
 circuit_index_t circuit_load_shard(const char* filepath, int rank, int world, int device_id, double max_imbalance);
 
+/* circuit_search_finish_async with a running threshold shared by the shards
+ * that search the same query (no reference counterpart; north_star's "running
+ * global threshold exchanged to tighten per-shard pruning").  Each shard owns
+ * one 64-bit word in its GPU's memory, dev_shared_word (8-byte aligned); its
+ * main scan raises that word and every peer's (dev_peer_words: a device array
+ * of num_peers pointers to the other shards' words, e.g. opened with
+ * circuit_ipc_import) with query_tag << 32 | key whenever it finds a higher
+ * k-th best, and prunes with the largest key carrying query_tag that it reads
+ * from its own word.  Every key is the k-th best score of k real rows of some
+ * shard, so it never exceeds the global k-th best and the merged top-k stays
+ * exact.  query_tag must be the same on every shard for one query and differ
+ * from the previous queries' (a counter); words carrying another tag are
+ * ignored, so the words need no clearing between queries.  The peers' words are
+ * written with remote atomics while their scans run (no TMA, no multicast).
+ * Other arguments and the order of calls as in circuit_search_finish_async. */
+int circuit_search_finish_shared_async(circuit_index_t index, const float* dev_query, int k,
+                                       const float* dev_threshold_in, unsigned long long* dev_shared_word,
+                                       unsigned long long* const* dev_peer_words, int num_peers, uint32_t query_tag,
+                                       float* dev_out_scores, int* dev_out_ids, int64_t* dev_out_rows, void* stream,
+                                       void* ev_scan_begin, void* ev_scan_end);
+
+/* CUDA IPC for the shared threshold words of shards in separate processes:
+ * circuit_ipc_export writes the 64-byte handle of the allocation holding
+ * dev_ptr (device memory from cudaMalloc or a caching allocator block; the
+ * handle names the start of that allocation, *offset_out the byte offset of
+ * dev_ptr in it); circuit_ipc_import opens a handle from another process on
+ * device_id (with peer access to the exporter's GPU enabled) and returns the
+ * mapped allocation start; circuit_ipc_close unmaps it.  Not for handles of the
+ * same process. */
+int circuit_ipc_export(const void* dev_ptr, void* handle_out, int64_t* offset_out);
+int circuit_ipc_import(const void* handle, int device_id, void** dev_ptr_out);
+int circuit_ipc_close(void* dev_ptr);
+
 #ifdef __cplusplus
 }
 #endif

@@ -107,3 +107,58 @@ def build_worker(rank, world, port, root, n, out_path):
     with open(out_path + ".json", "w") as f:
         json.dump(idx.shard_info, f)
     dist.destroy_process_group()
+
+
+def ipc_word_worker(rank, root, conn, barrier, result_q):
+    """One of two processes on one GPU that open each other's shared threshold
+    word through CUDA IPC and search the same query with the same tag."""
+    _paths(root)
+    import ctypes
+    import dataclasses
+
+    import numpy as np
+
+    import torch
+
+    from circuit_rag import _native, build_circuit_index
+    from circuit_rag.synthetic import WORKLOADS
+
+    try:
+        torch.cuda.set_device(0)
+        w = dataclasses.replace(WORKLOADS["clustered-50k"], name="c200k", n=200_000)
+        X = w.corpus(device="cuda")
+        idx = build_circuit_index(X, num_roots=w.num_roots, children_per_root=w.children_per_root, rank=w.rank,
+                                  device="cuda")
+        L = _native.lib()
+        word = torch.zeros(1, dtype=torch.int64, device="cuda")
+        handle = (ctypes.c_ubyte * 64)()
+        off = ctypes.c_int64()
+        assert L.circuit_ipc_export(word.data_ptr(), handle, ctypes.byref(off)) == 0, _native.last_error()
+        conn.send((bytes(handle), off.value))
+        peer_handle, peer_off = conn.recv()
+        ptr = ctypes.c_void_p()
+        assert L.circuit_ipc_import(peer_handle, 0, ctypes.byref(ptr)) == 0, _native.last_error()
+        peers = torch.tensor([ptr.value + peer_off], dtype=torch.int64, device="cuda")
+        barrier.wait(timeout=120)
+        q = w.query_batch(3, device="cuda")[2].contiguous()
+        k = w.k
+        st = torch.cuda.current_stream().cuda_stream
+        T = torch.empty(1, device="cuda")
+        s = torch.empty(k, device="cuda")
+        i = torch.empty(k, dtype=torch.int32, device="cuda")
+        assert L.circuit_search_seed_async(idx.native_handle(), q.data_ptr(), k, T.data_ptr(), st) == 0
+        assert L.circuit_search_finish_shared_async(idx.native_handle(), q.data_ptr(), k, T.data_ptr(),
+                                                    word.data_ptr(), peers.data_ptr(), 1, 7, s.data_ptr(),
+                                                    i.data_ptr(), None, st, None, None) == 0
+        torch.cuda.synchronize()
+        exact = (X.double() @ q.double()).cpu().numpy()
+        oracle_kth = float(np.sort(exact)[-k])
+        ok_ids = set(np.argsort(-exact)[:k].tolist())
+        barrier.wait(timeout=120)  # both scans are complete: both words are final
+        torch.cuda.synchronize()
+        result_q.put((rank, int(word.item()), oracle_kth, sorted(i.cpu().tolist()) == sorted(ok_ids)))
+        barrier.wait(timeout=120)  # the peer has read its word before the mapping goes
+        assert L.circuit_ipc_close(ptr) == 0
+        idx.close()
+    except Exception as e:  # reported to the parent
+        result_q.put((rank, None, repr(e), False))
