@@ -360,9 +360,10 @@ class Searcher:
 
     _shared = None  # one SharedThreshold per process (its set-up is collective)
 
-    def __init__(self, idx, k, world, exchange, dev):
+    def __init__(self, idx, k, world, exchange, dev, min_hier=0):
         from circuit_rag import _native
 
+        self.min_hier = min_hier
         if exchange == "shared" and Searcher._shared is None:
             from circuit_rag.shard import SharedThreshold
 
@@ -382,7 +383,7 @@ class Searcher:
         from circuit_rag.search import _launch
 
         if not self.exchange:
-            _launch(self.h, q, self.k, 0, self.s, self.i, None, self.stream, e0, e1)
+            _launch(self.h, q, self.k, self.min_hier, self.s, self.i, None, self.stream, e0, e1)
             return
         import torch.distributed as dist
 
@@ -415,7 +416,7 @@ class Searcher:
         return merge_topk(self.gs, self.gi, self.k)
 
 
-def single_query(idx, Q, k, warm, steps, world, exchange, dev, scan_events=True):
+def single_query(idx, Q, k, warm, steps, world, exchange, dev, scan_events=True, min_hier=0):
     """Timed single queries: returns dict(value, p50, p99, scan_ms, main_rows,
     seed_rows, streamed_rows, scan_rows, out_s, out_i, elapsed_ms).
 
@@ -430,7 +431,7 @@ def single_query(idx, Q, k, warm, steps, world, exchange, dev, scan_events=True)
 
     from circuit_rag import _native
 
-    se = Searcher(idx, k, world, exchange, dev)
+    se = Searcher(idx, k, world, exchange, dev, min_hier)
     stream = se.stream
     out_s = torch.empty((steps, k), device=dev)
     out_i = torch.empty((steps, k), dtype=torch.int32, device=dev)
@@ -723,6 +724,9 @@ def other_workloads(dev, hbm_peak):
             sq = single_query(idx, Q, w.k, 20, n_q, 1, False, dev, scan_events=False)
             ex_s, ex_i = exact_topk(idx.leaf_vectors, idx.original_ids, Q[20:20 + n_q], w.k)
             bad = count_mismatches(sq["out_s"], sq["out_i"], ex_s, ex_i, w.k)
+            # the same queries through the flat scan (no bounds): where pruning pays
+            fq = single_query(idx, Q, w.k, 20, n_q, 1, False, dev, scan_events=False, min_hier=1 << 40)
+            bad += count_mismatches(fq["out_s"], fq["out_i"], ex_s, ex_i, w.k)
             mean_rows = statistics.mean(sq["main_rows"])
             scan = statistics.mean(sq["scan_ms"])
             scan_rows = statistics.mean(sq["scan_rows"])
@@ -730,7 +734,9 @@ def other_workloads(dev, hbm_peak):
             R, C, D, rk = idx.num_roots, idx.num_total_children, w.dim, w.rank
             meta_bytes = 4 * R * D + 4 * R * D * rk + 4 * C * (2 * rk + 2) + statistics.mean(sq["seed_rows"]) * D * 4
             r.update({"single_query_qps": round(sq["value"], 1), "p50_us": round(sq["p50_us"], 2),
-                      "p99_us": round(sq["p99_us"], 2), "pruned_leaf_fraction": round(1 - mean_rows / w.n, 5),
+                      "p99_us": round(sq["p99_us"], 2),
+                      "flat_scan": {"p50_us": round(fq["p50_us"], 2), "p99_us": round(fq["p99_us"], 2)},
+                      "pruned_leaf_fraction": round(1 - mean_rows / w.n, 5),
                       "rows_streamed_fraction": round(statistics.mean(sq["streamed_rows"]) / w.n, 5),
                       "main_scan": {"rows": scan_rows, "mean_launch_us": round(scan * 1000, 2),
                                     "frac_of_hbm": round(scan_rows * w.dim * 4 / (scan * 1e-3) / 1e9 / hbm_peak, 4),
@@ -740,7 +746,8 @@ def other_workloads(dev, hbm_peak):
                                          "frac_of_hbm_at_p50": round((leaf_bytes + meta_bytes) / (sq["p50_us"] * 1e-6)
                                                                      / 1e9 / hbm_peak, 4)},
                       "phase_split": phase_split(idx, Q, w.k, dev),
-                      "check": {"checked_queries": n_q, "mismatches": bad}})
+                      "check": {"checked_queries": 2 * n_q, "mismatches": bad,
+                                "how": "float64 brute force on the device, hierarchical and flat"}})
         r["host_to_host"] = host_to_host(idx, Q, w.k, 2000)
         out[name] = r
         idx.close()
