@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) k_scan(ScanParams P) {
           continue;
         }
         const uint32_t i = (uint32_t)r;
-        if (i >= n_live) return -1;
+        if (i >= n_live || i >= n_chunks) return -1;
         list_entry = (uint32_t)__ldcg(P.live_list + i);
         claim();
         return -2;
@@ -1522,20 +1522,29 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
             total += (uint32_t)__popc(bal[u]);
           }
           if (total == 0u) continue;
-          uint32_t at = 0u;
+          // the first entries fill the shared staging up to LIST_SMEM, the
+          // others go straight to the list (their own reservation): no slot
+          // of either is left unused, so the list holds at most n_scan_chunks
+          uint32_t at = 0u, gat = 0u;
           if (lane == 0) at = atomicAdd(&s_nlist, total);
           at = __shfl_sync(FULL_MASK, at, 0);
-          int* dst = s_list;
-          if (at + total > LIST_SMEM) {  // shared staging full: straight to the list
-            for (uint32_t i = at + lane; i < LIST_SMEM; i += 32) s_list[i] = -1;  // (reserved, unused)
-            if (lane == 0) at = atomicAdd(&sync->n_live, total);
-            at = __shfl_sync(FULL_MASK, at, 0);
-            dst = live_list;
-          }
+          const uint32_t n_sm = at < LIST_SMEM ? min(total, LIST_SMEM - at) : 0u;
+          if (lane == 0 && total > n_sm) gat = atomicAdd(&sync->n_live, total - n_sm);
+          gat = __shfl_sync(FULL_MASK, gat, 0);
+          uint32_t idx = 0u;  // entries of this batch before the current step
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            if (fresh[u]) dst[at + __popc(bal[u] & lanemask_lt())] = jlo + t0 + u;
-            at += (uint32_t)__popc(bal[u]);
+            if (fresh[u]) {
+              const uint32_t e = idx + (uint32_t)__popc(bal[u] & lanemask_lt());
+              if (e < n_sm) {
+                s_list[at + e] = jlo + t0 + u;
+              } else if (gat + (e - n_sm) < n_scan_chunks) {
+                live_list[gat + (e - n_sm)] = jlo + t0 + u;
+              } else {
+                atomicOr(&ctrl->error, ERR_BAD_RANGE);  // (cannot happen: every chunk is listed once)
+              }
+            }
+            idx += (uint32_t)__popc(bal[u]);
           }
         }
       }
@@ -1560,7 +1569,10 @@ __global__ void __launch_bounds__(BOUNDS_WARPS * 32) k_bounds(IndexView ix, cons
   }
   if (!chunk_mark) return;
   __syncthreads();
-  for (uint32_t i = threadIdx.x; i < min(s_nlist, LIST_SMEM); i += blockDim.x) live_list[s_base + i] = s_list[i];
+  for (uint32_t i = threadIdx.x; i < min(s_nlist, LIST_SMEM); i += blockDim.x) {
+    if (s_base + i < n_scan_chunks) live_list[s_base + i] = s_list[i];
+    else atomicOr(&ctrl->error, ERR_BAD_RANGE);  // (cannot happen: every chunk is listed once)
+  }
   __threadfence();  // each thread's list entries reach the GPU before the CTA's ticket
   __syncthreads();
   if (threadIdx.x == 0 && atomicAdd(&sync->bounds_done, 1u) == gridDim.x - 1) {

@@ -161,4 +161,7 @@ def test_chunk_and_list_shapes(law, n, roots, cpr):
                                           ev0.cuda_event, ev1.cuda_event) == 0
             _check(X, q, kk, s2, i2)
             assert torch.equal(i, i2) and torch.equal(s, s2)
+            tx = _native.TraceEx()
+            assert L.circuit_last_trace(h, ctypes.byref(tx)) == 0
+            assert tx.device_error == 0  # (a list or range bounds check would set a bit)
     idx.close()
