@@ -74,8 +74,8 @@ int circuit_plan_shard_parts(const int64_t* atom_rows, const int64_t* root_atom_
 circuit_index_t circuit_load_shard(const char* filepath, int rank, int world, int device_id, double max_imbalance);
 
 /* circuit_search_finish_async with a running threshold shared by the shards
- * that search the same query (no reference counterpart; north_star's "running
- * global threshold exchanged to tighten per-shard pruning").  Each shard owns
+ * that search the same query, exchanged while their scans run to tighten each
+ * shard's pruning (no reference counterpart: the reference is single-GPU).  Each shard owns
  * one 64-bit word in its GPU's memory, dev_shared_word (8-byte aligned); its
  * main scan raises that word and every peer's (dev_peer_words: a device array
  * of num_peers pointers to the other shards' words, e.g. opened with
