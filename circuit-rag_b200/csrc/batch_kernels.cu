@@ -27,8 +27,9 @@
 //                 query's candidate list, with its tf32 score.  The threshold
 //                 is always the tf32 score of the k-th best of k distinct rows:
 //                 for k <= 32 a per-thread top-k in registers plus rotated
-//                 per-query slots, for larger k slots keyed by row (see
-//                 slot_min).
+//                 per-query slots; for larger k, 4k slots keyed by row whose
+//                 k-th largest a seventh warp per CTA keeps published (see
+//                 threshold_sweeps).
 //               Both operands are streamed: with the queries resident in TMEM
 //               (384 of 512 columns at D = 384) only N = 64 accumulators fit,
 //               4x the MMA instructions per flop of N = 256.
@@ -62,6 +63,8 @@ constexpr int BN = 256;                  // leaf rows per tile (UMMA N); each CT
 constexpr int HALF_N = BN / 2;
 constexpr int EPI_COLS = 64;             // accumulator columns per epilogue pass
 constexpr int BATCH_THREADS = 192;       // warps 0-3 epilogue, 4 TMA, 5 MMA
+constexpr int BATCH_THREADS_SLOTS = 224; // k > 32: + warp 6, the threshold warp
+constexpr int THRESHOLD_MAX_SWEEPS = 1 << 24;  // bound of the threshold warp's loop
 constexpr int BATCH_MAX_STAGES = 8;
 constexpr int SLICE_ROWS = 8192;         // rows per work unit of the main pass
 constexpr int SEED_ROWS = 32768;         // rows of the threshold pass (one unit per query tile)
@@ -86,7 +89,8 @@ struct BatchScanParams {
   int cap;
   int* err;
   int seed_only;         // threshold pass: raise theta, append no candidates
-  uint32_t* slots;       // [B * k] per-query threshold slots (slot_min)
+  uint32_t* slots;       // [B * nslots] per-query threshold slots
+  int nslots;            // slots per query (batch_slot_count(k))
   int row_step;          // leaf row = scan row * row_step (threshold pass: sampled rows)
   int* unit_counter;     // next work unit (dynamic scheduling; zeroed before the launch)
   int slice_rows;        // rows per work unit
@@ -153,40 +157,72 @@ __device__ __forceinline__ void epi_pass_topk(const uint32_t (&sc0)[32], const u
   }
 }
 
-// Per-query threshold from k slots.  Leaf row r publishes its tf32 score into
-// slot r mod k by atomicMax.  The slots cover disjoint sets of rows, so each
-// holds the score of one real row and no row is in two slots: the smallest
-// slot is the k-th best of k distinct rows, a valid threshold (0 = a slot not
-// yet filled).  A row always maps to the same slot, so rows seen twice (the
-// threshold pass samples rows that the main pass scans again) cannot count
-// twice.  No per-thread top-k list is needed, for any k.
-// The slots are read through L2 (other threads raise them with atomicMax; a
-// stale value is still one real row's score, so the minimum stays valid), 16
-// bytes at a time with the loads issued together: k = 100 slots take a few L2
-// round trips, not one per slot.
-__device__ __forceinline__ uint32_t slot_min(const uint32_t* sl, int k) {
-  uint32_t m0 = 0xffffffffu, m1 = m0, m2 = m0, m3 = m0;
-  int i = 0;
-  for (; i < k && (reinterpret_cast<uintptr_t>(sl + i) & 15u); ++i) m0 = min(m0, __ldcg(sl + i));
-  const uint4* v4 = reinterpret_cast<const uint4*>(sl + i);
-  const int n4 = (k - i) >> 2;
-#pragma unroll 8
-  for (int j = 0; j < n4; ++j) {
-    const uint4 v = __ldcg(v4 + j);
-    m0 = min(m0, v.x);
-    m1 = min(m1, v.y);
-    m2 = min(m2, v.z);
-    m3 = min(m3, v.w);
+// Per-query threshold from 4k slots (k > 32).  Leaf row r publishes its tf32
+// score key into slot r mod nslots by atomicMax (0 = a slot not yet filled).
+// The slots cover disjoint sets of rows, so each holds the score of one real
+// row and no row is in two slots: the k-th largest slot is the k-th best of k
+// distinct rows, a valid threshold.  A row always maps to the same slot, so
+// rows seen twice (the threshold pass samples rows that the main pass scans
+// again) cannot count twice.  With nslots = 4k the k-th largest slot sits near
+// the 1.15k-th best row seen (k of 4k residue classes are hit among the top
+// 4k ln(4/3) rows), where the minimum of k slots (one per residue mod k) sits
+// near the k ln k-th.
+//
+// Warp 6 of every CTA keeps the published thresholds current: it refreshes
+// queries blockIdx.x, blockIdx.x + gridDim.x, ... in turn, loading a query's
+// slots (PL per lane, coalesced, through L2: other CTAs raise them) while it
+// selects the previous query's k-th largest, by bisection on the key bits with
+// one warp-wide count per bit.  A query with fewer than k slots above its
+// published key is skipped after one count.  The epilogue threads only raise
+// slots and read the published key one tile ahead, so no L2 round trip sits on
+// their path.  The warp stops when the CTA's epilogue has finished (`done`) or
+// after THRESHOLD_MAX_SWEEPS sweeps; a stale threshold only costs candidates.
+template <int PL>
+__device__ __forceinline__ void load_slots(const uint32_t* sl, int per, int lane, uint32_t (&v)[PL]) {
+#pragma unroll
+  for (int i = 0; i < PL; ++i) v[i] = i < per ? __ldcg(sl + 32 * i + lane) : 0u;
+}
+
+template <int PL>
+__device__ void threshold_sweeps(const BatchScanParams& P, const volatile int* done) {
+  const int lane = threadIdx.x & 31;
+  const int per = P.nslots >> 5;
+  const int q0 = (int)blockIdx.x, dq = (int)gridDim.x;
+  if (q0 >= P.B) return;
+  uint32_t v[PL], nv[PL];
+  for (int sweep = 0; sweep < THRESHOLD_MAX_SWEEPS && !*done; ++sweep) {
+    load_slots<PL>(P.slots + (size_t)q0 * P.nslots, per, lane, nv);
+    for (int q = q0; q < P.B; q += dq) {
+#pragma unroll
+      for (int i = 0; i < PL; ++i) v[i] = nv[i];
+      const uint32_t cur = ld_volatile_u32(P.theta + q);
+      if (q + dq < P.B) load_slots<PL>(P.slots + (size_t)(q + dq) * P.nslots, per, lane, nv);
+      // empty slots (0) never count: cur >= 0 and every probe below is >= 1
+      int c = 0;
+#pragma unroll
+      for (int i = 0; i < PL; ++i) c += v[i] > cur;
+      if (__reduce_add_sync(FULL_MASK, (unsigned)c) < (unsigned)P.k) continue;
+      // largest x with #{slots >= x} >= k, i.e. the k-th largest slot (> cur)
+      uint32_t x = 0u;
+#pragma unroll 1
+      for (int bit = 31; bit >= 0; --bit) {
+        const uint32_t t = x | (1u << bit);
+        int n = 0;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) n += v[i] >= t;
+        if (__reduce_add_sync(FULL_MASK, (unsigned)n) >= (unsigned)P.k) x = t;
+      }
+      if (lane == 0 && x > cur) atomicMax(P.theta + q, x);
+      if (*done) break;
+    }
+    __nanosleep(500);
   }
-  for (i += 4 * n4; i < k; ++i) m1 = min(m1, __ldcg(sl + i));
-  return min(min(m0, m1), min(m2, m3));
 }
 
 // One epilogue pass over 64 accumulator columns (rows row_base + i of the scan's
 // row space) of this thread's query: rows within `band` of the threshold are
-// appended as candidates (main pass), rows above it raise their slot.  Returns
-// whether a slot was raised.
-__device__ __forceinline__ bool epi_pass(const uint32_t (&sc0)[32], const uint32_t (&sc1)[32], int row_base, int nrow,
+// appended as candidates (main pass), rows above it raise their slot.
+__device__ __forceinline__ void epi_pass(const uint32_t (&sc0)[32], const uint32_t (&sc1)[32], int row_base, int nrow,
                                          float band, float theta, int q, float* stash, const BatchScanParams& P) {
   const float lim = theta - band;
   uint64_t mask = 0ull;
@@ -196,15 +232,14 @@ __device__ __forceinline__ bool epi_pass(const uint32_t (&sc0)[32], const uint32
     mask |= (uint64_t)(__uint_as_float(sc1[i]) >= lim) << (32 + i);
   }
   if (nrow < EPI_COLS) mask &= nrow > 0 ? (1ull << nrow) - 1ull : 0ull;
-  if (!mask) return false;
+  if (!mask) return;
   // rare: stage the scores ([column][thread], conflict-free) and walk the rows
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     stash[i * BQ + threadIdx.x] = __uint_as_float(sc0[i]);
     stash[(32 + i) * BQ + threadIdx.x] = __uint_as_float(sc1[i]);
   }
-  uint32_t* sl = P.slots + (size_t)q * P.k;
-  bool raised = false;
+  uint32_t* sl = P.slots + (size_t)q * P.nslots;
   // every row of the mask is a candidate: one reservation in the query's list
   int slot = P.seed_only ? 0 : atomicAdd(P.cand_count + q, __popcll(mask));
   for (uint64_t m = mask; m; m &= m - 1ull) {
@@ -213,15 +248,13 @@ __device__ __forceinline__ bool epi_pass(const uint32_t (&sc0)[32], const uint32
     const uint32_t key = f2key(sv);
     if (sv > theta) {  // a row below every slot cannot raise one
       const uint32_t leaf_row = (uint32_t)(row_base + i) * (uint32_t)P.row_step;
-      atomicMax(sl + leaf_row % (uint32_t)P.k, key);
-      raised = true;
+      atomicMax(sl + leaf_row % (uint32_t)P.nslots, key);
     }
     if (!P.seed_only) {
       if (slot < P.cap) P.cand[(size_t)q * P.cap + slot] = ((unsigned long long)key << 32) | (uint32_t)(row_base + i);
       ++slot;
     }
   }
-  return raised;
 }
 
 // Launched as clusters of 2 CTAs.  CTA rank r of the pair loads queries
@@ -249,9 +282,10 @@ __device__ __forceinline__ int take_unit(uint64_t* unit_full, const int* ring, u
   return u;
 }
 
-// KB > 0: per-thread top-KB epilogue (k <= KB); KB == 0: slot thresholds (any k).
+// KB > 0: per-thread top-KB epilogue (k <= KB); KB == 0: slot thresholds (any
+// k) kept published by the threshold warp (warp 6, BATCH_THREADS_SLOTS threads).
 template <int KB>
-__global__ void __launch_bounds__(BATCH_THREADS, 1)
+__global__ void __launch_bounds__(KB == 0 ? BATCH_THREADS_SLOTS : BATCH_THREADS, 1)
     k_batch_scan(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap xmap,
                  BatchScanParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -264,6 +298,7 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
   __shared__ int unit_ring[UNIT_RING];
   __shared__ uint32_t tmem_base;
   __shared__ int s_err;
+  __shared__ int s_done;  // set once this CTA's epilogue has left its loop
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = tc::cluster_ctarank();
   const bool leader = rank == 0;
@@ -280,6 +315,7 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
       mbar_init(&acc_empty[b], 8);  // one lane of each epilogue warp of both CTAs
     }
     mbar_init(&drain, 1);
+    s_done = 0;
     for (int r = 0; r < UNIT_RING; ++r) {
       mbar_init(&unit_full[r], 1);
       mbar_init(&unit_empty[r], 10);  // odd producer + MMA warp + 8 epilogue warps
@@ -398,6 +434,14 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
         }
       }
     }
+  } else if (warp == 6) {
+    // ---------------------------------------------------------- threshold warp (k > 32 only)
+    if constexpr (KB == 0) {
+      const volatile int* done = &s_done;
+      if (P.nslots <= 8 * 32) threshold_sweeps<8>(P, done);
+      else if (P.nslots <= 16 * 32) threshold_sweeps<16>(P, done);
+      else threshold_sweeps<32>(P, done);
+    }
   } else {
     // ---------------------------------------------------------- epilogue (one query per thread)
     const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
@@ -497,7 +541,6 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
       }
       } else {
       const float band = qv ? __ldg(P.qband + q) : 0.f;
-      const uint32_t* sl = P.slots + (size_t)q * P.k;
       uint32_t g_key = qv ? ld_volatile_u32(P.theta + q) : 0u;
       uint32_t g_pending = g_key;
       float theta = g_key ? key2f(g_key) : -INFINITY;
@@ -514,7 +557,6 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
         }
         // two halves of 128 columns: all four loads of a half issued before one
         // wait; the common case is one max per score and one compare per half
-        bool raised = false;
 #pragma unroll 1
         for (int half = 0; half < 2; ++half) {
           uint32_t sa[32], sb[32], sc[32], sd[32];
@@ -541,21 +583,15 @@ __global__ void __launch_bounds__(BATCH_THREADS, 1)
             for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
           if (mx[0] >= theta - band) {
             const int rb = row0 + half * 128;
-            raised |= epi_pass(sa, sb, rb, r1 - rb, band, theta, q, stash, P);
-            raised |= epi_pass(sc, sd, rb + 64, r1 - rb - 64, band, theta, q, stash, P);
-          }
-        }
-        if (raised) {
-          // this thread raised a slot: recompute the slot minimum and publish it
-          const uint32_t mn = slot_min(sl, P.k);
-          if (mn != 0u && mn != 0xffffffffu) {
-            theta = fmaxf(theta, key2f(mn));
-            if (mn > g_pending) atomicMax(P.theta + q, mn);
+            epi_pass(sa, sb, rb, r1 - rb, band, theta, q, stash, P);
+            epi_pass(sc, sd, rb + 64, r1 - rb - 64, band, theta, q, stash, P);
           }
         }
       }
       }
     }
+    // the threshold warp stops with this CTA's epilogue (error path included)
+    if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(&s_done) = 1;
   }
   // Normally every MMA has completed here (each epilogue waited for its last
   // accumulator).  On the error path a wait gave up: the even CTA waits
@@ -780,7 +816,7 @@ static cudaError_t launch_batch_scan(const void* qmap, const void* xmap, const B
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(BATCH_THREADS);
+  cfg.blockDim = dim3(KB == 0 ? BATCH_THREADS_SLOTS : BATCH_THREADS);
   cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = st;
   cfg.attrs = attr;
@@ -828,7 +864,8 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   if ((e = cudaMemsetAsync(bw.overflow, 0, sizeof(int), st)) != cudaSuccess) return e;
   // a wait that gave up in an earlier batch must not send this one down the error path
   if ((e = cudaMemsetAsync(bw.err, 0, sizeof(int), st)) != cudaSuccess) return e;
-  if ((e = cudaMemsetAsync(bw.slots, 0, sizeof(uint32_t) * (size_t)B * k, st)) != cudaSuccess) return e;
+  const int nslots = batch_slot_count(k);
+  if ((e = cudaMemsetAsync(bw.slots, 0, sizeof(uint32_t) * (size_t)B * nslots, st)) != cudaSuccess) return e;
   if ((e = cudaMemsetAsync(bw.unit_counter, 0, 2 * sizeof(int), st)) != cudaSuccess) return e;
   BatchScanParams P{};
   P.Q = Q;
@@ -852,6 +889,7 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   P.theta = bw.theta;
   P.slots = bw.slots;
+  P.nslots = nslots;
   P.cand_count = bw.cand_count;
   P.cand = bw.cand;
   // candidate entries per query: the workspace's fixed pool shared by the batch
@@ -880,9 +918,12 @@ cudaError_t launch_batch_search(const IndexView& ix, const BatchWorkspace& bw, c
     // which removes most cold-start candidates and rare-path epilogue work
     BatchScanParams S = P;
     S.N = bw.sample_rows;
-    S.units = P.QP;
     S.seed_only = 1;
-    S.slice_rows = SEED_ROWS;  // one unit per query tile
+    // k <= 32: one unit per query tile (a unit's own k best set the threshold);
+    // k > 32: the slots are keyed by row, so the sample is cut into slices of
+    // 2,048 rows and spread over 16x as many CTA pairs
+    S.slice_rows = k > 32 ? SEED_ROWS / 16 : SEED_ROWS;
+    S.units = P.QP * ((S.N + S.slice_rows - 1) / S.slice_rows);
     S.row_step = sample_step(ix.N);
     S.unit_counter = bw.unit_counter + 1;
     if ((e = scan(bw.smap, S)) != cudaSuccess) return e;

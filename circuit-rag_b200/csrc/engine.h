@@ -220,10 +220,14 @@ constexpr int BATCH_MAX_DIM = 2048;  // the rescoring keeps the query in registe
 constexpr int BATCH_MAX_K = KMAX;  // any k of the single-query search
 constexpr int BATCH_CAND_CAP = 16384;  // candidate entries per query of a full-capacity batch
 constexpr int BATCH_CAND_MAX = 65536;  // per query when the batch is smaller than the workspace
+// threshold slots per query: 4k for k > 32 (rows r -> slot r mod 4k, threshold
+// = k-th largest slot), rounded up to whole warps of 32; k for k <= 32
+constexpr int batch_slot_count(int k) { return k > 32 ? ((4 * k + 31) / 32) * 32 : k; }
+constexpr int BATCH_MAX_SLOTS = batch_slot_count(BATCH_MAX_K);
 
 struct BatchWorkspace {
   uint32_t* theta = nullptr;      // [capacity] running k-th best keys
-  uint32_t* slots = nullptr;      // [capacity * BATCH_MAX_K] per-query threshold slots
+  uint32_t* slots = nullptr;      // [capacity * BATCH_MAX_SLOTS] per-query threshold slots
   int* unit_counter = nullptr;    // [2] work-unit counters (main pass, threshold pass)
   int* cand_count = nullptr;      // [capacity]
   unsigned long long* cand = nullptr;  // [cand_entries] tf32 key << 32 | row

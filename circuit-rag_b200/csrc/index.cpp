@@ -884,7 +884,7 @@ int circuit_index_opaque::ensure_batch(int B) {
       return p;
     };
     bw.theta = (uint32_t*)grab(sizeof(uint32_t) * cap_B, "cudaMalloc(theta)");
-    bw.slots = (uint32_t*)grab(sizeof(uint32_t) * (size_t)cap_B * cb::BATCH_MAX_K, "cudaMalloc(slots)");
+    bw.slots = (uint32_t*)grab(sizeof(uint32_t) * (size_t)cap_B * cb::BATCH_MAX_SLOTS, "cudaMalloc(slots)");
     bw.cand_count = (int*)grab(sizeof(int) * cap_B, "cudaMalloc(cand_count)");
     // the candidate pool holds at least 4,096 queries x 16,384 entries, so a
     // smaller batch gets up to BATCH_CAND_MAX entries per query

@@ -200,3 +200,19 @@ def test_batch_threshold_pass_and_slots(k):
     Q = w.query_batch(300, device=DEV)
     scores, ids = circuit_search_batch(Q, index, k)
     _check_batch(X, Q[:60], index, k, scores[:60], ids[:60])
+
+
+@pytest.mark.parametrize("k", [33, 100, 256])
+def test_batch_slot_thresholds_full_batch(k):
+    """1,024 queries at k > 32 on 300K rows: every CTA's threshold warp refreshes
+    several queries per sweep (the k-th largest of 4k row-keyed slots), the
+    threshold pass is cut into 2,048-row slices; the first, middle and last
+    queries of the batch equal the single-query search's results and pass the
+    oracle's rule."""
+    w = WORKLOADS["zipf-10m"]
+    X = w.corpus(0, 300_000, device=DEV)
+    index = build_circuit_index(X, num_roots=32, children_per_root=8, rank=16, device=DEV)
+    Q = w.query_batch(1024, device=DEV)
+    scores, ids = circuit_search_batch(Q, index, k)
+    pick = torch.tensor(list(range(0, 16)) + list(range(500, 516)) + list(range(1008, 1024)), device=DEV)
+    _check_batch(X, Q[pick], index, k, scores[pick], ids[pick])
