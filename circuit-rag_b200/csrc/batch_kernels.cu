@@ -190,7 +190,8 @@ __device__ void threshold_sweeps(const BatchScanParams& P, const volatile int* d
   const int q0 = (int)blockIdx.x, dq = (int)gridDim.x;
   if (q0 >= P.B) return;
   uint32_t v[PL], nv[PL];
-  for (int sweep = 0; sweep < THRESHOLD_MAX_SWEEPS && !*done; ++sweep) {
+  // the stop decision is made warp-wide: every lane must reach each redux.sync
+  for (int sweep = 0; sweep < THRESHOLD_MAX_SWEEPS && !__any_sync(FULL_MASK, *done != 0); ++sweep) {
     load_slots<PL>(P.slots + (size_t)q0 * P.nslots, per, lane, nv);
     for (int q = q0; q < P.B; q += dq) {
 #pragma unroll
@@ -213,7 +214,7 @@ __device__ void threshold_sweeps(const BatchScanParams& P, const volatile int* d
         if (__reduce_add_sync(FULL_MASK, (unsigned)n) >= (unsigned)P.k) x = t;
       }
       if (lane == 0 && x > cur) atomicMax(P.theta + q, x);
-      if (*done) break;
+      if (__any_sync(FULL_MASK, *done != 0)) break;
     }
     __nanosleep(500);
   }
