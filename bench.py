@@ -33,8 +33,9 @@ from the driver's measured bf16 GEMM rate.
 
 `workloads` (N = 1, default workload): the other configurations measured after
 the headline index is released: spread-200k single-query latency, the
-clustered-50k pruning regime with its per-kernel split, zipf-10m batches at
-k = 100, and the 5,183-row flat path host-to-host.
+clustered-50k pruning regime with its per-kernel split, the reference's own
+exactness-test corpus (reftest-40k), clustered-4m, zipf-10m batches at k = 100,
+and the 5,183-row flat path host-to-host.
 
 `cpu_baseline`: the reference's CPU search path (brute force topk(X @ q),
 circuit_rag/search.py:58-61; the oracle port) on a 12.5M-row sample of the same
@@ -720,8 +721,8 @@ def other_workloads(dev, hbm_peak):
     from circuit_rag.synthetic import WORKLOADS
 
     out = {}
-    for name, n_q, flat in (("spread-200k", 300, False), ("clustered-50k", 300, False), ("clustered-4m", 100, False),
-                            ("spread-5k", 300, True)):
+    for name, n_q, flat in (("spread-200k", 300, False), ("clustered-50k", 300, False), ("reftest-40k", 300, False),
+                            ("clustered-4m", 100, False), ("spread-5k", 300, True)):
         w = WORKLOADS[name]
         X = w.corpus(0, w.n, device=dev)
         idx = build_circuit_index(X, num_roots=w.num_roots, children_per_root=w.children_per_root, rank=w.rank,

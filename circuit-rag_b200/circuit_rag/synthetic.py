@@ -14,10 +14,16 @@ Workloads (N x D, float32, unit norm):
               rescaled to norm 0.6, plus a shared mean direction of norm 0.6,
               renormalised (mean pairwise cosine about 0.5).
   mixed     : half clustered (Zipf), half spread, interleaved by row parity.
+  reftest   : the reference's exactness-test corpus (tests/test_exact.py:9-14):
+              n_centers Gaussian (non-unit) centres, random labels, sigma = 0.3
+              per dimension, renormalised; numpy generators seeded 0 (corpus)
+              and 1 (query row indices, tests/test_exact.py:19); queries are
+              corpus rows, as in that test.
 """
 from dataclasses import dataclass
 from typing import Optional
 
+import numpy as np
 import torch
 
 CHUNK = 1 << 16  # rows per generator chunk; a chunk is always drawn whole
@@ -85,6 +91,14 @@ def spread(start: int, stop: int, dim: int, seed: int, device="cpu") -> torch.Te
     return out
 
 
+def reftest(n: int, dim: int, n_centers: int, sigma: float, seed: int) -> torch.Tensor:
+    """The whole reftest corpus (float32, unit rows, on the CPU)."""
+    rng = np.random.default_rng(seed)
+    centers = rng.normal(size=(n_centers, dim))
+    x = centers[rng.integers(0, n_centers, n)] + sigma * rng.normal(size=(n, dim))
+    return torch.from_numpy((x / np.linalg.norm(x, axis=1, keepdims=True)).astype(np.float32))
+
+
 @dataclass(frozen=True)
 class Workload:
     name: str
@@ -108,9 +122,14 @@ class Workload:
     def query_batch(self, n: Optional[int] = None, device="cpu") -> torch.Tensor:
         """Queries drawn from the same law as the corpus (independent rows)."""
         n = self.queries if n is None else n
+        if self.kind == "reftest":
+            rows = np.random.default_rng(self.seed + 1).integers(0, self.n, n)
+            return self.corpus(device="cpu")[torch.from_numpy(rows)].to(device)
         return self._rows(0, n, self.seed + 1, device)
 
     def _rows(self, start, stop, seed, device):
+        if self.kind == "reftest":
+            return reftest(self.n, self.dim, self.n_centers, self.sigma, seed)[start:stop].to(device)
         if self.kind == "spread":
             return spread(start, stop, self.dim, seed, device)
         centers = sphere(self.n_centers, self.dim, self.seed + 101, device)
@@ -125,6 +144,8 @@ class Workload:
 
 WORKLOADS = {
     "clustered-50k": Workload("clustered-50k", 50_000, 128, 64, 16, 8, 10, 25, "clustered", 64, 0.05),
+    # the reference's own exactness test (tests/test_exact.py:9-19): 40K x 128, R = 32 x 8, rank 8
+    "reftest-40k": Workload("reftest-40k", 40_000, 128, 32, 8, 8, 10, 25, "reftest", 64, 0.3),
     # the clustered-50k law at 4M rows (2 GB): too large to stream whole while the bounds are computed
     "clustered-4m": Workload("clustered-4m", 4_000_000, 128, 64, 16, 8, 10, 25, "clustered", 64, 0.05),
     "spread-5k": Workload("spread-5k", 5_183, 384, 64, 16, 8, 10, 300, "spread"),

@@ -120,3 +120,19 @@ def test_check_topk_rejects_wrong_answers():
         oracle.check_topk(exact, 10, s + 1e-3, rows)
     with pytest.raises(AssertionError):
         oracle.check_topk(exact, 10, s[::-1], rows[::-1])
+
+
+def test_reftest_workload_is_the_reference_test_data():
+    """The bench's reftest-40k workload generates the reference test's corpus
+    and its query rows (tests/test_exact.py:9-19), pinned to the fixture."""
+    import torch
+    from circuit_rag.synthetic import WORKLOADS
+
+    g = np.load(_g("ref_test_exact.npz"))
+    w = WORKLOADS["reftest-40k"]
+    X = w.corpus().numpy()
+    assert np.isclose(X.astype(np.float64).sum(), float(g["x_sum"]), rtol=0, atol=1e-6)
+    assert np.array_equal(X[0], g["x_row0"]) and np.array_equal(X[-1], g["x_row_last"])
+    Q = w.query_batch(25).numpy()
+    assert np.array_equal(Q, X[g["qids"]])
+    assert torch.equal(w.corpus(1000, 1100), torch.from_numpy(X[1000:1100]))
