@@ -100,6 +100,9 @@ def parse():
     ap.add_argument("--shared-threshold", action="store_true",
                     help="N > 1: also share the running threshold between the shards while their scans run "
                          "(circuit_search_finish_shared_async over CUDA IPC)")
+    ap.add_argument("--no-seed-allreduce", action="store_true",
+                    help="with --shared-threshold: skip the seed all-reduce, so each shard's bounds and scan "
+                         "follow its own seed on the GPU and thresholds cross only through the shared words")
     return ap.parse_args()
 
 
@@ -374,11 +377,11 @@ class Searcher:
         from circuit_rag import _native
 
         self.min_hier = min_hier
-        if exchange == "shared" and Searcher._shared is None:
+        if exchange in ("shared", "running") and Searcher._shared is None:
             from circuit_rag.shard import SharedThreshold
 
             Searcher._shared = SharedThreshold(torch.device(dev), None)
-        self.shared = Searcher._shared if exchange == "shared" else None
+        self.shared = Searcher._shared if exchange in ("shared", "running") else None
         self.L = _native.lib()
         self.h = idx.native_handle()
         self.k, self.world, self.exchange = k, world, exchange
@@ -399,7 +402,8 @@ class Searcher:
 
         assert self.L.circuit_search_seed_async(self.h, q.data_ptr(), self.k, self.T.data_ptr(),
                                                 self.stream.cuda_stream) == 0
-        dist.all_reduce(self.T, op=dist.ReduceOp.MAX)
+        if self.exchange != "running":
+            dist.all_reduce(self.T, op=dist.ReduceOp.MAX)
         if self.shared is not None:
             sh = self.shared
             sh.tag = ((sh.tag + 1) & 0xFFFFFFFF) or 1
@@ -823,7 +827,7 @@ def main():
     n_local = idx.N
     exchange = world > 1 and not args.no_threshold_exchange
     if exchange and args.shared_threshold:
-        exchange = "shared"
+        exchange = "running" if args.no_seed_allreduce else "shared"
 
     steps, warm = args.steps, args.warmup
     Q = w.query_batch(steps + warm, device=dev)
@@ -869,7 +873,8 @@ def main():
         dist.all_reduce(tmin, op=dist.ReduceOp.MIN)
         phases = {"local_search_ms_max_min": [round(float(tmax[0]), 4), round(float(tmin[0]), 4)],
                   "all_gather_ms_max": round(float(tmax[1]), 4), "merge_ms_max": round(float(tmax[2]), 4),
-                  "how": "median of 20 untimed queries per rank; local search includes the seed all-reduce"}
+                  "how": "median of 20 untimed queries per rank; local search includes the seed all-reduce "
+                         "(when one runs)"}
 
     # e2e through the public API
     e2e_steps = args.e2e_steps or min(steps, 50)
@@ -894,8 +899,12 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e = {"value": e2e_steps / float(t.item()), "unit": "queries/s", "h2d_bytes_per_step": D * 4,
                "d2h_bytes_per_step": k * 8,
-               "api": ("circuit_search_seed_async + NCCL all-reduce(MAX) + circuit_search_finish_async"
-                       if exchange else "circuit_search_async") + " + NCCL all-gather + circuit_merge_topk"}
+               "api": {False: "circuit_search_async",
+                       True: "circuit_search_seed_async + NCCL all-reduce(MAX) + circuit_search_finish_async",
+                       "shared": "circuit_search_seed_async + NCCL all-reduce(MAX) + "
+                                 "circuit_search_finish_shared_async",
+                       "running": "circuit_search_seed_async + circuit_search_finish_shared_async"}[exchange]
+               + " + NCCL all-gather + circuit_merge_topk"}
 
     bat = None
     if args.batch > 0:

@@ -295,14 +295,23 @@ class ShardedSearcher:
 
     def search(self, query: torch.Tensor, k: int = 10, min_hierarchy_n: int = 10000,
                exchange_threshold: bool = False, local_seed: Optional[Callable] = None,
-               local_finish: Optional[Callable] = None):
+               local_finish: Optional[Callable] = None, seed_allreduce: bool = True):
         """Global exact top-k of one query.  With exchange_threshold, every rank
         first computes its shard's seed threshold, one all-reduce (MAX) makes
         the largest of them every rank's pruning threshold (it never exceeds
-        the global k-th best score), then each rank finishes its search."""
+        the global k-th best score), then each rank finishes its search.
+        seed_allreduce=False (needs enable_shared_threshold) skips that
+        all-reduce: each rank starts from its own seed and the ranks exchange
+        thresholds only through the shared running threshold while their scans
+        run, so the bounds and the scan follow the seed on the GPU without
+        waiting for the other ranks."""
         if exchange_threshold:
+            if not seed_allreduce and self._shared is None and local_finish is None:
+                raise ValueError("seed_allreduce=False exchanges thresholds only through the shared running "
+                                 "threshold: call enable_shared_threshold() first")
             T = (local_seed or self._native_seed)(query, k)
-            self.dist.all_reduce(T, op=self.dist.ReduceOp.MAX, group=self.group)
+            if seed_allreduce:
+                self.dist.all_reduce(T, op=self.dist.ReduceOp.MAX, group=self.group)
             s, i = (local_finish or self._native_finish)(query, k, T)
         else:
             s, i = self._local(query, k, min_hierarchy_n)

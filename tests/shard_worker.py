@@ -72,8 +72,20 @@ def search_worker(rank, world, port, root, index_path, queries_path, out_path, k
         for q in Q:
             s, i = srch.search(torch.from_numpy(q), k=k, exchange_threshold=True, local_seed=seed, local_finish=finish)
             ex.append({"scores": s.tolist(), "ids": i.tolist()})
+        # no seed all-reduce: each shard finishes from its own seed
+        own = []
+        for q in Q:
+            s, i = srch.search(torch.from_numpy(q), k=k, exchange_threshold=True, local_seed=seed, local_finish=finish,
+                               seed_allreduce=False)
+            own.append({"scores": s.tolist(), "ids": i.tolist()})
+        try:
+            srch.search(torch.from_numpy(Q[0]), k=k, exchange_threshold=True, local_seed=seed, seed_allreduce=False)
+            needs_shared = False
+        except ValueError:
+            needs_shared = True
         result.update(ok=True, results=res, shard_rows=int(len(X)), shard_ids=gid.tolist(),
-                      batch_results={"scores": bs.tolist(), "ids": bi.tolist()}, exchange_results=ex)
+                      batch_results={"scores": bs.tolist(), "ids": bi.tolist()}, exchange_results=ex,
+                      own_seed_results=own, own_seed_needs_shared=needs_shared)
     except SystemExit:
         raise
     except Exception as e:  # the survivor of a lost rank lands here

@@ -37,7 +37,11 @@ def _trace(L, h):
     return tx
 
 
-def test_three_shards_share_the_running_threshold(tmp_path):
+@pytest.mark.parametrize("seed", ["max", "own"])
+def test_three_shards_share_the_running_threshold(tmp_path, seed):
+    """seed = "max": every shard starts from the largest seed (the all-reduce);
+    "own": no seed exchange, each shard starts from its own seed and learns
+    the others' thresholds only through the shared words."""
     import dataclasses
 
     w = dataclasses.replace(WORKLOADS["clustered-50k"], name="clustered-600k", n=600_000)
@@ -71,8 +75,9 @@ def test_three_shards_share_the_running_threshold(tmp_path):
                 s = torch.empty(k, device=DEV)
                 i = torch.empty(k, dtype=torch.int32, device=DEV)
                 if shared:
+                    T_in = Tmax if seed == "max" else Ts[r]
                     assert L.circuit_search_finish_shared_async(
-                        sh.native_handle(), q.data_ptr(), k, Tmax.data_ptr(), words[r:r + 1].data_ptr(),
+                        sh.native_handle(), q.data_ptr(), k, T_in.data_ptr(), words[r:r + 1].data_ptr(),
                         peers[r].data_ptr(), world - 1, tag, s.data_ptr(), i.data_ptr(), None, st, None, None) == 0
                 else:
                     assert L.circuit_search_finish_async(sh.native_handle(), q.data_ptr(), k, Tmax.data_ptr(),

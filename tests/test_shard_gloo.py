@@ -110,6 +110,9 @@ def test_sharded_search_is_exact(index_file, tmp_path, world):
             assert r["batch_results"]["ids"][qi] == r["results"][qi]["ids"]
             # all-reduce(MAX) of the shards' seed thresholds, then the finish phase
             assert r["exchange_results"][qi]["ids"] == r["results"][qi]["ids"]
+            # no seed all-reduce (each shard from its own seed): the same answers
+            assert r["own_seed_results"][qi]["ids"] == r["results"][qi]["ids"]
+            assert r["own_seed_needs_shared"]  # the native finish needs the shared running threshold
             oracle.check_topk(exact, 10, r["batch_results"]["scores"][qi], r["batch_results"]["ids"][qi])
 
 
