@@ -41,7 +41,8 @@ def _trace(L, h):
 def test_three_shards_share_the_running_threshold(tmp_path, seed):
     """seed = "max": every shard starts from the largest seed (the all-reduce);
     "own": no seed exchange, each shard starts from its own seed and learns
-    the others' thresholds only through the shared words."""
+    the others' thresholds only through the shared words (exact either way;
+    only "max" is held to reading no more rows than the unshared search)."""
     import dataclasses
 
     w = dataclasses.replace(WORKLOADS["clustered-50k"], name="clustered-600k", n=600_000)
@@ -95,7 +96,12 @@ def test_three_shards_share_the_running_threshold(tmp_path, seed):
         for wv in words.cpu().numpy().astype(np.uint64):
             assert int(wv) >> 32 == tag
             assert int(wv) & 0xFFFFFFFF <= _f2key(kth + 1e-6)
-    assert rows_shared <= rows_plain, (rows_shared, rows_plain)
+    if seed == "max":
+        assert rows_shared <= rows_plain, (rows_shared, rows_plain)
+    else:
+        # the shards run one after another here, so the first learns nothing from
+        # the others and every shard starts below the largest seed: more rows
+        print(f"\n[own seeds] rows streamed {rows_shared} (with the largest seed and no words: {rows_plain})")
     for sh in shards:
         sh.close()
 
