@@ -172,3 +172,55 @@ def test_file_shards_cut_oversized_roots(tmp_path):
     assert sorted(ids) == list(range(len(X)))
     sizes = idx.leaf_sizes.numpy()
     assert max(loads) <= 1.05 * len(X) / world + sizes.max()
+
+
+def _random_roots(rng, num_roots, max_atoms, max_rows, zero_frac):
+    atoms, ptr = [], [0]
+    for _ in range(num_roots):
+        n = int(rng.integers(0, max_atoms + 1))
+        sizes = rng.integers(0, max_rows + 1, size=n)
+        sizes[rng.random(n) < zero_frac] = 0
+        atoms.extend(int(x) for x in sizes)
+        ptr.append(len(atoms))
+    return np.array(atoms, np.int64), np.array(ptr, np.int64)
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_plan_invariants_on_random_roots(seed):
+    """Any roots (empty roots, zero-row atoms, one root holding most rows, more
+    ranks than roots): every non-empty atom is planned once, each part is a
+    contiguous atom range of one root, the rank loads add up, no rank exceeds
+    max_imbalance x the mean by more than one atom, and the plan is the same
+    every time (every rank computes it on its own)."""
+    rng = np.random.default_rng(seed)
+    num_roots = int(rng.integers(1, 40))
+    atoms, ptr = _random_roots(rng, num_roots, max_atoms=int(rng.integers(1, 12)),
+                               max_rows=int(rng.choice([1, 10, 1000])), zero_frac=float(rng.choice([0.0, 0.3])))
+    if seed % 5 == 0 and len(atoms):
+        atoms[int(rng.integers(0, len(atoms)))] += int(atoms.sum()) * 3  # one dominant atom's root
+    world = int(rng.integers(1, 10))
+    imb = float(rng.choice([1.0, 1.05, 1.5]))
+    plan = plan_shard_parts(atoms, ptr, world, imb)
+    loads = _check_plan(plan, atoms, ptr, world)
+    if atoms.sum() > 0:
+        assert loads.max() <= imb * atoms.sum() / world + atoms.max(), (loads, imb, atoms.max())
+    again = plan_shard_parts(atoms, ptr, world, imb)
+    for key in plan:
+        assert np.array_equal(plan[key], again[key]), key
+    # parts are ordered by rank, root, first atom
+    order = list(zip(plan["part_rank"], plan["part_root"], plan["part_atom_begin"]))
+    assert order == sorted(order)
+
+
+def test_plan_rejects_bad_arguments():
+    from circuit_rag import _native
+
+    atoms = np.array([3, 4, 5], np.int64)
+    with pytest.raises(_native.NativeLibraryError):
+        plan_shard_parts(atoms, np.array([0, 2, 3], np.int64), 0, 1.05)  # no ranks
+    with pytest.raises(_native.NativeLibraryError):
+        plan_shard_parts(atoms, np.array([0, 2, 3], np.int64), 2, 0.9)  # imbalance below 1
+    with pytest.raises(_native.NativeLibraryError):
+        plan_shard_parts(atoms, np.array([0, 2, 1], np.int64), 2, 1.05)  # decreasing pointers
+    with pytest.raises(_native.NativeLibraryError):
+        plan_shard_parts(np.array([3, -4, 5], np.int64), np.array([0, 2, 3], np.int64), 2, 1.05)  # negative rows
