@@ -57,6 +57,18 @@ def test_search_requires_cuda_and_validates_shape():
         circuit_search(torch.zeros(7), idx)
     with pytest.raises(RuntimeError, match="CUDA"):
         circuit_search(torch.zeros(8), idx)
+    # the batched search and the per-stage ops refuse CPU tensors too (no CPU path)
+    from circuit_rag import circuit_search_batch
+    import circuit_cuda
+
+    with pytest.raises(ValueError):
+        circuit_search_batch(torch.zeros(3, 7), idx, 2)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        circuit_search_batch(torch.zeros(3, 8), idx, 2)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        circuit_cuda.flat_exact_score(torch.zeros(8), torch.zeros(300, 8))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        circuit_cuda.evaluate_root_bounds(torch.zeros(8), torch.zeros(4, 8), torch.zeros(4), 0.0)
 
 
 def test_append_keeps_certificates_and_layout():
