@@ -13,6 +13,11 @@
  *
  * Output buffers are fully written by each op (masks, counts, zero / -1e9
  * fills), so callers may pass uninitialised memory.
+ * Like the reference ops, these take the index tables as given: the sizes and
+ * pointers are checked on the host, but survivor lists, parent ids and leaf
+ * offsets / sizes are used as indices on the device without a range check, so
+ * they must describe a valid index (one that circuit_load_index or
+ * circuit_index_from_device accepts: those validate every table once).
  * Return value: 0 on success, a negative CIRCUIT_ERR_* code otherwise
  * (description in circuit_last_error()).
  */
