@@ -346,7 +346,10 @@ def gather_exact(ex_s, ex_i, world):
 def count_mismatches(got_s, got_i, ex_s, ex_i, k):
     """Queries that break the parity rule: every id whose exact score is above
     the k-th by more than 1e-6 returned, no id below the k-th by more than
-    1e-6, scores within 1e-5 relative (+1e-6) of exact, sorted, no duplicates."""
+    1e-6, scores within 1e-5 relative (+1e-6) of exact, sorted, no duplicates.
+    ex_s / ex_i are the exact top-(k + extra) lists; a returned id outside them
+    scores at most their last entry, so it passes only where that last entry is
+    still tied with the k-th (the list was cut inside a tie)."""
     got_s, got_i = got_s.cpu().numpy().astype(np.float64), got_i.cpu().numpy().astype(np.int64)
     ex_s, ex_i = ex_s.cpu().numpy(), ex_i.cpu().numpy()
     bad = 0
@@ -359,7 +362,7 @@ def count_mismatches(got_s, got_i, ex_s, ex_i, k):
         for sc, idv in zip(s, i):
             e = exact_of.get(int(idv))
             if e is None:
-                ok = ok and sc >= kth - TIE_ABS - SCORE_REL * abs(kth)
+                ok = ok and es[-1] >= kth - TIE_ABS and sc >= kth - TIE_ABS - SCORE_REL * abs(kth)
             else:
                 ok = ok and e >= kth - TIE_ABS and abs(sc - e) <= SCORE_REL * abs(e) + TIE_ABS
         bad += 0 if ok else 1
