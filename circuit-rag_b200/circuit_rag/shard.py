@@ -25,7 +25,7 @@ import torch
 
 from circuit_rag import _native
 from circuit_rag.hierarchy.build import CircuitIndex
-from circuit_rag.storage.format import TENSOR_ORDER, read_header
+from circuit_rag.storage.format import TENSOR_ORDER, check_child_tables, read_header
 
 
 def plan_shards(root_rows: Sequence[int], world: int) -> np.ndarray:
@@ -98,6 +98,7 @@ def load_shard(filepath: str, rank: int, world: int, device: str = "cuda",
                               shape=tuple(info["shape"]))
 
         parent, offsets, sizes = (arr(n).copy() for n in ("child_parent_ids", "leaf_offsets", "leaf_sizes"))
+        check_child_tables(parent, offsets, sizes, R, int(meta["N"]))
         ptr, kids_all = _root_children(parent, offsets, sizes, R)
         plan = plan_shard_parts(sizes[kids_all].astype(np.int64), ptr, world, max_imbalance)
         own = np.nonzero(plan["part_rank"] == rank)[0]

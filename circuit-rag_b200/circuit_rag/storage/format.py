@@ -150,6 +150,31 @@ def read_header(filepath: str) -> Dict[str, Any]:
     return meta
 
 
+def check_child_tables(parent, offsets, sizes, num_roots: int, n: int) -> None:
+    """The child-table checks the native loader makes before it uses the tables
+    as indices (csrc/index.cpp, build_host_tables): no negative size; every
+    non-empty child has a parent in [0, num_roots) and a row range inside
+    [0, n); the ranges are disjoint and cover all n rows.  Empty children may
+    carry any parent id and offset (the reference builder leaves them 0)."""
+    parent = np.asarray(parent, dtype=np.int64)
+    offsets = np.asarray(offsets, dtype=np.int64)
+    sizes = np.asarray(sizes, dtype=np.int64)
+    if (sizes < 0).any():
+        raise CircuitFormatError("leaf_sizes has a negative entry")
+    live = sizes > 0
+    p, o, z = parent[live], offsets[live], sizes[live]
+    if ((p < 0) | (p >= num_roots)).any():
+        raise CircuitFormatError("child_parent_ids out of range for a non-empty child")
+    if ((o < 0) | (o + z > n)).any():
+        raise CircuitFormatError("leaf_offsets/leaf_sizes reach outside leaf_vectors")
+    order = np.argsort(o, kind="stable")
+    o, z = o[order], z[order]
+    if len(o) > 1 and (o[:-1] + z[:-1] > o[1:]).any():
+        raise CircuitFormatError("child leaf ranges overlap")
+    if int(z.sum()) != int(n):
+        raise CircuitFormatError(f"children do not cover all N leaf rows ({int(z.sum())} of {int(n)})")
+
+
 def load_circuit_index(filepath: str, device: str = "cuda", use_mmap: bool = True):
     """Load a .circuit file (reference format.py:82-142).  With ``use_mmap`` the
     tensors are zero-copy views of a private (copy-on-write) mapping until they
@@ -173,6 +198,8 @@ def load_circuit_index(filepath: str, device: str = "cuda", use_mmap: bool = Tru
                 data = f.read(int(info["nbytes"]))
                 arr = np.frombuffer(data, dtype=np.dtype(dt)).reshape(tuple(info["shape"]))
                 tensors[name] = torch.from_numpy(arr.copy())
+    check_child_tables(tensors["child_parent_ids"].numpy(), tensors["leaf_offsets"].numpy(),
+                       tensors["leaf_sizes"].numpy(), int(meta["num_roots"]), int(meta["N"]))
     return CircuitIndex(
         root_centers=tensors["root_centers"],
         root_radii=tensors["root_radii"],

@@ -47,8 +47,9 @@ class Parser {
     skip();
     if (!value(out, 0)) return false;
     skip();
-    // trailing zero padding (the header block is zero padded) is allowed
-    while (p_ < end_ && (*p_ == '\0' || is_ws(*p_))) ++p_;
+    // then only the header block's zero padding (as json.loads of the text
+    // with its trailing NULs stripped: whitespace after a NUL is not allowed)
+    while (p_ < end_ && *p_ == '\0') ++p_;
     return p_ == end_;
   }
 
